@@ -1,0 +1,418 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 SpectralConv2d / FNO-NS forward.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+One process per GPU (torchrun for N > 1, NCCL).  The headline workload is the
+SpectralConv2d forward at B=20 per GPU, Cin=Cout=32, 128x128, modes 16 on a Gaussian
+random field; the batch is sharded across GPUs (weak scaling: 20 items per GPU, no
+collective on the data path).  ``value`` = samples processed by all ranks / max-over-ranks
+device time of exactly K steps (CUDA events, after W warm-up steps).  Between timed steps
+the inputs rotate over enough buffer sets that every step reads data larger than L2.
+
+Rank 0 prints ONE JSON line.  Besides the contract keys it carries
+* ``roofline``: the dominant kernel's algorithmic bytes per launch / its CUDA-event
+  duration against the measured HBM copy bandwidth, and ``roofline_fused_path`` for the
+  whole forward (x read + y written + both weight tensors read);
+* ``e2e``: the same metric through the public host API (``spectral_conv2d_supa`` with a
+  pinned host input and a host result), H2D and D2H inside the timed region;
+* ``cpu_baseline``: the reference's CPU recipe (torch.fft + einsum, all host threads) on
+  the same workload (rank 0, N=1);
+* ``workloads``: the 64x64 and 256x256 SpectralConv2d forwards measured the same way.
+
+``--impl reference`` times the reference's CPU implementation of the path (its torch.fft
++ einsum recipe restated in ``oracle/``) on this host's cores, same workload and metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "birensupa-spectralconv_b200"
+sys.path.insert(0, str(PKG))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+HEADLINE = "spectral_b20_c32_128x128_m16_grf"
+EXTRA_WORKLOADS = ["spectral_b20_c32_64x64_m12", "spectral_b16_c64_256x256_m32"]
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default=HEADLINE)
+    ap.add_argument("--no-extras", action="store_true", help="skip the 64x64 / 256x256 entries")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------- helpers
+
+def hbm_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        v = float(json.loads(p.read_text())["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def spectral_bytes(c: dict) -> dict:
+    """Algorithmic HBM bytes: every operand read once, every result written once."""
+    B, Cin, Cout, H, W, m1, m2 = (c[k] for k in ("B", "Cin", "Cout", "H", "W", "m1", "m2"))
+    nm = m1 * m2
+    return {
+        "dft_fwd": 4 * B * Cin * H * W + 16 * B * Cin * nm,
+        "mix": 16 * B * Cin * nm + 16 * Cin * Cout * nm + 16 * B * Cout * nm,
+        "dft_inv": 16 * B * Cout * nm + 4 * B * Cout * H * W,
+        "fused_path": 4 * B * H * W * (Cin + Cout) + 16 * Cin * Cout * nm,
+    }
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the GPU is loaded."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            import tempfile
+            fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        if not self.path or not os.path.exists(self.path):
+            return out
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return out
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, flags in rows for i, f in enumerate(flags) if f.lower() == "active"})
+        out.update(sm_mhz=statistics.median(r[0] for r in rows), sm_max_mhz=max(r[1] for r in rows),
+                   reasons=reasons, samples=len(rows))
+        return out
+
+
+# ------------------------------------------------------------------------- our arm
+
+def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: int, *, with_e2e: bool,
+                 with_breakdown: bool, sampler_gpu: int | None):
+    import scx_data
+    import spectral_conv_ext as ext
+    import spectral_conv_ops as ops
+    import scx_dist
+
+    x_cpu, w1c, w2c, c = scx_data.make_spectral_case(name)
+    B, Cin, Cout, H, W, m1, m2 = (c[k] for k in ("B", "Cin", "Cout", "H", "W", "m1", "m2"))
+    w1 = torch.view_as_real(w1c.to(device)).contiguous()
+    w2 = torch.view_as_real(w2c.to(device)).contiguous()
+    per_set = 4 * B * H * W * (Cin + Cout)
+    nsets = max(1, math.ceil(3 * L2_BYTES / per_set))
+    xs = [x_cpu.to(device) for _ in range(nsets)]
+    ys = [torch.empty(B, Cout, H, W, device=device) for _ in range(nsets)]
+    ext.prepare(H, W, m1, m2)
+    ws_bytes = ext._scx.lib.scx_spectral_conv2d_workspace_size(B, Cin, Cout, H, W, m1, m2)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+    lib = ext._scx.lib
+    stream = torch.cuda.current_stream(device)
+    sh = stream.cuda_stream
+
+    def step(i):
+        s = i % nsets
+        rc = lib.scx_spectral_conv2d_fwd(xs[s].data_ptr(), w1.data_ptr(), w2.data_ptr(), ys[s].data_ptr(), B, Cin,
+                                         Cout, H, W, m1, m2, ws.data_ptr(), ws_bytes, sh)
+        if rc != 0:
+            raise RuntimeError(f"scx_spectral_conv2d_fwd failed: {rc}")
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize(device)
+    barrier()
+    torch.cuda.synchronize(device)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    clocks = None
+    sampler = ClockSampler(sampler_gpu) if sampler_gpu is not None else None
+    if sampler:
+        sampler.__enter__()
+    ev0.record(stream)
+    for i in range(steps):
+        step(i)
+    ev1.record(stream)
+    torch.cuda.synchronize(device)
+    t_ms = ev0.elapsed_time(ev1)
+    if sampler:
+        # keep the same load running for >= 1 s so that the 100 ms sampler sees it
+        t_end = time.perf_counter() + 1.2
+        i = 0
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                step(i)
+                i += 1
+            torch.cuda.synchronize(device)
+        sampler.__exit__()
+        clocks = sampler.summary()
+    barrier()
+    t_ms_max = scx_dist.max_over_ranks(t_ms, device)
+    ms_per_step = t_ms_max / steps
+    res = {"cfg": c, "ms_per_step": ms_per_step, "samples_per_s": world * B / (ms_per_step / 1e3),
+           "launches_per_step": 3, "clocks": clocks}
+
+    nbytes = spectral_bytes(c)
+    peak, peak_kind = hbm_peak()
+    res["roofline_fused_path"] = {
+        "bound": "hbm", "achieved": nbytes["fused_path"] / (ms_per_step / 1e3) / 1e9, "peak": peak,
+        "unit": "GB/s", "peak_kind": peak_kind, "bytes": nbytes["fused_path"]}
+    res["roofline_fused_path"]["frac"] = res["roofline_fused_path"]["achieved"] / peak
+
+    if with_breakdown:
+        # per-kernel CUDA-event durations of the three launches of one forward
+        ci = B * Cin * m1 * m2 * 2
+        co = B * Cout * m1 * m2 * 2
+        X1 = ws.view(torch.float32)[:ci]
+        X2 = ws.view(torch.float32)[ci:2 * ci]
+        Y1 = ws.view(torch.float32)[2 * ci:2 * ci + co]
+        Y2 = ws.view(torch.float32)[2 * ci + co:2 * ci + 2 * co]
+        reps = max(10, steps)
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(reps)]
+        for r in range(reps):
+            s = r % nsets
+            e = evs[r]
+            e[0].record(stream)
+            lib.scx_rfft2_corners(xs[s].data_ptr(), X1.data_ptr(), X2.data_ptr(), B, Cin, H, W, m1, m2, sh)
+            e[1].record(stream)
+            lib.scx_spectral_mul_dual(X1.data_ptr(), X2.data_ptr(), w1.data_ptr(), w2.data_ptr(), Y1.data_ptr(),
+                                      Y2.data_ptr(), B, Cin, Cout, m1, m2, sh)
+            e[2].record(stream)
+            lib.scx_irfft2_corners(Y1.data_ptr(), Y2.data_ptr(), ys[s].data_ptr(), B, Cout, H, W, m1, m2, sh)
+            e[3].record(stream)
+        torch.cuda.synchronize(device)
+        kern = {"dft_fwd": 0.0, "mix": 0.0, "dft_inv": 0.0}
+        for e in evs:
+            kern["dft_fwd"] += e[0].elapsed_time(e[1]) / reps
+            kern["mix"] += e[1].elapsed_time(e[2]) / reps
+            kern["dft_inv"] += e[2].elapsed_time(e[3]) / reps
+        total = sum(kern.values())
+        res["kernels"] = {k: {"ms": v, "share": v / total, "bytes": nbytes[k],
+                              "gbs": nbytes[k] / (v / 1e3) / 1e9} for k, v in kern.items()}
+        dom = max(kern, key=kern.get)
+        achieved = nbytes[dom] / (kern[dom] / 1e3) / 1e9
+        res["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                           "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                           "bytes_per_launch": nbytes[dom], "ms_per_launch": kern[dom]}
+        prof = REPO / "profiles" / "ncu_traffic.json"
+        if prof.exists():
+            try:
+                entry = json.loads(prof.read_text()).get(name, {}).get(dom)
+                if entry is not None:
+                    res["roofline"]["traffic"] = entry
+            except Exception:
+                pass
+
+    if with_e2e:
+        # public host API: pinned host input in, host result out, copies inside the region
+        x_host = x_cpu.pin_memory()
+        w1p = w1c.to(device)
+        w2p = w2c.to(device)
+        n_e2e = max(3, min(steps, 20))
+        for _ in range(2):
+            ops.spectral_conv2d_supa(x_host, w1p, w2p, m1, m2, use_sufft="fused", to_cpu=True)
+        torch.cuda.synchronize(device)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(n_e2e):
+            out = ops.spectral_conv2d_supa(x_host, w1p, w2p, m1, m2, use_sufft="fused", to_cpu=True)
+        torch.cuda.synchronize(device)
+        t_e2e = (time.perf_counter() - t0) * 1e3 / n_e2e
+        t_e2e = scx_dist.max_over_ranks(t_e2e, device)
+        assert out.device.type == "cpu"
+        res["e2e"] = {"value": world * B / (t_e2e / 1e3), "unit": "samples/s", "ms_per_step": t_e2e,
+                      "h2d_bytes_per_step": x_host.numel() * 4, "d2h_bytes_per_step": out.numel() * 4,
+                      "api": "spectral_conv_ops.spectral_conv2d_supa(to_cpu=True)"}
+    return res
+
+
+def cpu_baseline(name: str, budget_s: float = 12.0) -> dict:
+    """The reference's CPU recipe on the same workload, all host threads, bounded sample."""
+    import scx_data
+    from oracle import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, w1, w2, c = scx_data.make_spectral_case(name)
+    oracle.spectral_conv2d_torch(x, w1, w2, c["m1"], c["m2"])  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < 3 or (time.perf_counter() - t_start < budget_s and len(times) < 50):
+        t0 = time.perf_counter()
+        oracle.spectral_conv2d_torch(x, w1, w2, c["m1"], c["m2"])
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > 4 * budget_s:
+            break
+    med = statistics.median(times)
+    return {"value": c["B"] / med, "unit": "samples/s", "cores": torch.get_num_threads(), "kind": "port",
+            "ms_per_step": med * 1e3,
+            "sample": f"{len(times)} full forwards of {name} (B={c['B']}), median; torch.fft+einsum on CPU"}
+
+
+def ours(args) -> None:
+    import scx_dist
+
+    rank, local_rank, world = scx_dist.env_rank()
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N>1 needs torchrun (one process per GPU)")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        scx_dist.init("nccl", timeout_s=300)
+    warmup = max(3, args.warmup)
+    res = run_spectral(args.workload, args.steps, warmup, device, world, rank, with_e2e=True,
+                       with_breakdown=True, sampler_gpu=local_rank if rank == 0 else None)
+    extras = {}
+    if not args.no_extras:
+        for wname in EXTRA_WORKLOADS:
+            if wname == args.workload:
+                continue
+            r = run_spectral(wname, max(10, args.steps // 2), warmup, device, world, rank, with_e2e=False,
+                             with_breakdown=True, sampler_gpu=None)
+            extras[wname] = {"ms_per_step": r["ms_per_step"], "samples_per_s": r["samples_per_s"],
+                             "roofline_fused_path_frac": r["roofline_fused_path"]["frac"],
+                             "dominant_kernel": r["roofline"]["kernel"],
+                             "dominant_kernel_frac": r["roofline"]["frac"],
+                             "kernels_ms": {k: v["ms"] for k, v in r["kernels"].items()}}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.workload)
+    if rank == 0:
+        c = res["cfg"]
+        line = {
+            "metric": "SpectralConv2d fwd samples/s (per-GPU B20, Cin=Cout=32, 128x128, modes 16, GRF input)"
+            if args.workload == HEADLINE else f"SpectralConv2d fwd samples/s ({args.workload})",
+            "value": res["samples_per_s"], "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded Gaussian random field)",
+            "config": {"workload": args.workload, "batch_per_gpu": c["B"], "global_batch": c["B"] * world,
+                       "channels_in": c["Cin"], "channels_out": c["Cout"], "height": c["H"], "width": c["W"],
+                       "modes1": c["m1"], "modes2": c["m2"], "parallelism": f"batch-shard x{world}",
+                       "l2": "inputs rotate over buffer sets totalling >= 3x L2 between steps"},
+            "roofline": res.get("roofline"), "roofline_fused_path": res["roofline_fused_path"],
+            "kernels": res.get("kernels"), "e2e": res.get("e2e"), "cpu_baseline": cpu,
+            "clocks": res["clocks"], "gpu_launches": res["launches_per_step"] * args.steps,
+            "workloads": extras,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def reference(args) -> None:
+    import scx_dist
+
+    rank, _, world = scx_dist.env_rank()
+    if rank != 0:
+        return
+    import scx_data
+    from oracle import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    x, w1, w2, c = scx_data.make_spectral_case(args.workload)
+    warmup = max(3, args.warmup)
+    # bound the run to a few minutes: one full forward per step when it is short enough,
+    # otherwise a batch slice of the same workload
+    t0 = time.perf_counter()
+    oracle.spectral_conv2d_torch(x, w1, w2, c["m1"], c["m2"])
+    t_one = time.perf_counter() - t0
+    budget = 150.0
+    nb = c["B"]
+    if t_one * (warmup + args.steps) > budget:
+        nb = max(1, int(c["B"] * budget / (t_one * (warmup + args.steps))))
+    xs = x[:nb].contiguous()
+    for _ in range(warmup):
+        oracle.spectral_conv2d_torch(xs, w1, w2, c["m1"], c["m2"])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.spectral_conv2d_torch(xs, w1, w2, c["m1"], c["m2"])
+    dt = (time.perf_counter() - t0) / args.steps
+    value = nb / dt
+    line = {
+        "impl": "reference", "metric": "SpectralConv2d fwd samples/s (per-GPU B20, Cin=Cout=32, 128x128, modes 16,"
+        " GRF input)" if args.workload == HEADLINE else f"SpectralConv2d fwd samples/s ({args.workload})",
+        "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian random field)",
+        "config": {"workload": args.workload, "batch_per_step": nb, "channels_in": c["Cin"],
+                   "channels_out": c["Cout"], "height": c["H"], "width": c["W"], "modes1": c["m1"],
+                   "modes2": c["m2"]},
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{args.steps} forwards of {nb} batch items; the reference's torch.fft + "
+                                   "einsum recipe (reference_pytorch.py) restated, on the host CPU"},
+        "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        reference(args)
+    else:
+        ours(args)
+
+
+if __name__ == "__main__":
+    main()

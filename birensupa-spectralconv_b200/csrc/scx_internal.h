@@ -1,0 +1,64 @@
+// Internal declarations shared by the sm_100a kernels and the C-ABI layer.
+//
+// Data layout in HBM (all fp32, complex values interleaved re/im = float2):
+//   x            [P = B*Cin ][H][W]          real input planes
+//   corner spec  [B][C][m1][m2] float2        one array per corner, the layout of
+//                                             spectral_conv/spectral_conv_ext.cpp:26-31
+//   weights      [Cin][Cout][m1][m2] float2   view_as_real of the complex64 Parameter
+//   y            [Q = B*Cout][H][W]          real output planes
+//
+// Corner 1 holds spectrum rows kx in [0, m1), corner 2 rows kx in [H-m1, H), both for
+// ky in [0, m2) (spectral_conv/reference_pytorch.py:41-46).  When 2*m1 > H the rows
+// overlap and corner 2 wins on the inverse side, exactly as the second slice
+// assignment in the reference overwrites the first.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace scx {
+
+// Host-built (double precision) twiddle tables for one (H, W, m1, m2) shape, resident on
+// one device.  Owned by a process-wide cache; never freed before process exit.
+struct Twiddles {
+    int H, W, m1, m2;
+    const float2* row_fwd;  // [W][m2]    (cos, -sin)(2 pi ky w / W)
+    const float2* col_fwd;  // [2*m1][H]  exp(-2 pi i kx(slot) h / H)
+    const float2* col_inv;  // [H][2*m1]  exp(+2 pi i kx(slot) h / H); 0 where corner 2 overwrites
+    const float2* row_inv;  // [m2][W]    c_ky/(H*W) * (cos, sin)(2 pi ky w / W)
+};
+
+// Returns the cached tables for the current device, building them on first use
+// (one cudaMalloc + one cudaMemcpy, so the first call must not happen inside stream
+// capture).  Thread-safe.
+cudaError_t get_twiddles(int H, int W, int m1, int m2, const Twiddles** out);
+
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+// ---- kernel launchers (no argument validation here; the C-ABI layer validates) ----
+
+// Truncated forward real DFT of P planes, writing the two corner spectra.
+// Output element (plane p, corner row j, ky) lives at
+//   out_c + p*out_plane_stride + j*out_row_stride + ky.
+cudaError_t launch_dft_fwd(const float* x, float2* out1, float2* out2,
+                           long long out_plane_stride, int out_row_stride,
+                           int P, int H, int W, int m1, int m2,
+                           const Twiddles& tw, cudaStream_t stream);
+
+// Zero-padded inverse real DFT of Q planes from the two corner spectra (corner 2
+// overwrites corner 1 where the rows overlap).  Input element (plane q, row j, ky) at
+//   in_c + q*in_plane_stride + j*in_row_stride + ky.
+cudaError_t launch_dft_inv(const float2* in1, const float2* in2,
+                           long long in_plane_stride, int in_row_stride,
+                           float* y, int Q, int H, int W, int m1, int m2,
+                           const Twiddles& tw, cudaStream_t stream);
+
+// Per-mode complex channel mixing y_c[b,o,k] = sum_i x_c[b,i,k] * w_c[i,o,k] for
+// ncorner (1 or 2) corners, k over NM = m1*m2 modes.
+cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, const float2* w2,
+                       float2* y1, float2* y2, int ncorner, int B, int Cin, int Cout, int NM,
+                       cudaStream_t stream);
+
+}  // namespace scx

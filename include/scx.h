@@ -1,0 +1,110 @@
+/*
+ * scx.h - C ABI of the B200 (sm_100a) SpectralConv2d / FNO-2d forward library (libscx.so).
+ *
+ * Drop-in device layer for the reference's SUPA extension: every entry point takes plain
+ * device pointers, sizes and a CUDA stream, returns a status code and never allocates the
+ * caller's buffers.  Status codes are cudaError_t values (0 = success, 1 =
+ * cudaErrorInvalidValue for bad arguments); scx_status_string() names them.  No entry
+ * point aborts, traps or synchronises the device.
+ *
+ * Tensor layouts (fp32; complex values interleaved re/im, i.e. view_as_real of complex64):
+ *   x        [B][Cin][H][W]             real input
+ *   y        [B][Cout][H][W]            real output
+ *   weights  [Cin][Cout][m1][m2][2]     one tensor per corner (weights1, weights2)
+ *   corner   [B][C][m1][m2][2]          corner 1 = rows kx in [0,m1), corner 2 = rows
+ *                                       kx in [H-m1,H), both for ky in [0,m2)
+ *   spectrum [B][C][H][W/2+1][2]        full half-spectrum (compatibility entry points)
+ * Shape rules are the reference's: 1 <= m1 <= H and 1 <= m2 <= W/2+1; when 2*m1 > H the
+ * corner rows overlap and corner 2 overwrites corner 1 (spectral_conv/reference_pytorch.py:41-46).
+ *
+ * Twiddle tables are built once per (device, H, W, m1, m2) by the library and kept for
+ * the life of the process; the first call for a shape performs that set-up (a
+ * cudaMalloc and a synchronous copy), so make it outside CUDA-graph capture, e.g. with
+ * scx_prepare().  Calls are thread-safe.
+ */
+#ifndef SCX_H_
+#define SCX_H_
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t; NULL selects the legacy default stream. */
+typedef void* scx_stream_t;
+
+/* Library version, major*10000 + minor*100 + patch. */
+int scx_version(void);
+
+/* Human-readable name of a status code returned by this library. */
+const char* scx_status_string(int status);
+
+/* Builds (if needed) the twiddle tables for one shape on the current device.
+ * Replaces the suFFT plan/work-area warm-up: get_cached_plan / get_workspace
+ * (spectral_conv/spectral_conv_ext.cpp:77-121) driven by warmup_spectral_plans
+ * (spectral_conv/spectral_conv_ops.py:459-477). */
+int scx_prepare(int H, int W, int modes1, int modes2);
+
+/* Single-corner complex mode mixing y[b,o,k] = sum_i x[b,i,k] * w[i,o,k].
+ * Replaces launch_spectral_mul (spectral_conv_combo/spectral_conv_ext.su:94-109), same
+ * argument order; the stream is honoured instead of the null stream.
+ * x_freq [B][Cin][m1][m2][2], weights [Cin][Cout][m1][m2][2], y_freq [B][Cout][m1][m2][2]. */
+int scx_spectral_mul(const float* x_freq, const float* weights, float* y_freq, int batch_size,
+                     int channels_in, int channels_out, int modes1, int modes2,
+                     scx_stream_t stream);
+
+/* Both corners in one launch.  Replaces launch_spectral_mul_dual_packed
+ * (spectral_conv_combo/spectral_conv_ext.su:111-127), same argument order; serves the
+ * pybind entry points spectral_mul_dual_out (spectral_conv/spectral_conv_ext.cpp:200-245). */
+int scx_spectral_mul_dual(const float* x1, const float* x2, const float* w1, const float* w2,
+                          float* y1, float* y2, int batch_size, int channels_in,
+                          int channels_out, int modes1, int modes2, scx_stream_t stream);
+
+/* Truncated forward real DFT writing only the two retained corners.
+ * Replaces rfft2_sufft followed by the corner gathers x_freq[:, :, :m1, :m2] and
+ * x_freq[:, :, -m1:, :m2] (spectral_conv/spectral_conv_ext.cpp:314-347,
+ * spectral_conv/spectral_conv_ops.py:385-392).
+ * x [B][C][H][W]; x1, x2 [B][C][m1][m2][2]. */
+int scx_rfft2_corners(const float* x, float* x1, float* x2, int batch_size, int channels,
+                      int height, int width, int modes1, int modes2, scx_stream_t stream);
+
+/* Zero-padded inverse real DFT from the two corners straight to the real output.
+ * Replaces the zeroed out_freq buffer, the two corner scatters and irfft2_sufft
+ * (spectral_conv/spectral_conv_ops.py:386-406, spectral_conv/spectral_conv_ext.cpp:349-384).
+ * y1, y2 [B][C][m1][m2][2]; y [B][C][H][W]. */
+int scx_irfft2_corners(const float* y1, const float* y2, float* y, int batch_size, int channels,
+                       int height, int width, int modes1, int modes2, scx_stream_t stream);
+
+/* Full half-spectrum forward 2-D real DFT, x [B][C][H][W] -> x_freq [B][C][H][W/2+1][2].
+ * Compatibility path for rfft2_sufft (spectral_conv/spectral_conv_ext.cpp:314-347);
+ * not used by the fused forward. */
+int scx_rfft2(const float* x, float* x_freq, int batch_size, int channels, int height,
+              int width, scx_stream_t stream);
+
+/* Full half-spectrum inverse 2-D real DFT (scale 1/(H*W)), x_freq [B][C][H][W/2+1][2] ->
+ * y [B][C][H][W].  Compatibility path for irfft2_sufft
+ * (spectral_conv/spectral_conv_ext.cpp:349-384); not used by the fused forward. */
+int scx_irfft2(const float* x_freq, float* y, int batch_size, int channels, int height,
+               int width, scx_stream_t stream);
+
+/* Bytes of device workspace scx_spectral_conv2d_fwd needs (the two corner spectra in and
+ * out); 0 on invalid sizes. */
+size_t scx_spectral_conv2d_workspace_size(int batch_size, int channels_in, int channels_out,
+                                          int height, int width, int modes1, int modes2);
+
+/* Fused SpectralConv2d forward: truncated rfft2 -> dual-corner mixing -> zero-padded
+ * irfft2, y = SpectralConv2d(x) of spectral_conv/reference_pytorch.py:30-47.
+ * Replaces spectral_conv2d_fused (spectral_conv/spectral_conv_ops.py:363-417) and its
+ * native calls.  workspace: caller-owned device memory of at least
+ * scx_spectral_conv2d_workspace_size() bytes, 16-byte aligned. */
+int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* weights2,
+                            float* y, int batch_size, int channels_in, int channels_out,
+                            int height, int width, int modes1, int modes2, void* workspace,
+                            size_t workspace_bytes, scx_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SCX_H_ */

@@ -1,0 +1,90 @@
+"""CPU: host-side logic of the drop-in API (no device calls)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import scx_dist
+import spectral_conv_ext
+import spectral_conv_ops
+
+
+@pytest.mark.parametrize("value,expected", [
+    (True, True), (False, False), ("fused", True), ("sufft", True), ("supa", True), ("v1", False),
+    ("cpu", False), (" Fused ", True),
+])
+def test_resolve_use_sufft_explicit(value, expected):
+    assert spectral_conv_ops.resolve_use_sufft(64, 64, value) is expected
+
+
+def test_resolve_use_sufft_auto_and_table():
+    assert spectral_conv_ops.resolve_use_sufft(64, 128, "auto") is True
+    assert spectral_conv_ops.resolve_use_sufft(32, 128, "auto") is False
+    spectral_conv_ops._AUTO_TUNE_TABLE[32] = {"use_sufft": True}
+    try:
+        assert spectral_conv_ops.resolve_use_sufft(32, 128, "adaptive") is True
+    finally:
+        spectral_conv_ops._AUTO_TUNE_TABLE.clear()
+
+
+def test_resolve_use_sufft_errors():
+    with pytest.raises(ValueError):
+        spectral_conv_ops.resolve_use_sufft(64, 64, "gpu")
+    with pytest.raises(TypeError):
+        spectral_conv_ops.resolve_use_sufft(64, 64, 1)
+
+
+def test_input_rank_checked_before_device_use():
+    w = torch.zeros(2, 2, 2, 2, dtype=torch.cfloat)
+    with pytest.raises(ValueError):
+        spectral_conv_ops.spectral_conv2d_supa(torch.zeros(2, 8, 8), w, w, 2, 2)
+
+
+def test_ext_checks_raise_runtime_error():
+    cpu = torch.zeros(1, 2, 2, 2, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        spectral_conv_ext.spectral_mul(cpu, cpu)
+    with pytest.raises(RuntimeError, match="last dim must be 2"):
+        spectral_conv_ext.spectral_mul(torch.zeros(1, 2, 2, 2, 3), cpu)
+    with pytest.raises(RuntimeError, match="float32"):
+        spectral_conv_ext.spectral_mul(torch.zeros(1, 2, 2, 2, 2, dtype=torch.float64), cpu)
+    with pytest.raises(RuntimeError, match="shape"):
+        spectral_conv_ext.spectral_mul(torch.zeros(2, 2, 2, 2), cpu)
+
+
+def test_module_parameters_match_reference_layout():
+    torch.manual_seed(0)
+    a = spectral_conv_ops.SpectralConv2dSupa(3, 4, 5, 6)
+    torch.manual_seed(0)
+    b = spectral_conv_ops.SpectralConv2d(3, 4, 5, 6)
+    assert list(a.state_dict()) == ["weights1", "weights2"] == list(b.state_dict())
+    assert a.weights1.shape == (3, 4, 5, 6) and a.weights1.dtype == torch.complex64
+    assert torch.equal(a.weights1, b.weights1) and torch.equal(a.weights2, b.weights2)
+    assert 0 <= a.weights1.real.min() and a.weights1.real.max() < 1.0 / 12
+    assert 0 <= a.weights1.imag.min() and a.weights1.imag.max() < 1.0 / 12
+
+
+@pytest.mark.parametrize("batch,world,expected", [
+    (20, 8, [3, 3, 3, 3, 2, 2, 2, 2]), (16, 8, [2] * 8), (160, 8, [20] * 8), (3, 4, [1, 1, 1, 0]),
+    (20, 1, [20]),
+])
+def test_shard_sizes(batch, world, expected):
+    assert scx_dist.shard_sizes(batch, world) == expected
+    ranges = [scx_dist.shard_range(batch, world, r) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == batch
+    assert all(ranges[i][1] == ranges[i + 1][0] for i in range(world - 1))
+
+
+def test_fno_model_structure():
+    import fno_model
+
+    torch.manual_seed(0)
+    m = fno_model.FNO2d(modes1=12, modes2=12, width=32, n_layers=4, in_channels=10)
+    names = list(m.state_dict())
+    assert names[:2] == ["lift.weight", "lift.bias"]
+    assert "fourier_layers.3.spectral_conv.weights2" in names and names[-1] == "project.2.bias"
+    with pytest.raises(ValueError):
+        fno_model.FNO2d(n_layers=3)
+    nn_free = fno_model.FNO2d(instance_norm=False)
+    assert list(nn_free.state_dict()) == names

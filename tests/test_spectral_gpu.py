@@ -1,0 +1,242 @@
+"""GPU parity of the CUDA SpectralConv2d path against the oracle and the reference's
+golden fixtures.  Tolerance: the reference's own 1e-4 on both metrics it uses (Frobenius
+relative error, spectral_conv_combo/test_accuracy.py:16,22-27; max-abs / max|ref|,
+spectral_conv_combo/test_irregular_shapes.py:78-80); the kernels compute in fp32."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import scx_data
+from conftest import GOLDEN, load_golden
+from oracle import oracle
+from test_oracle import check_against_golden, regenerate
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-4
+SPECTRAL_FIXTURES = sorted(p.name for p in GOLDEN.glob("spectral_*.npz"))
+
+
+def run_device(x, w1, w2, m1, m2, device):
+    import spectral_conv_ops
+
+    y = spectral_conv_ops.spectral_conv2d_supa(x.to(device), w1.to(device), w2.to(device), m1, m2,
+                                               use_sufft="fused", to_cpu=False)
+    torch.cuda.synchronize(device)
+    return y
+
+
+def assert_close(ref, got, tol=TOL):
+    fro, mx = oracle.rel_errors(ref, got)
+    assert fro <= tol and mx <= tol, f"frobenius rel {fro:.3e}, max-abs rel {mx:.3e}"
+    return fro, mx
+
+
+@pytest.mark.parametrize("fixture", SPECTRAL_FIXTURES)
+def test_parity_with_reference_fixtures(fixture, cuda_device):
+    g = load_golden(fixture)
+    x, w1, w2, (B, Cin, Cout, H, W, m1, m2) = regenerate(g)
+    y = run_device(x, w1, w2, m1, m2, cuda_device).cpu().numpy()
+    assert np.isfinite(y).all()
+    check_against_golden(g, y, TOL)
+    ref = oracle.spectral_conv2d_torch(x, w1, w2, m1, m2).numpy()
+    assert_close(ref, y)
+
+
+@pytest.mark.parametrize("shape", [
+    (2, 3, 4, 9, 11, 6, 6),     # 2*m1 > H (overlap), odd H and W
+    (1, 2, 2, 7, 7, 7, 4),      # m1 = H, odd W, m2 = W//2+1
+    (2, 3, 5, 12, 10, 4, 6),    # Nyquist column included (W even, m2 = W//2+1)
+    (1, 1, 1, 1, 1, 1, 1),      # 1x1 grid
+    (3, 5, 2, 16, 8, 1, 1),     # DC only
+    (1, 3, 7, 33, 31, 5, 16),   # odd, Cin != Cout, B = 1
+    (5, 6, 4, 40, 64, 20, 33),  # m1 = H/2 exactly, Nyquist
+    (2, 4, 4, 300, 20, 3, 11),  # tall, more rows than one chunk
+    (1, 2, 3, 16, 600, 8, 40),  # wide: more than one 256-column pass
+])
+def test_edge_shapes_vs_f64_oracle(shape, cuda_device):
+    B, Cin, Cout, H, W, m1, m2 = shape
+    g = torch.Generator().manual_seed(sum(shape))
+    x = torch.randn(B, Cin, H, W, generator=g)
+    scale = 1.0 / (Cin * Cout)
+    w1 = scale * torch.rand(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g)
+    w2 = scale * torch.rand(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g)
+    y = run_device(x, w1, w2, m1, m2, cuda_device).cpu().numpy()
+    ref = oracle.spectral_conv2d_f64(x.numpy(), w1.numpy(), w2.numpy(), m1, m2)
+    assert_close(ref, y)
+
+
+@pytest.mark.parametrize("name", list(scx_data.SPECTRAL_WORKLOADS))
+def test_workloads_full_size(name, cuda_device):
+    x, w1, w2, c = scx_data.make_spectral_case(name)
+    y = run_device(x, w1, w2, c["m1"], c["m2"], cuda_device)
+    ref = oracle.spectral_conv2d_torch(x, w1, w2, c["m1"], c["m2"])
+    assert_close(ref.numpy(), y.cpu().numpy())
+
+
+def test_linearity_full_size(cuda_device):
+    """Size-independent property at the 256x256 workload: f(a x1 + b x2) = a f(x1) + b f(x2)."""
+    x, w1, w2, c = scx_data.make_spectral_case("spectral_b16_c64_256x256_m32", batch=4)
+    x2 = scx_data.gaussian(tuple(x.shape), 99)
+    a, b = 0.75, -1.5
+    y1 = run_device(x, w1, w2, c["m1"], c["m2"], cuda_device)
+    y2 = run_device(x2, w1, w2, c["m1"], c["m2"], cuda_device)
+    y12 = run_device(a * x + b * x2, w1, w2, c["m1"], c["m2"], cuda_device)
+    assert_close((a * y1 + b * y2).cpu().numpy(), y12.cpu().numpy(), 1e-5)
+
+
+def test_deterministic_and_fully_written(cuda_device):
+    """Two runs are bitwise identical and every output element is written (NaN-poisoned
+    output buffer)."""
+    import spectral_conv_ext
+
+    x, w1, w2, c = scx_data.make_spectral_case("spectral_b20_c32_64x64_m12")
+    xd = x.to(cuda_device)
+    w1d = torch.view_as_real(w1.to(cuda_device))
+    w2d = torch.view_as_real(w2.to(cuda_device))
+    out = torch.full((c["B"], c["Cout"], c["H"], c["W"]), float("nan"), device=cuda_device)
+    y1 = spectral_conv_ext.spectral_conv2d_fwd(xd, w1d, w2d, c["m1"], c["m2"], out=out).clone()
+    y2 = spectral_conv_ext.spectral_conv2d_fwd(xd, w1d, w2d, c["m1"], c["m2"])
+    assert torch.isfinite(y1).all()
+    assert torch.equal(y1, y2)
+
+
+def test_spectral_mul_entry_points(cuda_device):
+    import spectral_conv_ext
+    import spectral_conv_ops
+
+    g = torch.Generator().manual_seed(3)
+    B, Cin, Cout, m1, m2 = 3, 5, 7, 6, 5
+    x = torch.randn(B, Cin, m1, m2, dtype=torch.cfloat, generator=g)
+    w = torch.randn(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g)
+    ref = torch.einsum("bixy,ioxy->boxy", x.to(torch.complex128), w.to(torch.complex128))
+    xd = torch.view_as_real(x.to(cuda_device)).contiguous()
+    wd = torch.view_as_real(w.to(cuda_device)).contiguous()
+    y = spectral_conv_ext.spectral_mul(xd, wd)
+    assert_close(torch.view_as_real(ref).numpy(), y.cpu().numpy(), 1e-6)
+    yo = torch.empty_like(y)
+    spectral_conv_ext.spectral_mul_out(xd, wd, yo)
+    assert torch.equal(yo, y)
+    # dual: both corners in one launch
+    x2 = torch.randn(B, Cin, m1, m2, dtype=torch.cfloat, generator=g)
+    w2 = torch.randn(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g)
+    x2d = torch.view_as_real(x2.to(cuda_device)).contiguous()
+    w2d = torch.view_as_real(w2.to(cuda_device)).contiguous()
+    y1 = torch.empty_like(y)
+    y2 = torch.empty_like(y)
+    spectral_conv_ext.spectral_mul_dual_out(xd, wd, x2d, w2d, y1, y2)
+    ref2 = torch.einsum("bixy,ioxy->boxy", x2.to(torch.complex128), w2.to(torch.complex128))
+    assert torch.equal(y1, y)
+    assert_close(torch.view_as_real(ref2).numpy(), y2.cpu().numpy(), 1e-6)
+    # legacy complex bridge (CPU complex out) and autograd wrapper
+    yc = spectral_conv_ops.spectral_mul_supa(x, w)
+    assert yc.device.type == "cpu" and yc.dtype == torch.complex64
+    assert_close(torch.view_as_real(ref).numpy(), torch.view_as_real(yc).numpy(), 1e-6)
+
+
+def test_spectral_mul_autograd_grads(cuda_device):
+    """spectral_conv_combo/test_backward.py:27-54 cases."""
+    import spectral_conv_ops
+
+    for (b, ci, co, m1, m2) in [(2, 2, 3, 4, 4), (2, 4, 4, 8, 8), (2, 4, 4, 12, 12)]:
+        g = torch.Generator().manual_seed(42)
+        x = torch.randn(b, ci, m1, m2, generator=g, dtype=torch.cfloat)
+        w = torch.randn(ci, co, m1, m2, generator=g, dtype=torch.cfloat)
+        xr = x.clone().requires_grad_(True)
+        wr = w.clone().requires_grad_(True)
+        yr = torch.einsum("bixy,ioxy->boxy", xr, wr)
+        (yr.real.pow(2) + yr.imag.pow(2)).sum().backward()
+        xa = x.clone().requires_grad_(True)
+        wa = w.clone().requires_grad_(True)
+        ya = spectral_conv_ops.spectral_mul_autograd(xa, wa)
+        (ya.real.pow(2) + ya.imag.pow(2)).sum().backward()
+        for ref, got in ((yr.detach(), ya.detach()), (xr.grad, xa.grad), (wr.grad, wa.grad)):
+            assert_close(torch.view_as_real(ref).numpy(), torch.view_as_real(got).numpy(), 1e-4)
+
+
+@pytest.mark.parametrize("H,W", [(16, 16), (9, 12), (12, 9), (64, 40), (5, 3)])
+def test_full_spectrum_compat(H, W, cuda_device):
+    """rfft2_sufft / irfft2_sufft compatibility entry points vs numpy FFT."""
+    import spectral_conv_ext
+
+    g = torch.Generator().manual_seed(H * 100 + W)
+    x = torch.randn(2, 3, H, W, generator=g)
+    xf = spectral_conv_ext.rfft2_sufft(x.to(cuda_device)).cpu()
+    ref = np.fft.rfft2(x.numpy().astype(np.float64))
+    got = xf[..., 0].numpy() + 1j * xf[..., 1].numpy()
+    assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+    spec = torch.randn(2, 3, H, W // 2 + 1, 2, generator=g)
+    y = spectral_conv_ext.irfft2_sufft(spec.to(cuda_device), H, W).cpu().numpy()
+    ref_y = np.fft.irfft2(spec[..., 0].numpy().astype(np.float64) + 1j * spec[..., 1].numpy(), s=(H, W))
+    assert np.abs(y - ref_y).max() <= 1e-5 * np.abs(ref_y).max()
+    # round trip
+    back = spectral_conv_ext.irfft2_sufft(spectral_conv_ext.rfft2_sufft(x.to(cuda_device)), H, W).cpu()
+    assert torch.allclose(back, x, atol=1e-5)
+
+
+def test_corner_entry_points_vs_f64(cuda_device):
+    import spectral_conv_ext
+
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(3, 4, 20, 18, generator=g)
+    c1, c2 = spectral_conv_ext.rfft2_corners(x.to(cuda_device), 6, 7)
+    r1, r2 = oracle.rfft2_corners_f64(x.numpy(), 6, 7)
+    for got, ref in ((c1, r1), (c2, r2)):
+        got = got.cpu().numpy()
+        got = got[..., 0] + 1j * got[..., 1]
+        assert np.abs(got - ref).max() <= 1e-5 * np.abs(ref).max()
+    y = spectral_conv_ext.irfft2_corners(c1, c2, 20, 18).cpu().numpy()
+    full = np.zeros((3, 4, 20, 10), dtype=np.complex128)
+    full[:, :, :6, :7] = r1
+    full[:, :, -6:, :7] = r2
+    ref_y = np.fft.irfft2(full, s=(20, 18))
+    assert np.abs(y - ref_y).max() <= 1e-5 * np.abs(ref_y).max()
+
+
+def test_non_default_stream_and_module_api(cuda_device):
+    import spectral_conv_ops
+
+    torch.manual_seed(0)
+    mod = spectral_conv_ops.SpectralConv2dSupa(6, 5, 4, 3)
+    x = torch.randn(2, 6, 16, 12)
+    ref = oracle.spectral_conv2d_f64(x.numpy(), mod.weights1.detach().numpy(), mod.weights2.detach().numpy(), 4, 3)
+    y_host = mod(x)                      # host in, host out (reference contract)
+    assert y_host.device.type == "cpu"
+    assert_close(ref, y_host.detach().numpy())
+    y_host2 = mod(x)
+    assert y_host2.data_ptr() != y_host.data_ptr()   # no aliasing of host results
+    s = torch.cuda.Stream(cuda_device)
+    with torch.cuda.stream(s):
+        y_dev = mod(x.to(cuda_device), to_cpu=False)
+    s.synchronize()
+    assert y_dev.is_cuda
+    assert_close(ref, y_dev.cpu().detach().numpy())
+    neutral = spectral_conv_ops.SpectralConv2d(6, 5, 4, 3)
+    neutral.load_state_dict(mod.state_dict())
+    neutral = neutral.to(cuda_device)
+    assert_close(ref, neutral(x.to(cuda_device)).cpu().detach().numpy())
+
+
+def test_errors_are_raised_not_faulted(cuda_device):
+    import spectral_conv_ext
+    import spectral_conv_ops
+
+    x = torch.randn(1, 2, 8, 8, device=cuda_device)
+    w = torch.zeros(2, 2, 9, 2, 2, device=cuda_device)
+    with pytest.raises(RuntimeError):
+        spectral_conv_ext.spectral_conv2d_fwd(x, w, w, 9, 2)       # m1 > H
+    w = torch.zeros(2, 2, 2, 6, 2, device=cuda_device)
+    with pytest.raises(RuntimeError):
+        spectral_conv_ext.spectral_conv2d_fwd(x, w, w, 2, 6)       # m2 > W//2+1
+    with pytest.raises(RuntimeError):
+        spectral_conv_ext.spectral_mul(torch.zeros(1, 2, 2, 2, 2, device=cuda_device),
+                                       torch.zeros(3, 2, 2, 2, 2, device=cuda_device))   # C_in mismatch
+    with pytest.raises(ValueError):
+        spectral_conv_ops.spectral_conv2d_supa(torch.zeros(2, 8, 8), w, w, 2, 2)
+    # the context is still usable
+    y = spectral_conv_ext.spectral_mul(torch.ones(1, 1, 1, 1, 2, device=cuda_device),
+                                       torch.ones(1, 1, 1, 1, 2, device=cuda_device))
+    assert y.cpu().tolist() == [[[[[0.0, 2.0]]]]]

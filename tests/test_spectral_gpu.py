@@ -208,9 +208,12 @@ def test_non_default_stream_and_module_api(cuda_device):
     assert_close(ref, y_host.detach().numpy())
     y_host2 = mod(x)
     assert y_host2.data_ptr() != y_host.data_ptr()   # no aliasing of host results
+    # "auto" on a map smaller than 64 selects the reference's v1 contract: host result
+    # even with to_cpu=False (spectral_conv/spectral_conv_ops.py:504-505)
+    assert mod(x.to(cuda_device), to_cpu=False).device.type == "cpu"
     s = torch.cuda.Stream(cuda_device)
     with torch.cuda.stream(s):
-        y_dev = mod(x.to(cuda_device), to_cpu=False)
+        y_dev = mod(x.to(cuda_device), use_sufft="fused", to_cpu=False)
     s.synchronize()
     assert y_dev.is_cuda
     assert_close(ref, y_dev.cpu().detach().numpy())

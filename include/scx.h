@@ -103,6 +103,27 @@ int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* 
                             int height, int width, int modes1, int modes2, void* workspace,
                             size_t workspace_bytes, scx_stream_t stream);
 
+/* Size of the fixed device scratch used by scx_spectral_conv2d_fwd_noalloc (16 MiB). */
+#define SCX_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* Allocation-free variant of scx_spectral_conv2d_fwd.  No counterpart in the reference:
+ * it exists for callers that cannot let a library call cudaMalloc (a process whose
+ * memory pool already owns the GPU's memory, or a latency-critical loop that cannot
+ * absorb an allocation's device synchronisation).  Same arguments and result as
+ * scx_spectral_conv2d_fwd minus the workspace: the corner spectra and the twiddle tables
+ * live in one library-owned static device array of SCX_NOALLOC_SCRATCH_BYTES, held by
+ * every GPU that loads the library until the process exits.  Its scratch need is
+ *   sum over {X1,X2,Y1,Y2,four twiddle tables} of the region size rounded up to 256 B,
+ * i.e. about 16*B*(Cin+Cout)*m1*m2 + 32*(W*m2 + 2*m1*H) bytes; larger shapes return
+ * cudaErrorMemoryAllocation (2) without launching.  The first call on a device looks up
+ * the array's address (cudaGetSymbolAddress) with that device current: make it before
+ * any stream capture.  All calls share the array: calls that overlap on the GPU race, so
+ * order them on one stream.  Nothing has to be cleared between calls. */
+int scx_spectral_conv2d_fwd_noalloc(const float* x, const float* weights1, const float* weights2,
+                                    float* y, int batch_size, int channels_in, int channels_out,
+                                    int height, int width, int modes1, int modes2,
+                                    scx_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

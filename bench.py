@@ -18,7 +18,8 @@ Rank 0 prints ONE JSON line.  Besides the contract keys it carries
   pinned host input and a host result), H2D and D2H inside the timed region;
 * ``cpu_baseline``: the reference's CPU recipe (torch.fft + einsum, all host threads) on
   the same workload (rank 0, N=1);
-* ``workloads``: the 64x64 and 256x256 SpectralConv2d forwards measured the same way.
+* ``workloads``: the 64x64 and 256x256 SpectralConv2d forwards measured the same way, and
+  the FNO-NS forward (B=20 per GPU, samples/s, NCCL output gather included when N > 1).
 
 ``--impl reference`` times the reference's CPU implementation of the path (its torch.fft
 + einsum recipe restated in ``oracle/``) on this host's cores, same workload and metric.
@@ -284,6 +285,62 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
     return res
 
 
+def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
+    """FNO-NS forward, B=20 per GPU, [B,64,64,12] channels-last input, width 32, modes 12,
+    4 layers, InstanceNorm layers; the whole forward is one libscx call replayed from a CUDA
+    graph.  L2 is flushed (256 MiB write) between timed steps; each step is timed with its
+    own CUDA events.  With N > 1 the step ends with the NCCL gather of all outputs to rank 0."""
+    import fno_model
+    import scx_data
+    import scx_dist
+
+    fw = scx_data.FNO_WORKLOAD
+    torch.manual_seed(fw["init_seed"])
+    model = fno_model.FNO2d(modes1=fw["modes"], modes2=fw["modes"], width=fw["width"], n_layers=fw["layers"],
+                            in_channels=fw["frames"]).to(device)
+    B = fw["B"]
+    x = scx_data.fno_input(B, fw["seed"] + rank, H=fw["H"], W=fw["W"], frames=fw["frames"]).to(device)
+    out = torch.empty(B, 1, fw["H"], fw["W"], device=device)
+    model.forward_device(x, channels_last=True, out=out)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        model.forward_device(x, channels_last=True, out=out)
+    torch.cuda.current_stream(device).wait_stream(side)
+    with torch.cuda.graph(graph):
+        model.forward_device(x, channels_last=True, out=out)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        graph.replay()
+        if world > 1:
+            scx_dist.gather_batch(out, B * world)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in evs:
+        flush.zero_()
+        e0.record(stream)
+        step()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    t_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
+    t_ms = scx_dist.max_over_ranks(t_ms, device)
+    ms = t_ms / steps
+    del graph
+    return {"ms_per_step": ms, "samples_per_s": world * B / (ms / 1e3), "batch_per_gpu": B,
+            "launches_per_step": 2 + 4 * fw["layers"], "cuda_graph": True,
+            "gather": "nccl all_gather_into_tensor to rank 0 inside the step" if world > 1 else None,
+            "l2": "256 MiB flush between steps (not timed)"}
+
+
 def cpu_baseline(name: str, budget_s: float = 12.0) -> dict:
     """The reference's CPU recipe on the same workload, all host threads, bounded sample."""
     import scx_data
@@ -334,6 +391,7 @@ def ours(args) -> None:
                              "dominant_kernel": r["roofline"]["kernel"],
                              "dominant_kernel_frac": r["roofline"]["frac"],
                              "kernels_ms": {k: v["ms"] for k, v in r["kernels"].items()}}
+        extras["fno_ns_b20_w32_64x64_m12_l4"] = run_fno(max(10, args.steps // 2), warmup, device, world, rank)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.workload)

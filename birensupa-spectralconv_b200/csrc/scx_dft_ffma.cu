@@ -235,14 +235,6 @@ __global__ void __launch_bounds__(kThreads) dft_inv_ffma_kernel(const InvArgs a)
     }
 }
 
-template <typename K>
-int blocks_per_sm(K kernel, size_t smem) {
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem) != cudaSuccess || n < 1)
-        n = 1;
-    return n;
-}
-
 }  // namespace
 
 cudaError_t launch_dft_fwd(const float* x, float2* out1, float2* out2, long long out_plane_stride,
@@ -282,10 +274,9 @@ cudaError_t launch_dft_fwd(const float* x, float2* out1, float2* out2, long long
     const int npt_needed = (ST * KT + kThreads - 1) / kThreads;
     const dim3 block(kThreads);
     auto run = [&](auto kernel) -> cudaError_t {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
+        int per_sm = 1;
+        cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(kernel), smem, kThreads, &per_sm);
         if (e != cudaSuccess) return e;
-        const int per_sm = blocks_per_sm(kernel, smem);
         const int gx = std::max(1, std::min(P, per_sm * num_sms()));
         const dim3 grid(gx, (m2 + KT - 1) / KT, (2 * m1 + ST - 1) / ST);
         kernel<<<grid, block, smem, stream>>>(a);
@@ -326,10 +317,9 @@ cudaError_t launch_dft_inv(const float2* in1, const float2* in2, long long in_pl
     const int wpt = (W + kThreads - 1) / kThreads;
     const int tiles = Q * ((H + kRt - 1) / kRt);
     auto run = [&](auto kernel) -> cudaError_t {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
+        int per_sm = 1;
+        cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(kernel), smem, kThreads, &per_sm);
         if (e != cudaSuccess) return e;
-        const int per_sm = blocks_per_sm(kernel, smem);
         const int gx = std::max(1, std::min(tiles, per_sm * num_sms()));
         kernel<<<gx, kThreads, smem, stream>>>(a);
         return cudaGetLastError();

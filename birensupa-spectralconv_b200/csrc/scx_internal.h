@@ -37,6 +37,11 @@ cudaError_t get_twiddles(int H, int W, int m1, int m2, const Twiddles** out);
 // Number of SMs of the current device (cached per device).
 int num_sms();
 
+// Raises a kernel's dynamic shared-memory limit to at least `bytes` on the current device
+// (once per kernel/device/size: later launches, e.g. inside stream capture, make no call)
+// and returns how many blocks of `threads` threads fit on one SM.
+cudaError_t prepare_kernel(const void* kernel, size_t bytes, int threads, int* blocks_per_sm);
+
 // ---- kernel launchers (no argument validation here; the C-ABI layer validates) ----
 
 // Truncated forward real DFT of P planes, writing the two corner spectra.

@@ -48,6 +48,37 @@ int num_sms() {
     return n;
 }
 
+cudaError_t prepare_kernel(const void* kernel, size_t bytes, int threads, int* blocks_per_sm) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    static std::mutex m;
+    static std::map<std::tuple<int, const void*, size_t, int>, int> seen;
+    // The shared-memory limit is one value per (device, kernel): only ever raise it, or a
+    // later smaller request would lower it under a launch that needs more.
+    static std::map<std::pair<int, const void*>, size_t> limit;
+    std::lock_guard<std::mutex> lock(m);
+    const auto key = std::make_tuple(dev, kernel, bytes, threads);
+    auto it = seen.find(key);
+    if (it != seen.end()) {
+        *blocks_per_sm = it->second;
+        return cudaSuccess;
+    }
+    size_t& cur = limit[std::make_pair(dev, kernel)];
+    if (bytes > 48 * 1024 && bytes > cur) {
+        err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+        if (err != cudaSuccess) return err;
+        cur = bytes;
+    }
+    int n = 0;
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, bytes);
+    if (err != cudaSuccess) return err;
+    if (n < 1) return cudaErrorInvalidConfiguration;
+    seen[key] = n;
+    *blocks_per_sm = n;
+    return cudaSuccess;
+}
+
 cudaError_t get_twiddles(int H, int W, int m1, int m2, const Twiddles** out) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);

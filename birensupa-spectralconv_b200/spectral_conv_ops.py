@@ -190,11 +190,15 @@ def spectral_conv2d_fused(x: torch.Tensor, weights1: torch.Tensor, weights2: tor
     w1 = _weights_to_device_cached(weights1, device)
     w2 = _weights_to_device_cached(weights2, device)
     y = spectral_conv_ext.spectral_conv2d_fwd(x_dev, w1, w2, int(modes1), int(modes2))
-    do_sync = to_cpu if synchronize is None else synchronize
-    if do_sync:
-        torch.cuda.current_stream(device).synchronize()
     if to_cpu:
-        return y.cpu()
+        # a fresh page-locked tensor per call (torch's host caching allocator makes this
+        # cheap), so the copy runs at full PCIe rate and results never alias
+        host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        host.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        return host
+    if synchronize:
+        torch.cuda.current_stream(device).synchronize()
     return y
 
 

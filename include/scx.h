@@ -103,6 +103,56 @@ int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* 
                             int height, int width, int modes1, int modes2, void* workspace,
                             size_t workspace_bytes, scx_stream_t stream);
 
+/* ---------------------------------------------------------------------------------
+ * FNO-2d forward (fno_ns/model.py:137-259): lift -> n_layers x Fourier layer ->
+ * projection, one call.  Replaces FNO2d.forward_supa_chain (fno_ns/model.py:219-259) with
+ * FourierLayer.forward_supa (:101-134).  Fourier layer:
+ *   h' = GELU(InstanceNorm(SpectralConv2d(h) + Conv1x1(h)))   (instance_norm = 1)
+ *   h' = GELU(SpectralConv2d(h) + Conv1x1(h))                  (instance_norm = 0)
+ * InstanceNorm2d defaults: no affine, no running stats, eps 1e-5, biased variance.
+ * GELU is the exact (erf) form.  Projection: Conv1x1(hidden->proj_hidden), GELU,
+ * Conv1x1(proj_hidden->out_channels).
+ * --------------------------------------------------------------------------------- */
+#define SCX_FNO_MAX_LAYERS 16
+
+typedef struct scx_fno2d_config {
+    int batch_size;    /* B */
+    int height;        /* H */
+    int width;         /* W */
+    int in_frames;     /* T: input frames; the lift sees T + 2 channels (frames, grid_x, grid_y) */
+    int input_layout;  /* 0: x [B][T][H][W], the grid is generated inside (fno_ns/model.py:168-194)
+                          1: x [B][H][W][T+2] channels-last, the frames then the 2 grid channels */
+    int hidden;        /* channel width of the Fourier layers */
+    int modes1;
+    int modes2;
+    int n_layers;      /* 1 .. SCX_FNO_MAX_LAYERS */
+    int proj_hidden;   /* 128 in fno_ns/model.py:162-166 */
+    int out_channels;  /* 1 */
+    int instance_norm; /* 1 or 0, see above */
+} scx_fno2d_config;
+
+typedef struct scx_fno2d_params {
+    const float* lift_w;                              /* [hidden][T+2]              */
+    const float* lift_b;                              /* [hidden]                   */
+    const float* spectral_w1[SCX_FNO_MAX_LAYERS];     /* [hidden][hidden][m1][m2][2] */
+    const float* spectral_w2[SCX_FNO_MAX_LAYERS];     /* [hidden][hidden][m1][m2][2] */
+    const float* skip_w[SCX_FNO_MAX_LAYERS];          /* [hidden][hidden] (out, in) */
+    const float* skip_b[SCX_FNO_MAX_LAYERS];          /* [hidden]                   */
+    const float* proj1_w;                             /* [proj_hidden][hidden]      */
+    const float* proj1_b;                             /* [proj_hidden]              */
+    const float* proj2_w;                             /* [out_channels][proj_hidden] */
+    const float* proj2_b;                             /* [out_channels]             */
+} scx_fno2d_params;
+
+/* Device workspace bytes scx_fno2d_fwd needs; 0 for an invalid configuration. */
+size_t scx_fno2d_workspace_size(const scx_fno2d_config* cfg);
+
+/* y [B][out_channels][H][W] = FNO2d(x).  All pointers are device pointers except cfg and
+ * params (host structs).  The first call for a (H, W, modes) shape builds the twiddle
+ * tables (see above). */
+int scx_fno2d_fwd(const scx_fno2d_config* cfg, const scx_fno2d_params* params, const float* x,
+                  float* y, void* workspace, size_t workspace_bytes, scx_stream_t stream);
+
 /* Size of the fixed device scratch used by scx_spectral_conv2d_fwd_noalloc (16 MiB). */
 #define SCX_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 

@@ -52,6 +52,7 @@ _SIGNATURES = {
     "scx_version": ([], _i),
     "scx_status_string": ([_i], ctypes.c_char_p),
     "scx_prepare": ([_i, _i, _i, _i], _i),
+    "scx_watchdog": ([_i], _i),
     "scx_spectral_mul": ([_p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
     "scx_spectral_mul_dual": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
     "scx_rfft2_corners": ([_p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),

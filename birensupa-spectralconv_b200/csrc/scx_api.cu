@@ -3,6 +3,7 @@
 // 123-245 and the launcher checks of spectral_conv_combo/spectral_conv_ext.su:98-101, but
 // reports cudaErrorInvalidValue instead of throwing.
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 
 #include "scx.h"
@@ -36,11 +37,40 @@ bool valid_mix(int B, int Cin, int Cout, int m1, int m2) {
     return fits(B, Cin, m1, m2, 2) && fits(B, Cout, m1, m2, 2) && fits(Cin, Cout, m1, m2, 2);
 }
 
+bool ffma_forced() {
+    const char* v = std::getenv("SCX_VARIANT");
+    return v != nullptr && std::strcmp(v, "ffma") == 0;
+}
+
 }  // namespace
+
+namespace scx {
+
+cudaError_t dft_fwd(const float* x, float2* out1, float2* out2, long long out_plane_stride, int out_row_stride,
+                    int P, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream) {
+    if (!ffma_forced() && tc_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+        return launch_dft_fwd_tc(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, stream);
+    return launch_dft_fwd(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, tw, stream);
+}
+
+cudaError_t dft_inv(const float2* in1, const float2* in2, long long in_plane_stride, int in_row_stride, float* y,
+                    int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream) {
+    if (!ffma_forced() && tc_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(y) & 15) == 0)
+        return launch_dft_inv_tc(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, stream);
+    return launch_dft_inv(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, tw, stream);
+}
+
+}  // namespace scx
 
 extern "C" {
 
 int scx_version(void) { return 100; }
+
+int scx_watchdog(int reset) {
+    int v = 0;
+    const cudaError_t e = scx::read_watchdog(&v, reset != 0);
+    return e == cudaSuccess ? v : -static_cast<int>(e);
+}
 
 const char* scx_status_string(int status) {
     return cudaGetErrorString(static_cast<cudaError_t>(status));
@@ -87,9 +117,9 @@ int scx_rfft2_corners(const float* x, float* x1, float* x2, int batch_size, int 
     const scx::Twiddles* tw = nullptr;
     cudaError_t e = scx::get_twiddles(height, width, modes1, modes2, &tw);
     if (e != cudaSuccess) return e;
-    return scx::launch_dft_fwd(x, reinterpret_cast<float2*>(x1), reinterpret_cast<float2*>(x2),
-                               static_cast<long long>(modes1) * modes2, modes2, batch_size * channels,
-                               height, width, modes1, modes2, *tw, as_stream(stream));
+    return scx::dft_fwd(x, reinterpret_cast<float2*>(x1), reinterpret_cast<float2*>(x2),
+                        static_cast<long long>(modes1) * modes2, modes2, batch_size * channels, height, width,
+                        modes1, modes2, *tw, as_stream(stream));
 }
 
 int scx_irfft2_corners(const float* y1, const float* y2, float* y, int batch_size, int channels,
@@ -100,9 +130,9 @@ int scx_irfft2_corners(const float* y1, const float* y2, float* y, int batch_siz
     const scx::Twiddles* tw = nullptr;
     cudaError_t e = scx::get_twiddles(height, width, modes1, modes2, &tw);
     if (e != cudaSuccess) return e;
-    return scx::launch_dft_inv(reinterpret_cast<const float2*>(y1), reinterpret_cast<const float2*>(y2),
-                               static_cast<long long>(modes1) * modes2, modes2, y, batch_size * channels,
-                               height, width, modes1, modes2, *tw, as_stream(stream));
+    return scx::dft_inv(reinterpret_cast<const float2*>(y1), reinterpret_cast<const float2*>(y2),
+                        static_cast<long long>(modes1) * modes2, modes2, y, batch_size * channels, height, width,
+                        modes1, modes2, *tw, as_stream(stream));
 }
 
 int scx_rfft2(const float* x, float* x_freq, int batch_size, int channels, int height, int width,
@@ -172,15 +202,13 @@ int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* 
     float2* Y1 = X2 + ci;
     float2* Y2 = Y1 + co;
     const long long NM = static_cast<long long>(modes1) * modes2;
-    e = scx::launch_dft_fwd(x, X1, X2, NM, modes2, batch_size * channels_in, height, width, modes1, modes2,
-                            *tw, s);
+    e = scx::dft_fwd(x, X1, X2, NM, modes2, batch_size * channels_in, height, width, modes1, modes2, *tw, s);
     if (e != cudaSuccess) return e;
     e = scx::launch_mix(X1, X2, reinterpret_cast<const float2*>(weights1),
                         reinterpret_cast<const float2*>(weights2), Y1, Y2, 2, batch_size, channels_in,
                         channels_out, static_cast<int>(NM), s);
     if (e != cudaSuccess) return e;
-    return scx::launch_dft_inv(Y1, Y2, NM, modes2, y, batch_size * channels_out, height, width, modes1,
-                               modes2, *tw, s);
+    return scx::dft_inv(Y1, Y2, NM, modes2, y, batch_size * channels_out, height, width, modes1, modes2, *tw, s);
 }
 
 }  // extern "C"

@@ -260,13 +260,13 @@ extern "C" int scx_fno2d_fwd(const scx_fno2d_config* cfg, const scx_fno2d_params
     int cur = 0;
     for (int l = 0; l < cfg->n_layers; ++l) {
         const int spec = (cur + 1) % 3, nxt = (cur + 2) % 3;
-        e = scx::launch_dft_fwd(act[cur], X1, X2, NM, m2, B * C, H, W, m1, m2, *tw, s);
+        e = scx::dft_fwd(act[cur], X1, X2, NM, m2, B * C, H, W, m1, m2, *tw, s);
         if (e != cudaSuccess) return e;
         e = scx::launch_mix(X1, X2, reinterpret_cast<const float2*>(prm->spectral_w1[l]),
                             reinterpret_cast<const float2*>(prm->spectral_w2[l]), Y1, Y2, 2, B, C, C,
                             static_cast<int>(NM), s);
         if (e != cudaSuccess) return e;
-        e = scx::launch_dft_inv(Y1, Y2, NM, m2, act[spec], B * C, H, W, m1, m2, *tw, s);
+        e = scx::dft_inv(Y1, Y2, NM, m2, act[spec], B * C, H, W, m1, m2, *tw, s);
         if (e != cudaSuccess) return e;
         const dim3 g((C + OG - 1) / OG, B);
         fno_skip_norm_gelu_kernel<<<g, kThreads, skip_smem, s>>>(act[spec], act[cur], act[nxt], prm->skip_w[l],

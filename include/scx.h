@@ -40,6 +40,12 @@ int scx_version(void);
 /* Human-readable name of a status code returned by this library. */
 const char* scx_status_string(int status);
 
+/* Diagnostic without a reference counterpart: the device watchdog word of the current
+ * device (0 = no kernel ever gave up waiting on its own tensor-core pipeline; a positive
+ * code names the wait that timed out), optionally resetting it.  Synchronous; negative
+ * values are -cudaError_t of the read. */
+int scx_watchdog(int reset);
+
 /* Builds (if needed) the twiddle tables for one shape on the current device.
  * Replaces the suFFT plan/work-area warm-up: get_cached_plan / get_workspace
  * (spectral_conv/spectral_conv_ext.cpp:77-121) driven by warmup_spectral_plans

@@ -243,3 +243,54 @@ def test_errors_are_raised_not_faulted(cuda_device):
     y = spectral_conv_ext.spectral_mul(torch.ones(1, 1, 1, 1, 2, device=cuda_device),
                                        torch.ones(1, 1, 1, 1, 2, device=cuda_device))
     assert y.cpu().tolist() == [[[[[0.0, 2.0]]]]]
+
+
+TC_SHAPES = [
+    (1, 3, 5, 64, 64, 12, 12),     # 3 planes at H=64: the last 128-row tile is half empty
+    (3, 2, 2, 128, 64, 32, 24),    # 4*m1 = 128, N1 = 48
+    (2, 5, 3, 128, 128, 7, 3),     # small modes, N1 = 16
+    (1, 2, 2, 64, 64, 16, 16),     # N2 = W
+    (4, 8, 8, 128, 128, 16, 16),
+]
+
+
+@pytest.mark.parametrize("shape", TC_SHAPES)
+def test_tensor_core_shapes_vs_f64_oracle(shape, cuda_device):
+    """Shapes routed to the tcgen05 kernels (H, W in {64, 128}) against the float64 oracle."""
+    B, Cin, Cout, H, W, m1, m2 = shape
+    g = torch.Generator().manual_seed(7 * sum(shape))
+    x = torch.randn(B, Cin, H, W, generator=g)
+    scale = 1.0 / (Cin * Cout)
+    w1 = scale * torch.rand(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g)
+    w2 = scale * torch.rand(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g)
+    y = run_device(x, w1, w2, m1, m2, cuda_device).cpu().numpy()
+    ref = oracle.spectral_conv2d_f64(x.numpy(), w1.numpy(), w2.numpy(), m1, m2)
+    assert_close(ref, y)
+
+
+def test_tensor_core_corners_vs_f64(cuda_device):
+    """The tcgen05 forward alone: corner spectra against the float64 direct DFT."""
+    import spectral_conv_ext
+
+    g = torch.Generator().manual_seed(12)
+    x = torch.randn(3, 4, 64, 64, generator=g)
+    c1, c2 = spectral_conv_ext.rfft2_corners(x.to(cuda_device), 12, 12)
+    r1, r2 = oracle.rfft2_corners_f64(x.numpy(), 12, 12)
+    for got, ref in ((c1, r1), (c2, r2)):
+        got = got.cpu().numpy()
+        got = got[..., 0] + 1j * got[..., 1]
+        assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
+    y = spectral_conv_ext.irfft2_corners(c1, c2, 64, 64).cpu().numpy()
+    full = np.zeros((3, 4, 64, 33), dtype=np.complex128)
+    full[:, :, :12, :12] = r1
+    full[:, :, -12:, :12] = r2
+    ref_y = np.fft.irfft2(full, s=(64, 64))
+    assert np.abs(y - ref_y).max() <= 1e-4 * np.abs(ref_y).max()
+
+
+def test_zz_watchdog_clean(cuda_device):
+    """No tensor-core kernel gave up on a wait during this session."""
+    import _scx
+
+    torch.cuda.synchronize(cuda_device)
+    assert _scx.lib.scx_watchdog(0) == 0

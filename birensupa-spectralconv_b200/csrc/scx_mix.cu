@@ -3,11 +3,12 @@
 //
 //   y_c[b][o][k] = sum_i x_c[b][i][k] * w_c[i][o][k]      c in {1, 2}, k over m1*m2 modes
 //
-// Unlike the reference kernel (one thread per output, weights re-read for every batch
-// item) a thread here keeps one weight in a register and applies it to a block of
-// batch items, and both corners run in one launch on the caller's stream.  Lanes of a
-// warp walk consecutive modes, so every weight and spectrum load is a coalesced 256-byte
-// row of the reference's [.., m1, m2, 2] layout.
+// One CTA owns one corner and a tile of TM consecutive modes for every batch item and
+// output channel.  It stages x_c[:, :, tile] and w_c[:, :, tile] in shared memory with
+// loads of TM contiguous modes (one 32-byte sector at TM = 4) - every weight byte is
+// read once - and then each thread accumulates a 2 (output channels) x 4 (batch items)
+// block of complex outputs per mode from shared memory.  Both corners run in one launch
+// on the caller's stream (the reference launched them serially on the null stream).
 #include <algorithm>
 
 #include "scx_internal.h"
@@ -15,52 +16,76 @@
 namespace scx {
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kBatch = 8;  // batch items per thread
+constexpr int kThreads = 256;
+constexpr int kOT = 2;  // output channels per thread
+constexpr int kBT = 4;  // batch items per thread
 
 struct MixArgs {
     const float2* x[2];
     const float2* w[2];
     float2* y[2];
-    int B, Cin, Cout, NM, nbchunk;
+    int B, Cin, Cout, NM, TM;
 };
 
-// grid = (mode tiles of 32, output-channel tiles of kWarps, ncorner * batch chunks)
-__global__ void __launch_bounds__(kWarps * 32) mix_ffma_kernel(const MixArgs a) {
-    const int corner = blockIdx.z / a.nbchunk;
-    const int b0 = (blockIdx.z - corner * a.nbchunk) * kBatch;
+__global__ void __launch_bounds__(kThreads) mix_smem_kernel(const MixArgs a) {
+    extern __shared__ float2 mix_smem[];
+    const int corner = blockIdx.y;
+    const int TM = a.TM;
+    const int k0 = blockIdx.x * TM;
+    const int tm = min(TM, a.NM - k0);
+    const int B = a.B, Cin = a.Cin, Cout = a.Cout, NM = a.NM;
+    float2* Xs = mix_smem;                                  // [B][Cin][TM]
+    float2* Ws = mix_smem + static_cast<size_t>(B) * Cin * TM;  // [Cin][Cout][TM]
     const float2* __restrict__ X = a.x[corner];
     const float2* __restrict__ Wt = a.w[corner];
     float2* __restrict__ Y = a.y[corner];
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int mode = blockIdx.x * 32 + lane;
-    const int o = blockIdx.y * kWarps + warp;
-    if (mode >= a.NM || o >= a.Cout) return;
-    const int nb = min(kBatch, a.B - b0);
-    const size_t xs_b = static_cast<size_t>(a.Cin) * a.NM;
-    float2 acc[kBatch];
-#pragma unroll
-    for (int j = 0; j < kBatch; ++j) acc[j] = make_float2(0.f, 0.f);
-    const float2* xp = X + static_cast<size_t>(b0) * xs_b + mode;
-    const float2* wp = Wt + static_cast<size_t>(o) * a.NM + mode;
-    const size_t ws_i = static_cast<size_t>(a.Cout) * a.NM;
-    for (int i = 0; i < a.Cin; ++i) {
-        const float2 wv = __ldg(wp + i * ws_i);
-#pragma unroll
-        for (int j = 0; j < kBatch; ++j) {
-            if (j < nb) {
-                const float2 xv = __ldg(xp + j * xs_b + static_cast<size_t>(i) * a.NM);
-                acc[j].x = fmaf(xv.x, wv.x, fmaf(-xv.y, wv.y, acc[j].x));
-                acc[j].y = fmaf(xv.x, wv.y, fmaf(xv.y, wv.x, acc[j].y));
-            }
-        }
+
+    for (int idx = threadIdx.x; idx < B * Cin * tm; idx += kThreads) {
+        const int row = idx / tm, kk = idx - row * tm;
+        Xs[row * TM + kk] = __ldg(X + static_cast<size_t>(row) * NM + k0 + kk);
     }
-    float2* yp = Y + (static_cast<size_t>(b0) * a.Cout + o) * a.NM + mode;
-    const size_t ys_b = static_cast<size_t>(a.Cout) * a.NM;
+    for (int idx = threadIdx.x; idx < Cin * Cout * tm; idx += kThreads) {
+        const int row = idx / tm, kk = idx - row * tm;
+        Ws[row * TM + kk] = __ldg(Wt + static_cast<size_t>(row) * NM + k0 + kk);
+    }
+    __syncthreads();
+
+    const int nog = (Cout + kOT - 1) / kOT;
+    const int nbg = (B + kBT - 1) / kBT;
+    const int ntiles = tm * nog * nbg;
+    for (int t = threadIdx.x; t < ntiles; t += kThreads) {
+        const int kk = t % tm;
+        const int rest = t / tm;
+        const int og = rest % nog, bg = rest / nog;
+        const int o0 = og * kOT, b0 = bg * kBT;
+        float2 acc[kOT][kBT];
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j)
-        if (j < nb) yp[j * ys_b] = acc[j];
+        for (int p = 0; p < kOT; ++p)
+#pragma unroll
+            for (int q = 0; q < kBT; ++q) acc[p][q] = make_float2(0.f, 0.f);
+        for (int i = 0; i < Cin; ++i) {
+            float2 wv[kOT], xv[kBT];
+#pragma unroll
+            for (int p = 0; p < kOT; ++p)
+                wv[p] = (o0 + p < Cout) ? Ws[(i * Cout + o0 + p) * TM + kk] : make_float2(0.f, 0.f);
+#pragma unroll
+            for (int q = 0; q < kBT; ++q)
+                xv[q] = (b0 + q < B) ? Xs[((b0 + q) * Cin + i) * TM + kk] : make_float2(0.f, 0.f);
+#pragma unroll
+            for (int p = 0; p < kOT; ++p)
+#pragma unroll
+                for (int q = 0; q < kBT; ++q) {
+                    acc[p][q].x = fmaf(xv[q].x, wv[p].x, fmaf(-xv[q].y, wv[p].y, acc[p][q].x));
+                    acc[p][q].y = fmaf(xv[q].x, wv[p].y, fmaf(xv[q].y, wv[p].x, acc[p][q].y));
+                }
+        }
+#pragma unroll
+        for (int p = 0; p < kOT; ++p)
+#pragma unroll
+            for (int q = 0; q < kBT; ++q)
+                if (o0 + p < Cout && b0 + q < B)
+                    Y[(static_cast<size_t>(b0 + q) * Cout + o0 + p) * NM + k0 + kk] = acc[p][q];
+    }
 }
 
 }  // namespace
@@ -79,12 +104,25 @@ cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, con
     a.Cin = Cin;
     a.Cout = Cout;
     a.NM = NM;
-    a.nbchunk = (B + kBatch - 1) / kBatch;
-    const long long gz = static_cast<long long>(ncorner) * a.nbchunk;
-    const long long gy = (Cout + kWarps - 1) / kWarps;
-    if (gz > 65535 || gy > 65535) return cudaErrorInvalidValue;
-    const dim3 grid((NM + 31) / 32, static_cast<unsigned>(gy), static_cast<unsigned>(gz));
-    mix_ffma_kernel<<<grid, kWarps * 32, 0, stream>>>(a);
+    // Largest mode tile (4, 2 or 1) whose staging fits 96 KB and still gives >= 2 CTAs per SM.
+    const size_t per_mode = (static_cast<size_t>(B) * Cin + static_cast<size_t>(Cin) * Cout) * sizeof(float2);
+    const long long want = 2LL * num_sms();
+    int TM = 1;
+    for (int t : {4, 2}) {
+        const long long ctas = static_cast<long long>(ncorner) * ((NM + t - 1) / t);
+        if (per_mode * t <= 96 * 1024 && ctas >= want) {
+            TM = t;
+            break;
+        }
+    }
+    const size_t smem = per_mode * TM;
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;  // B*Cin + Cin*Cout too large for one mode
+    a.TM = TM;
+    int per_sm = 1;
+    cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(mix_smem_kernel), smem, kThreads, &per_sm);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((NM + TM - 1) / TM, ncorner);
+    mix_smem_kernel<<<grid, kThreads, smem, stream>>>(a);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,504 @@
+// Tensor-core (tcgen05, bf16x3 -> fp32) truncated forward real DFT, column transform first:
+// the B200 replacement for the suFFT R2C + corner gather of spectral_conv2d_supa
+// (spectral_conv/spectral_conv_ops.py:372-399, spectral_conv/spectral_conv_ext.cpp:123-178).
+//
+// For every plane x[h][w] (H, W in {64, 128}) and corner slots s < 2*m1 <= 32 (row
+// kx_s = s for corner 1, H - 2*m1 + s for corner 2), ky < m2 <= 32:
+//
+//   S2  column DFT on the tensor core, A = x^T straight from TMEM:
+//         D2[(g,w)][j] = sum_h x_g[h][w] * F[j][h]       lanes (g,w): G1 = 128/W planes
+//       F rows j = 32*grp + 16*cs + i hold cos (cs = 0) / sin (cs = 1) of 2 pi kx_s h / H
+//       for slot s = 16*grp + i.  Each plane is read once from HBM by the TMA engine, each
+//       thread reads its column (lane = w) from shared memory, splits it into bf16 hi/lo
+//       in registers and writes the pairs to TMEM with tcgen05.st.
+//   E2  D2 rows -> C/S operand in shared memory (MN-major: each thread writes the 64
+//       values of its column as 16-byte vectors), rows m = 64*plane + j, K = w
+//   S1  row DFT:   D1[m][n] = sum_w CS[m][w] * TW[n][w]   (M = 128 = 2 planes)
+//       TW rows n < R2: cos(2 pi n w / W), rows R2 + n: -sin(2 pi n w / W)
+//   E1  X[s][ky] = (Cc + Ss) + i (Cs - Sc) from the cos row (lane i) and the sin row
+//       (lane i + 16) of slot s, exchanged with one shuffle; written to the corner arrays.
+//
+// Every product is bf16x3 (hi*hi + hi*lo + lo*hi) accumulated in fp32 TMEM: S2 issues
+// MMA(x_hi, [F_hi; F_lo]) + MMA(x_lo, F_hi) per K step and S1 the same with CS and TW.
+//
+// Warp roles (persistent, one CTA per SM, planes split into contiguous balanced ranges):
+//   warp 17      lane 0 streams 32-row chunks of x into a shared-memory ring with 1-D bulk
+//                copies (about 100 KB in flight per SM, which is what HBM needs here)
+//   warps 0..7   converters: ring -> bf16 hi/lo -> the TMEM A operand, whose two K halves
+//                are refilled independently
+//   warps 8..15  epilogue: E2 for every column tile (D2 double-buffered in TMEM), E1 for
+//                every 2-plane tile
+//   warp 16      lane 0 issues every MMA
+// All hand-offs are mbarriers; every wait is bounded (about a second): a role that gives up
+// stores a code in the device watchdog word and leaves its loop, so the kernel returns.
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "scx_internal.h"
+#include "scx_tc.cuh"
+#include "scx_tc_host.h"
+
+namespace scx {
+namespace {
+
+constexpr int kConvWarps = 8;                      // 2 per TMEM sub-partition
+constexpr int kEpiWarps = 8;                       // 2 per TMEM sub-partition
+constexpr int kMmaWarp = kConvWarps + kEpiWarps;   // 16
+constexpr int kTmaWarp = kMmaWarp + 1;             // 17
+constexpr int kThreads = (kTmaWarp + 1) * 32;      // 576
+constexpr int kBarEpi = 1;                         // named barrier of the epilogue warps
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kJF = 64;                            // column-DFT rows per plane (2 groups x 32)
+constexpr int kFRows = 2 * kJF;                    // [F_hi; F_lo]
+constexpr int kChunkRows = 32;                     // rows of x per ring slot
+constexpr int kMaxSlots = 8;
+
+struct FwdArgs {
+    const float* x;
+    float2* out1;
+    float2* out2;
+    long long ops;  // output plane stride (float2 units)
+    int ors;        // output row stride (float2 units)
+    int P, m1, m2;
+    const uint4* tab;  // [F_hi; F_lo] then [TW_hi; TW_lo], both K-major SW128
+    uint32_t tab_bytes;
+    int* watchdog;
+};
+
+struct FwdBars {
+    uint64_t full[kMaxSlots], empty[kMaxSlots];  // x ring
+    uint64_t aFull[2], aEmpty[2];                // per K half of the A operand
+    uint64_t d2Full[2], d2Empty[2], csFull, csEmpty, d1Full, d1Empty, drain;
+};
+
+template <int H, int W, int R2>
+struct FwdCfg {
+    static constexpr int G1 = 128 / W;  // planes per column tile (TMEM lanes = (plane, w))
+    static constexpr int CT = 2 / G1;   // column tiles per 2-plane tile
+    static constexpr int N1 = 2 * R2;   // S1 columns per TW part (cos block | -sin block)
+    static constexpr int CPC = H / kChunkRows;  // ring chunks per column tile
+    static constexpr int CPH = CPC / 2;         // ring chunks per K half
+    static constexpr uint32_t PLANE_CHUNK = static_cast<uint32_t>(kChunkRows) * W * 4u;
+    static constexpr uint32_t SLOT = PLANE_CHUNK * G1;  // 16 KB
+    static constexpr uint32_t CSB = 128u * W * 2u;      // one CS operand (hi or lo), MN-major
+    static constexpr uint32_t OFF_FB = 2u * CSB;        // CS hi | CS lo
+    static constexpr uint32_t FB_BYTES = static_cast<uint32_t>(kFRows) * H * 2u;
+    static constexpr uint32_t OFF_TW = OFF_FB + FB_BYTES;
+    static constexpr uint32_t TW_BYTES = 2u * N1 * W * 2u;
+    static constexpr uint32_t OFF_RING = OFF_TW + TW_BYTES;
+    static constexpr uint32_t BUDGET = 227u * 1024u - 1024u - 512u;  // minus alignment slack and static smem
+    static constexpr int NS = static_cast<int>((BUDGET - OFF_RING) / SLOT) < kMaxSlots
+                                  ? static_cast<int>((BUDGET - OFF_RING) / SLOT)
+                                  : kMaxSlots;
+    static constexpr uint32_t SMEM = OFF_RING + static_cast<uint32_t>(NS) * SLOT + 1024u;
+    static_assert(NS >= 3, "x ring too small");
+    // TMEM columns: A (hi: H/2 packed columns | lo: H/2) | D2 x 2 (2*kJF each) | D1 (2*N1)
+    static constexpr uint32_t COL_D2 = static_cast<uint32_t>(H);
+    static constexpr uint32_t COL_D1 = COL_D2 + 4u * kJF;
+    static constexpr uint32_t COLS = COL_D1 + 2u * N1;
+    static constexpr uint32_t TMEM_COLS = COLS <= 256 ? 256u : 512u;
+    static_assert(COLS <= 512, "TMEM budget");
+};
+
+template <int H, int W, int R2>
+__global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a) {
+    using C = FwdCfg<H, W, R2>;
+    constexpr int N1 = C::N1;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ FwdBars bars;
+    __shared__ uint32_t tmem_base;
+    uint8_t* base = tc::align1024(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // this CTA's planes [p0, p1): contiguous, sizes differ by at most one
+    const int P = a.P;
+    const int p0 = static_cast<int>(static_cast<long long>(blockIdx.x) * P / gridDim.x);
+    const int p1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * P / gridDim.x);
+    const int NC = (p1 - p0 + C::G1 - 1) / C::G1;  // column tiles
+    const int NT = (NC + C::CT - 1) / C::CT;        // 2-plane tiles
+
+    tc::copy_table(base + C::OFF_FB, a.tab, a.tab_bytes);
+    if (warp == 0) {
+        tc::tmem_alloc(&tmem_base, C::TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int i = 0; i < kMaxSlots; ++i) {
+            tc::mbar_init(&bars.full[i], 1);
+            tc::mbar_init(&bars.empty[i], kConvWarps);
+        }
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&bars.aFull[i], kConvWarps);
+            tc::mbar_init(&bars.aEmpty[i], 1);
+            tc::mbar_init(&bars.d2Full[i], 1);
+            tc::mbar_init(&bars.d2Empty[i], 1);
+        }
+        tc::mbar_init(&bars.csFull, 1);
+        tc::mbar_init(&bars.csEmpty, 1);
+        tc::mbar_init(&bars.d1Full, 1);
+        tc::mbar_init(&bars.d1Empty, 1);
+        tc::mbar_init(&bars.drain, 1);
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_base;
+
+    if (warp < kConvWarps) {
+        // ------------------------------------------------------------ converters
+        // Warp (q, hf) owns TMEM lanes 32q.. and rows [16 hf, 16 hf + 16) of every ring chunk:
+        // it reads its column of those rows from shared memory, splits them into bf16 hi/lo
+        // pairs and stores 8 packed columns of each into the A operand.
+        const int q = warp & 3, hf = warp >> 2;
+        const int l = q * 32 + lane, g = l / W, w = l % W;
+        const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+        const uint8_t* ring = base + C::OFF_RING;
+        const int NK = NC * C::CPC;
+        bool ok = true;
+        for (int k = 0; k < NK && ok; ++k) {
+            const int c = k / C::CPC, ch = k % C::CPC, half = ch / C::CPH;
+            const int slot = k % C::NS, use = k / C::NS;
+            // A column tile is written only after every MMA of the previous one has completed
+            // (both K halves).  Refilling K half 0 while the MMAs of half 1, with the row DFT
+            // of the previous tile queued behind them, were still running corrupted about 1%
+            // of the planes on B200, although the MMAs of half 0 had completed.
+            if (ch == 0)
+                ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.aEmpty[0], (c & 1) ^ 1) &&
+                                                 tc::mbar_wait_bounded(&bars.aEmpty[1], (c & 1) ^ 1));
+            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.full[slot], use & 1));
+            if (!ok) break;
+            tc::fence_after_sync();  // the TMEM stores below stay behind the aEmpty wait
+            const bool live = p0 + c * C::G1 + g < p1;  // warp-uniform
+            const float* src = reinterpret_cast<const float*>(ring + static_cast<uint32_t>(slot) * C::SLOT +
+                                                              static_cast<uint32_t>(g) * C::PLANE_CHUNK) +
+                               (16 * hf) * W + w;
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = live ? src[j * W] : 0.f;
+            uint32_t hi[8], lo[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tc::split_pair(v[2 * j], v[2 * j + 1], hi[j], lo[j]);
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars.empty[slot]);
+            const uint32_t col = tmem + lane_addr + static_cast<uint32_t>((ch * kChunkRows + 16 * hf) / 2);
+            tc::tmem_st8(col, hi);
+            tc::tmem_st8(col + H / 2, lo);
+            if (ch % C::CPH == C::CPH - 1) {
+                tc::tmem_wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&bars.aFull[half]);
+            }
+        }
+        if (!ok && lane == 0) atomicExch(a.watchdog, 20);
+    } else if (warp < kMmaWarp) {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3, sub = (warp - kConvWarps) >> 2;  // sub-partition, column half
+        const int etid = tid - kConvWarps * 32;                   // 0..255
+        const int l = q * 32 + lane;
+        const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+        const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
+
+        // E2: D2 of column tile c -> CS operand rows of its planes (this warp: j in [32 sub, 32 sub + 32))
+        auto e2 = [&](int c) -> bool {
+            const int i = c / C::CT, ct = c % C::CT, b = c & 1;
+            bool ok = tc::mbar_wait_bounded(&bars.d2Full[b], (c >> 1) & 1);
+            if (ok && ct == 0) ok = tc::mbar_wait_bounded(&bars.csEmpty, (i & 1) ^ 1);
+            if (tc::named_any(kBarEpi, kEpiThreads, !ok)) return false;
+            tc::fence_after_sync();
+            const int g = l / W, w = l % W;
+            const int pit = ct * C::G1 + g;  // plane within the tile
+            uint8_t* cs_hi = base;
+            uint8_t* cs_lo = cs_hi + C::CSB;
+            const uint32_t row_off = static_cast<uint32_t>(w >> 3) * 2048u + static_cast<uint32_t>(pit) * 1024u +
+                                     static_cast<uint32_t>(w & 7) * 128u;
+            const uint32_t d2 = tmem + lane_addr + C::COL_D2 + static_cast<uint32_t>(b) * (2u * kJF) + 32u * sub;
+            float v[32], u[32];
+            tc::tmem_ld32_nowait(d2, v);
+            tc::tmem_ld32_nowait(d2 + kJF, u);
+            tc::tmem_wait_ld();
+            tc::fence_before_sync();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] += u[k];
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+                uint4 h4, l4;
+                tc::split8(v + 8 * c8, h4, l4);
+                const uint32_t off = row_off + (static_cast<uint32_t>((sub * 4 + c8) ^ (w & 7)) << 4);
+                *reinterpret_cast<uint4*>(cs_hi + off) = h4;
+                *reinterpret_cast<uint4*>(cs_lo + off) = l4;
+            }
+            tc::fence_async_smem();
+            tc::named_sync(kBarEpi, kEpiThreads);
+            if (etid == 0) {
+                tc::mbar_arrive(&bars.d2Empty[b]);
+                if (ct == C::CT - 1 || c == NC - 1) tc::mbar_arrive(&bars.csFull);
+            }
+            return true;
+        };
+
+        // E1: D1 of tile i -> corner spectra.  Lane l holds CS row l: plane l / 64, slot
+        // group (l / 32) % 2, cos (lanes 0..15) or sin (lanes 16..31) row of slot 16*group + lane%16.
+        // Warp set `sub` finishes ky in [sub*QR, sub*QR + QR): the cos lane the first HQ of
+        // them, the sin lane the rest, after one exchange of partial sums.
+        auto e1 = [&](int i) -> bool {
+            constexpr int QR = R2 / 2, HQ = QR / 2;
+            const bool ok = tc::mbar_wait_bounded(&bars.d1Full, i & 1);
+            if (tc::named_any(kBarEpi, kEpiThreads, !ok)) return false;
+            tc::fence_after_sync();
+            const uint32_t d1 = tmem + lane_addr + C::COL_D1 + static_cast<uint32_t>(sub * QR);
+            float ch[QR], cl[QR], sh[QR], sl[QR];
+            tc::tmem_ld_cols_nowait<QR>(d1, ch);
+            tc::tmem_ld_cols_nowait<QR>(d1 + N1, cl);
+            tc::tmem_ld_cols_nowait<QR>(d1 + R2, sh);
+            tc::tmem_ld_cols_nowait<QR>(d1 + N1 + R2, sl);
+            tc::tmem_wait_ld();
+            tc::fence_before_sync();
+            const int pit = l >> 6, grp = (l >> 5) & 1, cs = lane >> 4, si = lane & 15;
+            const int s = 16 * grp + si;
+            const int p = p0 + 2 * i + pit;
+            const bool valid = s < S && p < p1;
+            float2* dst = nullptr;
+            if (valid)
+                dst = (s < m1 ? a.out1 + static_cast<long long>(p) * a.ops + static_cast<long long>(s) * a.ors
+                              : a.out2 + static_cast<long long>(p) * a.ops + static_cast<long long>(s - m1) * a.ors);
+#pragma unroll
+            for (int k = 0; k < HQ; ++k) {
+                const float uc0 = ch[k] + cl[k], us0 = sh[k] + sl[k];
+                const float uc1 = ch[HQ + k] + cl[HQ + k], us1 = sh[HQ + k] + sl[HQ + k];
+                const float ra = __shfl_xor_sync(0xffffffffu, cs ? uc0 : uc1, 16);
+                const float rb = __shfl_xor_sync(0xffffffffu, cs ? us0 : us1, 16);
+                const float Cc = cs ? ra : uc0, Cs = cs ? rb : us0;
+                const float Sc = cs ? uc1 : ra, Ss = cs ? us1 : rb;
+                const int ky = sub * QR + (cs ? HQ + k : k);
+                if (valid && ky < m2) dst[ky] = make_float2(Cc + Ss, Cs - Sc);
+            }
+            tc::named_sync(kBarEpi, kEpiThreads);
+            if (etid == 0) tc::mbar_arrive(&bars.d1Empty);
+            return true;
+        };
+
+        bool ok = true;
+        for (int c = 0; c < NC && ok; ++c) {
+            const int i = c / C::CT, ct = c % C::CT;
+            ok = e2(c);
+            if (ok && ct == 0 && i > 0) ok = e1(i - 1);
+        }
+        if (ok && NT > 0) ok = e1(NT - 1);
+        if (!ok && etid == 0) atomicExch(a.watchdog, 21);
+    } else if (warp == kMmaWarp && lane == 0) {
+        // ------------------------------------------------------------ MMA issuer
+        const uint32_t sb = tc::smem_u32(base);
+        const uint64_t dFB = tc::desc_sw128(sb + C::OFF_FB);
+        const uint64_t dTW = tc::desc_sw128(sb + C::OFF_TW);
+        const uint64_t dCShi = tc::desc_mn_sw128(sb, 1024u, 2048u);
+        const uint64_t dCSlo = tc::desc_mn_sw128(sb + C::CSB, 1024u, 2048u);
+        constexpr uint32_t idA = tc::idesc_bf16(128, 2 * kJF), idB = tc::idesc_bf16(128, kJF);
+        constexpr uint32_t idC = tc::idesc_bf16(128, 2 * N1) | tc::kIdescAMajorMN;
+        constexpr uint32_t idD = tc::idesc_bf16(128, N1) | tc::kIdescAMajorMN;
+        constexpr int KH = H / 32;  // K steps per A half
+        const uint32_t d1 = tmem + C::COL_D1;
+
+        auto s1 = [&](int i) -> bool {
+            if (!tc::mbar_wait_bounded(&bars.csFull, i & 1)) return false;
+            if (!tc::mbar_wait_bounded(&bars.d1Empty, (i & 1) ^ 1)) return false;
+            tc::fence_after_sync();
+#pragma unroll
+            for (int ks = 0; ks < W / 16; ++ks) {
+                const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4;
+                const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * (2u * N1) * 128u + (ks & 3) * 32u) >> 4;
+                tc::mma_bf16(d1, dCShi + ao, dTW + bo, idC, ks > 0 ? 1u : 0u);
+                tc::mma_bf16(d1, dCSlo + ao, dTW + bo, idD, 1u);
+            }
+            tc::mma_commit(&bars.csEmpty);
+            tc::mma_commit(&bars.d1Full);
+            return true;
+        };
+
+        bool ok = true;
+        for (int c = 0; c < NC && ok; ++c) {
+            const int i = c / C::CT, ct = c % C::CT, b = c & 1;
+            const uint32_t d2 = tmem + C::COL_D2 + static_cast<uint32_t>(b) * (2u * kJF);
+            ok = tc::mbar_wait_bounded(&bars.d2Empty[b], ((c >> 1) & 1) ^ 1);
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                if (ok) ok = tc::mbar_wait_bounded(&bars.aFull[hf], c & 1);
+                if (!ok) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int kk = 0; kk < KH; ++kk) {
+                    const int ks = hf * KH + kk;
+                    const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * kFRows * 128u + (ks & 3) * 32u) >> 4;
+                    tc::mma_ts(d2, tmem + 8u * ks, dFB + bo, idA, ks > 0 ? 1u : 0u);
+                    tc::mma_ts(d2, tmem + H / 2 + 8u * ks, dFB + bo, idB, 1u);
+                }
+                tc::mma_commit(&bars.aEmpty[hf]);
+            }
+            if (!ok) break;
+            tc::mma_commit(&bars.d2Full[b]);
+            if (ct == 0 && i > 0) ok = s1(i - 1);
+        }
+        if (ok && NT > 0) ok = s1(NT - 1);
+        if (!ok) atomicExch(a.watchdog, 22);
+        // every MMA issued above has completed before TMEM is released
+        tc::mma_commit(&bars.drain);
+        tc::mbar_wait_bounded(&bars.drain, 0);
+    } else if (warp == kTmaWarp && lane == 0) {
+        // ------------------------------------------------------------ TMA producer
+        // 1-D bulk copies of 32-row chunks of each live plane of a column tile into the ring.
+        uint8_t* ring = base + C::OFF_RING;
+        const int NK = NC * C::CPC;
+        for (int k = 0; k < NK; ++k) {
+            const int c = k / C::CPC, ch = k % C::CPC;
+            const int slot = k % C::NS, use = k / C::NS;
+            if (!tc::mbar_wait_bounded(&bars.empty[slot], (use & 1) ^ 1)) {
+                atomicExch(a.watchdog, 23);
+                break;
+            }
+            const int pa = p0 + c * C::G1, np = min(C::G1, p1 - pa);
+            tc::mbar_arrive_expect_tx(&bars.full[slot], static_cast<uint32_t>(np) * C::PLANE_CHUNK);
+            for (int g = 0; g < np; ++g)
+                tc::bulk_g2s(ring + static_cast<uint32_t>(slot) * C::SLOT + static_cast<uint32_t>(g) * C::PLANE_CHUNK,
+                             a.x + (static_cast<size_t>(pa + g) * H + ch * kChunkRows) * W, C::PLANE_CHUNK,
+                             &bars.full[slot]);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+struct FwdTable {
+    const uint4* data;
+    uint32_t bytes;
+};
+
+std::mutex g_mutex;
+std::map<std::tuple<int, int, int, int, int>, FwdTable> g_tables;
+
+// [F_hi; F_lo] (kFRows x H) followed by [TW_hi; TW_lo] (2*N1 x W), K-major SW128 bf16.
+cudaError_t get_fwd_table(int H, int W, int m1, int m2, const FwdTable** out) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    const auto key = std::make_tuple(dev, H, W, m1, m2);
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_tables.find(key);
+    if (it != g_tables.end()) {
+        *out = &it->second;
+        return cudaSuccess;
+    }
+    const int R2 = host::round_up(m2, 8), N1 = 2 * R2, S = 2 * m1;
+    host::KMajor fb(kFRows, H);
+    for (int j = 0; j < kJF; ++j) {
+        const int grp = j / 32, cs = (j / 16) & 1, s = 16 * grp + (j & 15);
+        if (s >= S) continue;
+        const int kx = host::slot_row(s, H, m1);
+        for (int h = 0; h < H; ++h) {
+            const double t = host::ang(kx, h, H);
+            uint16_t hi, lo;
+            host::bf16_split(cs ? std::sin(t) : std::cos(t), hi, lo);
+            fb.set(j, h, hi);
+            fb.set(kJF + j, h, lo);
+        }
+    }
+    host::KMajor tw(2 * N1, W);
+    for (int n = 0; n < m2; ++n)
+        for (int w = 0; w < W; ++w) {
+            const double t = host::ang(n, w, W);
+            uint16_t hi, lo;
+            host::bf16_split(std::cos(t), hi, lo);
+            tw.set(n, w, hi);
+            tw.set(N1 + n, w, lo);
+            host::bf16_split(-std::sin(t), hi, lo);
+            tw.set(R2 + n, w, hi);
+            tw.set(N1 + R2 + n, w, lo);
+        }
+    std::vector<uint16_t> host_buf(fb.data);
+    host_buf.insert(host_buf.end(), tw.data.begin(), tw.data.end());
+    const size_t bytes = host_buf.size() * 2;
+    void* d = nullptr;
+    err = cudaMalloc(&d, bytes);
+    if (err != cudaSuccess) return err;
+    err = cudaMemcpy(d, host_buf.data(), bytes, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        cudaFree(d);
+        return err;
+    }
+    FwdTable t;
+    t.data = static_cast<const uint4*>(d);
+    t.bytes = static_cast<uint32_t>(bytes);
+    auto res = g_tables.emplace(key, t);
+    *out = &res.first->second;
+    return cudaSuccess;
+}
+
+template <int H, int W, int R2>
+cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
+    using C = FwdCfg<H, W, R2>;
+    static_assert(C::SMEM <= 227u * 1024u - 512u, "shared memory budget");
+    auto kernel = dft_fwd_tc_kernel<H, W, R2>;
+    int per_sm = 1;
+    cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), C::SMEM, kThreads, &per_sm);
+    if (err != cudaSuccess) return err;
+    const int grid = std::max(1, std::min(a.P, num_sms()));
+    kernel<<<grid, kThreads, C::SMEM, stream>>>(a);
+    return cudaGetLastError();
+}
+
+template <int H, int W>
+cudaError_t run_fwd_r2(const FwdArgs& a, int R2, cudaStream_t stream) {
+    switch (R2) {
+        case 8: return run_fwd<H, W, 8>(a, stream);
+        case 16: return run_fwd<H, W, 16>(a, stream);
+        case 24: return run_fwd<H, W, 24>(a, stream);
+        case 32: return run_fwd<H, W, 32>(a, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+bool tc_fwd_supported(int H, int W, int m1, int m2) {
+    return (H == 64 || H == 128) && (W == 64 || W == 128) && m1 >= 1 && 2 * m1 <= 32 && m2 >= 1 && m2 <= 32 &&
+           m1 <= H && m2 <= W / 2 + 1;
+}
+
+cudaError_t launch_dft_fwd_tc(const float* x, float2* out1, float2* out2, long long ops, int ors, int P, int H,
+                              int W, int m1, int m2, cudaStream_t stream) {
+    if (!tc_fwd_supported(H, W, m1, m2) || P <= 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+        return cudaErrorInvalidValue;
+    const FwdTable* t = nullptr;
+    cudaError_t e = get_fwd_table(H, W, m1, m2, &t);
+    if (e != cudaSuccess) return e;
+    int* wd = nullptr;
+    e = device_watchdog(&wd);
+    if (e != cudaSuccess) return e;
+    FwdArgs a;
+    a.x = x;
+    a.out1 = out1;
+    a.out2 = out2;
+    a.ops = ops;
+    a.ors = ors;
+    a.P = P;
+    a.m1 = m1;
+    a.m2 = m2;
+    a.tab = t->data;
+    a.tab_bytes = t->bytes;
+    a.watchdog = wd;
+    const int R2 = host::round_up(m2, 8);
+    if (H == 64 && W == 64) return run_fwd_r2<64, 64>(a, R2, stream);
+    if (H == 64 && W == 128) return run_fwd_r2<64, 128>(a, R2, stream);
+    if (H == 128 && W == 64) return run_fwd_r2<128, 64>(a, R2, stream);
+    return run_fwd_r2<128, 128>(a, R2, stream);
+}
+
+}  // namespace scx

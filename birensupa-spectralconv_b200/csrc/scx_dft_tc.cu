@@ -33,8 +33,6 @@
 
 namespace scx {
 
-__device__ int g_watchdog = 0;
-
 namespace {
 
 constexpr int kTcThreads = 256;
@@ -78,6 +76,7 @@ inline int round_up(int v, int m) { return (v + m - 1) / m * m; }
 struct TcShape {
     int H, W, m1, m2;
     int R2, N1, np, N2, Kg;  // re block, 2*R2, planes per tile, np*N1, 4*m1 rounded to 16
+    int MF;                  // rows of the forward column-DFT operand: 64 if 4*m1 <= 64, else 128
 };
 
 TcShape tc_shape(int H, int W, int m1, int m2) {
@@ -91,15 +90,21 @@ TcShape tc_shape(int H, int W, int m1, int m2) {
     s.np = 128 / H;
     s.N2 = s.np * s.N1;
     s.Kg = round_up(4 * m1, 16);
+    s.MF = (4 * m1 <= 64) ? 64 : 128;
     return s;
 }
 
+constexpr size_t kMaxDynSmem = 227 * 1024 - 256;  // minus the kernel's static shared memory
+size_t inv_smem_bytes(const TcShape& s) {
+    const int kgp = round_up(s.Kg, 64);
+    return static_cast<size_t>(128) * kgp * 4 + static_cast<size_t>(s.W) * 64 * 4 +
+           static_cast<size_t>(s.N2) * kgp * 4 + static_cast<size_t>(s.np) * 128 * 128 * 2 * 2 + 1024;
+}
+
 struct TcTables {
-    const uint4* fwd_tw;
-    const uint4* fwd_f;
     const uint4* inv_g;
     const uint4* inv_e;
-    uint32_t tw_bytes, f_bytes, g_bytes, e_bytes;
+    uint32_t g_bytes, e_bytes;
 };
 
 std::mutex g_tc_mutex;
@@ -117,20 +122,6 @@ cudaError_t get_tc_tables(const TcShape& s, const TcTables** out) {
         return cudaSuccess;
     }
     const int H = s.H, W = s.W, m1 = s.m1, m2 = s.m2;
-    Operand tw(s.N1, W);  // S1 B operand
-    for (int n = 0; n < m2; ++n)
-        for (int w = 0; w < W; ++w) {
-            tw.put(n, w, std::cos(ang(n, w, W)));
-            tw.put(s.R2 + n, w, -std::sin(ang(n, w, W)));
-        }
-    Operand f(128, H);  // S2 A operand
-    for (int j = 0; j < 2 * m1; ++j) {
-        const int kx = slot_row(j, H, m1);
-        for (int h = 0; h < H; ++h) {
-            f.put(j, h, std::cos(ang(kx, h, H)));
-            f.put(2 * m1 + j, h, std::sin(ang(kx, h, H)));
-        }
-    }
     Operand g(128, round_up(s.Kg, 64));  // S4 A operand
     for (int h = 0; h < H; ++h)
         for (int j = 0; j < 2 * m1; ++j) {
@@ -149,18 +140,19 @@ cudaError_t get_tc_tables(const TcShape& s, const TcTables** out) {
             e.put(w, s.R2 + ky, -c * std::sin(ang(ky, w, W)));
         }
     }
-    const size_t total = tw.bytes() + f.bytes() + g.bytes() + e.bytes();
+    const size_t total = g.bytes() + e.bytes();
     uint8_t* dbuf = nullptr;
     err = cudaMalloc(&dbuf, total);
     if (err != cudaSuccess) return err;
     std::vector<uint8_t> host(total);
     size_t off = 0;
-    const Operand* ops[4] = {&tw, &f, &g, &e};
-    size_t offs[4];
-    for (int i = 0; i < 4; ++i) {
+    const void* srcs[2] = {g.data.data(), e.data.data()};
+    const size_t sizes[2] = {g.bytes(), e.bytes()};
+    size_t offs[2];
+    for (int i = 0; i < 2; ++i) {
         offs[i] = off;
-        std::memcpy(host.data() + off, ops[i]->data.data(), ops[i]->bytes());
-        off += ops[i]->bytes();
+        std::memcpy(host.data() + off, srcs[i], sizes[i]);
+        off += sizes[i];
     }
     err = cudaMemcpy(dbuf, host.data(), total, cudaMemcpyHostToDevice);
     if (err != cudaSuccess) {
@@ -168,12 +160,8 @@ cudaError_t get_tc_tables(const TcShape& s, const TcTables** out) {
         return err;
     }
     TcTables t;
-    t.fwd_tw = reinterpret_cast<const uint4*>(dbuf + offs[0]);
-    t.fwd_f = reinterpret_cast<const uint4*>(dbuf + offs[1]);
-    t.inv_g = reinterpret_cast<const uint4*>(dbuf + offs[2]);
-    t.inv_e = reinterpret_cast<const uint4*>(dbuf + offs[3]);
-    t.tw_bytes = static_cast<uint32_t>(tw.bytes());
-    t.f_bytes = static_cast<uint32_t>(f.bytes());
+    t.inv_g = reinterpret_cast<const uint4*>(dbuf + offs[0]);
+    t.inv_e = reinterpret_cast<const uint4*>(dbuf + offs[1]);
     t.g_bytes = static_cast<uint32_t>(g.bytes());
     t.e_bytes = static_cast<uint32_t>(e.bytes());
     auto res = g_tc_cache.emplace(key, t);
@@ -189,23 +177,13 @@ inline uint32_t tmem_cols_for(int n) {
 
 // ------------------------------------------------------------------ device helpers
 
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-    const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023);
-    return reinterpret_cast<uint8_t*>(a);
-}
-
-__device__ __forceinline__ void copy_table(uint8_t* dst, const uint4* src, uint32_t bytes) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
-    for (uint32_t i = threadIdx.x; i < bytes / 16; i += blockDim.x) d[i] = __ldg(src + i);
-}
-
 // all threads: bounded wait, then agree on success
-__device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t& phase, int* abort_flag, int code) {
+__device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t& phase, int* abort_flag, int* watchdog, int code) {
     const bool ok = tc::mbar_wait_bounded(bar, phase);
     phase ^= 1u;
     if (!ok) {
         *abort_flag = 1;
-        atomicExch(&g_watchdog, code);
+        atomicExch(watchdog, code);
     }
     __syncthreads();
     return *abort_flag == 0;
@@ -217,176 +195,6 @@ __device__ __forceinline__ void mma3(uint32_t d, uint32_t a_hi, uint32_t a_lo, u
     tc::mma_bf16(d, tc::desc_sw128(a_hi), tc::desc_sw128(b_hi), idesc, first ? 0u : 1u);
     tc::mma_bf16(d, tc::desc_sw128(a_hi), tc::desc_sw128(b_lo), idesc, 1u);
     tc::mma_bf16(d, tc::desc_sw128(a_lo), tc::desc_sw128(b_hi), idesc, 1u);
-}
-
-// ------------------------------------------------------------------ forward
-
-struct FwdTcArgs {
-    const float* x;
-    float2* out1;
-    float2* out2;
-    long long ops;
-    int ors;
-    int P, H, W, m1, m2, R2, N1, np, N2, ntiles;
-    const uint4* tw;
-    const uint4* f;
-    uint32_t tw_bytes, f_bytes;
-    uint32_t off_tw, off_f, off_b2, a_half, b2_half, tmem_cols;
-};
-
-template <int UPT>  // 8-float units of x per thread per tile (W/8*128/256)
-__global__ void __launch_bounds__(kTcThreads, 1) dft_fwd_tc_kernel(const FwdTcArgs a) {
-    extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t bar;
-    __shared__ uint32_t tmem_base;
-    __shared__ int abort_flag;
-    uint8_t* base = align1024(smem_raw);
-    uint8_t* sA = base;  // x tile hi | lo, 128 rows x W, aliased by the D2 staging
-    uint8_t* sTW = base + a.off_tw;
-    uint8_t* sF = base + a.off_f;
-    uint8_t* sB2 = base + a.off_b2;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int W = a.W, H = a.H, N1 = a.N1, N2 = a.N2;
-
-    copy_table(sTW, a.tw, a.tw_bytes);
-    copy_table(sF, a.f, a.f_bytes);
-    if (warp == 0) {
-        tc::tmem_alloc(&tmem_base, a.tmem_cols);
-        tc::tmem_relinquish();
-    }
-    if (tid == 0) {
-        tc::mbar_init(&bar, 1);
-        abort_flag = 0;
-    }
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    const uint32_t tmem = tmem_base;
-    const uint32_t d1 = tmem, d2 = tmem + static_cast<uint32_t>(N1);
-    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint32_t phase = 0;
-    const int upr = W / 8;                 // 8-float units per row
-    const long long rows_total = static_cast<long long>(a.P) * H;
-    const uint32_t id1 = tc::idesc_bf16(128, N1), id2 = tc::idesc_bf16(128, N2);
-
-    float4 buf[UPT][2];
-    auto load_tile = [&](int t) {
-#pragma unroll
-        for (int i = 0; i < UPT; ++i) {
-            const int u = tid + i * kTcThreads;
-            const int r = u / upr, c8 = u - r * upr;
-            const long long grow = static_cast<long long>(t) * 128 + r;
-            if (grow < rows_total) {
-                const float4* src = reinterpret_cast<const float4*>(a.x + grow * W + c8 * 8);
-                buf[i][0] = __ldcs(src);
-                buf[i][1] = __ldcs(src + 1);
-            } else {
-                buf[i][0] = buf[i][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-        }
-    };
-
-    int tile = blockIdx.x;
-    if (tile < a.ntiles) load_tile(tile);
-    for (; tile < a.ntiles; tile += gridDim.x) {
-        // x tile -> bf16 hi/lo A operand
-#pragma unroll
-        for (int i = 0; i < UPT; ++i) {
-            const int u = tid + i * kTcThreads;
-            const int r = u / upr, c8 = u - r * upr;
-            const float v[8] = {buf[i][0].x, buf[i][0].y, buf[i][0].z, buf[i][0].w,
-                                buf[i][1].x, buf[i][1].y, buf[i][1].z, buf[i][1].w};
-            uint4 hi, lo;
-            tc::split8(v, hi, lo);
-            const uint32_t off = tc::kmajor_offset(128, r, c8 * 8);
-            *reinterpret_cast<uint4*>(sA + off) = hi;
-            *reinterpret_cast<uint4*>(sA + a.a_half + off) = lo;
-        }
-        if (tile + static_cast<int>(gridDim.x) < a.ntiles) load_tile(tile + gridDim.x);  // prefetch
-        tc::fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            tc::fence_after_sync();
-            const uint32_t A = tc::smem_u32(sA), B = tc::smem_u32(sTW);
-            for (int k = 0; k < W / 16; ++k) {
-                const uint32_t ao = tc::kmajor_offset(128, 0, k * 16), bo = tc::kmajor_offset(N1, 0, k * 16);
-                mma3(d1, A + ao, A + a.a_half + ao, B + bo, B + a.tw_bytes / 2 + bo, id1, k == 0);
-            }
-            tc::mma_commit(&bar);
-        }
-        if (!cta_wait(&bar, phase, &abort_flag, 1)) break;
-        tc::fence_after_sync();
-        // E1: D1 -> R^T (rows plane*N1 + n, K = h)
-        {
-            const int r = (warp & 3) * 32 + lane;
-            const int pl = r / H, h = r - pl * H;
-            const int half = warp >> 2;
-            for (int c0 = half * 16; c0 < N1; c0 += 32) {  // 16-column chunks dealt alternately
-                float v[16];
-                tc::tmem_ld16(d1 + lane_base + static_cast<uint32_t>(c0), v);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    __nv_bfloat16 hi, lo;
-                    tc::split2(v[i], hi, lo);
-                    const uint32_t off = tc::kmajor_offset(N2, pl * N1 + c0 + i, h);
-                    *reinterpret_cast<__nv_bfloat16*>(sB2 + off) = hi;
-                    *reinterpret_cast<__nv_bfloat16*>(sB2 + a.b2_half + off) = lo;
-                }
-            }
-        }
-        tc::fence_async_smem();
-        tc::fence_before_sync();
-        __syncthreads();
-        if (tid == 0) {
-            tc::fence_after_sync();
-            const uint32_t A = tc::smem_u32(sF), B = tc::smem_u32(sB2);
-            for (int k = 0; k < H / 16; ++k) {
-                const uint32_t ao = tc::kmajor_offset(128, 0, k * 16), bo = tc::kmajor_offset(N2, 0, k * 16);
-                mma3(d2, A + ao, A + a.f_bytes / 2 + ao, B + bo, B + a.b2_half + bo, id2, k == 0);
-            }
-            tc::mma_commit(&bar);
-        }
-        if (!cta_wait(&bar, phase, &abort_flag, 2)) break;
-        tc::fence_after_sync();
-        // E2: D2 -> fp32 staging [128][N2] (over the x tile, whose MMAs are complete)
-        float* st = reinterpret_cast<float*>(sA);
-        {
-            const int j = (warp & 3) * 32 + lane;
-            const int half = warp >> 2;
-            for (int c0 = half * 16; c0 < N2; c0 += 32) {
-                float v[16];
-                tc::tmem_ld16(d2 + lane_base + static_cast<uint32_t>(c0), v);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) st[j * N2 + c0 + i] = v[i];
-            }
-        }
-        tc::fence_before_sync();
-        __syncthreads();
-        const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
-        const int nout = a.np * S * m2;
-        for (int o = tid; o < nout; o += kTcThreads) {
-            const int pl = o / (S * m2);
-            const int rem = o - pl * S * m2;
-            const int s = rem / m2, ky = rem - s * m2;
-            const int p = tile * a.np + pl;
-            if (p >= a.P) continue;
-            const int cre = pl * N1 + ky, cim = cre + a.R2;
-            const float pc_re = st[s * N2 + cre], pc_im = st[s * N2 + cim];
-            const float ps_re = st[(S + s) * N2 + cre], ps_im = st[(S + s) * N2 + cim];
-            float2* dst = (s < m1 ? a.out1 + p * a.ops + static_cast<long long>(s) * a.ors
-                                  : a.out2 + p * a.ops + static_cast<long long>(s - m1) * a.ors) +
-                          ky;
-            *dst = make_float2(pc_re + ps_im, pc_im - ps_re);
-        }
-        __syncthreads();  // staging consumed before the next tile overwrites the x tile
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    if (warp == 0) {
-        tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, a.tmem_cols);
-    }
 }
 
 // ------------------------------------------------------------------ inverse
@@ -402,6 +210,7 @@ struct InvTcArgs {
     const uint4* e;
     uint32_t g_bytes, e_bytes;
     uint32_t off_e, off_b4, off_a5, b4_half, a5_half, tmem_cols;
+    int* watchdog;
 };
 
 __global__ void __launch_bounds__(kTcThreads, 1) dft_inv_tc_kernel(const InvTcArgs a) {
@@ -409,7 +218,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) dft_inv_tc_kernel(const InvTcAr
     __shared__ uint64_t bar;
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag;
-    uint8_t* base = align1024(smem_raw);
+    uint8_t* base = tc::align1024(smem_raw);
     uint8_t* sG = base;
     uint8_t* sE = base + a.off_e;
     uint8_t* sB4 = base + a.off_b4;
@@ -417,8 +226,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) dft_inv_tc_kernel(const InvTcAr
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int W = a.W, H = a.H, N1 = a.N1, N4 = a.N4, np = a.np;
 
-    copy_table(sG, a.g, a.g_bytes);
-    copy_table(sE, a.e, a.e_bytes);
+    tc::copy_table(sG, a.g, a.g_bytes);
+    tc::copy_table(sE, a.e, a.e_bytes);
     {  // padded rows / K columns of the spectrum operand stay zero for the whole kernel
         uint4* z = reinterpret_cast<uint4*>(sB4);
         for (uint32_t i = tid; i < 2 * a.b4_half / 16; i += kTcThreads) z[i] = make_uint4(0, 0, 0, 0);
@@ -478,7 +287,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) dft_inv_tc_kernel(const InvTcAr
             }
             tc::mma_commit(&bar);
         }
-        if (!cta_wait(&bar, phase, &abort_flag, 3)) break;
+        if (!cta_wait(&bar, phase, &abort_flag, a.watchdog, 3)) break;
         tc::fence_after_sync();
         // E4: D4 (lane = h) -> Z operand rows h of plane pl, K = c (re block | im block)
         {
@@ -515,7 +324,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) dft_inv_tc_kernel(const InvTcAr
             }
             tc::mma_commit(&bar);
         }
-        if (!cta_wait(&bar, phase, &abort_flag, 4)) break;
+        if (!cta_wait(&bar, phase, &abort_flag, a.watchdog, 4)) break;
         tc::fence_after_sync();
         // E5: D5 -> y rows
         {
@@ -550,69 +359,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) dft_inv_tc_kernel(const InvTcAr
 
 }  // namespace
 
-bool tc_supported(int H, int W, int m1, int m2) {
+bool tc_inv_supported(int H, int W, int m1, int m2) {
     if (!((H == 64 || H == 128) && (W == 64 || W == 128) && m2 >= 1 && m2 <= 32 && m1 >= 1 && 4 * m1 <= 128))
         return false;
     const TcShape s = tc_shape(H, W, m1, m2);
-    // forward: the fp32 D2 staging [128][N2] reuses the x tile (128 x W bf16 hi + lo)
-    if (s.N2 > W || s.N2 > 256) return false;
+    if (s.N2 > 256) return false;
+    if (inv_smem_bytes(s) > kMaxDynSmem) return false;
     // inverse: D4 (N2 columns) and D5 (np*W columns) share one 256-column TMEM allocation
     if (s.N2 + s.np * W > 256) return false;
     return true;
 }
 
-cudaError_t launch_dft_fwd_tc(const float* x, float2* out1, float2* out2, long long ops, int ors, int P, int H,
-                              int W, int m1, int m2, cudaStream_t stream) {
-    if (!tc_supported(H, W, m1, m2) || (reinterpret_cast<uintptr_t>(x) & 15) != 0) return cudaErrorInvalidValue;
-    const TcShape s = tc_shape(H, W, m1, m2);
-    const TcTables* t = nullptr;
-    cudaError_t e = get_tc_tables(s, &t);
-    if (e != cudaSuccess) return e;
-    FwdTcArgs a;
-    a.x = x;
-    a.out1 = out1;
-    a.out2 = out2;
-    a.ops = ops;
-    a.ors = ors;
-    a.P = P;
-    a.H = H;
-    a.W = W;
-    a.m1 = m1;
-    a.m2 = m2;
-    a.R2 = s.R2;
-    a.N1 = s.N1;
-    a.np = s.np;
-    a.N2 = s.N2;
-    a.ntiles = static_cast<int>((static_cast<long long>(P) * H + 127) / 128);
-    a.tw = t->fwd_tw;
-    a.f = t->fwd_f;
-    a.tw_bytes = t->tw_bytes;
-    a.f_bytes = t->f_bytes;
-    a.a_half = 128u * static_cast<uint32_t>(W) * 2u;
-    a.b2_half = static_cast<uint32_t>(s.N2) * static_cast<uint32_t>(H) * 2u;
-    a.off_tw = 2 * a.a_half;
-    a.off_f = a.off_tw + a.tw_bytes;
-    a.off_b2 = a.off_f + a.f_bytes;
-    const size_t smem = a.off_b2 + 2 * a.b2_half + 1024;
-    a.tmem_cols = tmem_cols_for(s.N1 + s.N2);
-    const int upt = 128 * (W / 8) / kTcThreads;
-    auto run = [&](auto kernel) -> cudaError_t {
-        int per_sm = 1;
-        cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), smem, kTcThreads, &per_sm);
-        if (err != cudaSuccess) return err;
-        per_sm = std::min<int>(per_sm, static_cast<int>(512 / a.tmem_cols));
-        const int grid = std::max(1, std::min(a.ntiles, per_sm * num_sms()));
-        kernel<<<grid, kTcThreads, smem, stream>>>(a);
-        return cudaGetLastError();
-    };
-    if (upt == 4) return run(dft_fwd_tc_kernel<4>);
-    if (upt == 8) return run(dft_fwd_tc_kernel<8>);
-    return cudaErrorInvalidValue;
-}
-
 cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long ips, int irs, float* y, int Q,
                               int H, int W, int m1, int m2, cudaStream_t stream) {
-    if (!tc_supported(H, W, m1, m2) || (reinterpret_cast<uintptr_t>(y) & 15) != 0) return cudaErrorInvalidValue;
+    if (!tc_inv_supported(H, W, m1, m2) || (reinterpret_cast<uintptr_t>(y) & 15) != 0) return cudaErrorInvalidValue;
     const TcShape s = tc_shape(H, W, m1, m2);
     if (s.np * W > 256 - s.N2) return cudaErrorInvalidValue;  // D4 + D5 columns
     const TcTables* t = nullptr;
@@ -646,6 +406,8 @@ cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long ip
     a.a5_half = static_cast<uint32_t>(s.np) * 128u * 128u;
     const size_t smem = a.off_a5 + 2 * a.a5_half + 1024;
     a.tmem_cols = tmem_cols_for(s.N2 + s.np * W);
+    e = device_watchdog(&a.watchdog);
+    if (e != cudaSuccess) return e;
     int per_sm = 1;
     e = prepare_kernel(reinterpret_cast<const void*>(dft_inv_tc_kernel), smem, kTcThreads, &per_sm);
     if (e != cudaSuccess) return e;
@@ -653,13 +415,6 @@ cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long ip
     const int grid = std::max(1, std::min(a.ntiles, per_sm * num_sms()));
     dft_inv_tc_kernel<<<grid, kTcThreads, smem, stream>>>(a);
     return cudaGetLastError();
-}
-
-cudaError_t read_watchdog(int* value, bool reset) {
-    cudaError_t e = cudaMemcpyFromSymbol(value, g_watchdog, sizeof(int));
-    if (e != cudaSuccess || !reset) return e;
-    const int zero = 0;
-    return cudaMemcpyToSymbol(g_watchdog, &zero, sizeof(int));
 }
 
 }  // namespace scx

@@ -60,10 +60,11 @@ cudaError_t launch_dft_inv(const float2* in1, const float2* in2,
                            float* y, int Q, int H, int W, int m1, int m2,
                            const Twiddles& tw, cudaStream_t stream);
 
-// Tensor-core (tcgen05) truncated DFT kernels, for H in {64,128}, W in {64,128},
-// m2 <= 32, 4*m1 <= 128 (tc_supported).  Their operand tables are built per shape on first
-// use (cudaMalloc + synchronous copy).
-bool tc_supported(int H, int W, int m1, int m2);
+// Tensor-core (tcgen05) truncated DFT kernels for the shapes tc_fwd_supported /
+// tc_inv_supported accept.  Their operand tables are built per shape on first use
+// (cudaMalloc + synchronous copy, so the first call must not happen inside stream capture).
+bool tc_fwd_supported(int H, int W, int m1, int m2);
+bool tc_inv_supported(int H, int W, int m1, int m2);
 cudaError_t launch_dft_fwd_tc(const float* x, float2* out1, float2* out2, long long out_plane_stride,
                               int out_row_stride, int P, int H, int W, int m1, int m2, cudaStream_t stream);
 cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long in_plane_stride,
@@ -77,7 +78,9 @@ cudaError_t dft_fwd(const float* x, float2* out1, float2* out2, long long out_pl
 cudaError_t dft_inv(const float2* in1, const float2* in2, long long in_plane_stride, int in_row_stride, float* y,
                     int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream);
 
-// Device watchdog word: non-zero after a tensor-core kernel gave up on a wait.
+// Device watchdog word of the current device (allocated and zeroed on first use, never
+// freed): the tensor-core kernels store a non-zero code there when they give up on a wait.
+cudaError_t device_watchdog(int** out);
 cudaError_t read_watchdog(int* value, bool reset);
 
 // Per-mode complex channel mixing y_c[b,o,k] = sum_i x_c[b,i,k] * w_c[i,o,k] for

@@ -68,6 +68,11 @@ cudaError_t prepare_kernel(const void* kernel, size_t bytes, int threads, int* b
     if (bytes > 48 * 1024 && bytes > cur) {
         err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
         if (err != cudaSuccess) return err;
+        // prefer the largest shared-memory carveout so that occupancy is limited by the
+        // kernel's own needs, not by the default L1/shared split
+        err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   static_cast<int>(cudaSharedmemCarveoutMaxShared));
+        if (err != cudaSuccess) return err;
         cur = bytes;
     }
     int n = 0;
@@ -77,6 +82,42 @@ cudaError_t prepare_kernel(const void* kernel, size_t bytes, int threads, int* b
     seen[key] = n;
     *blocks_per_sm = n;
     return cudaSuccess;
+}
+
+cudaError_t device_watchdog(int** out) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    static std::mutex m;
+    static std::map<int, int*> words;
+    std::lock_guard<std::mutex> lock(m);
+    auto it = words.find(dev);
+    if (it != words.end()) {
+        *out = it->second;
+        return cudaSuccess;
+    }
+    int* w = nullptr;
+    err = cudaMalloc(&w, sizeof(int));
+    if (err != cudaSuccess) return err;
+    const int zero = 0;
+    err = cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        cudaFree(w);
+        return err;
+    }
+    words[dev] = w;
+    *out = w;
+    return cudaSuccess;
+}
+
+cudaError_t read_watchdog(int* value, bool reset) {
+    int* w = nullptr;
+    cudaError_t e = device_watchdog(&w);
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpy(value, w, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess || !reset) return e;
+    const int zero = 0;
+    return cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice);
 }
 
 cudaError_t get_twiddles(int H, int W, int m1, int m2, const Twiddles** out) {

@@ -288,6 +288,34 @@ def test_tensor_core_corners_vs_f64(cuda_device):
     assert np.abs(y - ref_y).max() <= 1e-4 * np.abs(ref_y).max()
 
 
+FWD_TC_SHAPES = [
+    (1, 3, 64, 64, 12, 12),      # W = 64: 2 planes per column tile, the last one half empty
+    (1, 1, 128, 128, 16, 16),    # one plane: fewer planes than SMs
+    (2, 5, 128, 64, 16, 24),     # H != W, 24 columns per TW block
+    (3, 3, 64, 128, 5, 32),      # m2 = 32, slots of the second group unused
+    (4, 8, 128, 128, 7, 3),      # 8 columns per TW block
+    (40, 32, 128, 128, 16, 16),  # several 2-plane tiles per CTA
+    (2, 151, 64, 64, 12, 12),    # odd plane count over all SMs
+]
+
+
+@pytest.mark.parametrize("shape", FWD_TC_SHAPES)
+def test_forward_corners_vs_f64(shape, cuda_device):
+    """Corner spectra of the forward transform against the float64 direct DFT."""
+    import spectral_conv_ext
+
+    B, C, H, W, m1, m2 = shape
+    g = torch.Generator().manual_seed(3 * sum(shape))
+    x = torch.randn(B, C, H, W, generator=g)
+    c1, c2 = spectral_conv_ext.rfft2_corners(x.to(cuda_device), m1, m2)
+    r1, r2 = oracle.rfft2_corners_f64(x.numpy(), m1, m2)
+    for got, ref in ((c1, r1), (c2, r2)):
+        got = got.cpu().numpy()
+        got = got[..., 0] + 1j * got[..., 1]
+        err = np.abs(got - ref).max() / np.abs(ref).max()
+        assert err <= 2e-5, err
+
+
 def test_zz_watchdog_clean(cuda_device):
     """No tensor-core kernel gave up on a wait during this session."""
     import _scx

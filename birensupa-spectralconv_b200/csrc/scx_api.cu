@@ -48,14 +48,14 @@ namespace scx {
 
 cudaError_t dft_fwd(const float* x, float2* out1, float2* out2, long long out_plane_stride, int out_row_stride,
                     int P, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream) {
-    if (!ffma_forced() && tc_fwd_supported(H, W, m1, m2))
+    if (!ffma_forced() && tc_fwd_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
         return launch_dft_fwd_tc(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, stream);
     return launch_dft_fwd(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, tw, stream);
 }
 
 cudaError_t dft_inv(const float2* in1, const float2* in2, long long in_plane_stride, int in_row_stride, float* y,
                     int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream) {
-    if (!ffma_forced() && tc_inv_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(y) & 15) == 0)
+    if (!ffma_forced() && tc_inv_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(y) & 3) == 0)
         return launch_dft_inv_tc(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, stream);
     return launch_dft_inv(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, tw, stream);
 }

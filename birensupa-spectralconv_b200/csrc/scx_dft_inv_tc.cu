@@ -1,0 +1,450 @@
+// Tensor-core (tcgen05, bf16x3 -> fp32) zero-padded inverse real DFT from the two corner
+// spectra: the B200 replacement for the corner scatter + suFFT C2R of spectral_conv2d_supa
+// (spectral_conv/spectral_conv_ops.py:400-431, spectral_conv/spectral_conv_ext.cpp:180-245).
+//
+// For planes y[h][w] (H, W in {64, 128}), corner slots s < 2*m1 <= 32 and ky < m2 <= 32:
+//
+//   S4  column inverse, 128 TMEM lanes = (plane, c) for G4 planes, c = (re|im, ky):
+//         D4[(p,c)][h] = sum_j Yr[(p,c)][j] * G[h][j]
+//       j = (cos|sin, slot); G = cos / sin(2 pi kx_s h / H), 0 for a corner-1 slot that
+//       corner 2 overwrites (spectral_conv/reference_pytorch.py:44-46);
+//       Yr rows (re, ky) = [Y_re | -Y_im], rows (im, ky) = [Y_im | Y_re].
+//   E4  D4 rows -> Z operand in shared memory, MN-major (n = h), one thread per (p, c)
+//       writing 16-byte vectors
+//   S5  row inverse, 128 TMEM lanes = w (W = 128) or (plane, w) for two planes (W = 64,
+//       block-diagonal twiddle operand):
+//         D5[w][h] = sum_c E[w][c] * Z[h][c],  E = c_ky/(HW) (cos | -sin)(2 pi ky w / W)
+//       with c_ky = 1 for ky = 0 and ky = W/2, else 2 (the C2R Hermitian weights).
+//   E5  each thread holds one column w of the plane: y[h][w] stores, 128 bytes per warp
+//       instruction, no shared-memory staging.
+//
+// Every product is bf16x3 (hi*hi + hi*lo + lo*hi) chained along K into one fp32
+// accumulator.  Warp roles (persistent, one CTA per SM, contiguous balanced plane ranges):
+//   warps 0..3   loaders: corner spectra -> Yr operand (MN-major, double-buffered)
+//   warps 4..7   E4;  warps 8..15  E5 (two per TMEM sub-partition, halves of h)
+//   warp 16      lane 0 issues every MMA (and first brings the twiddle tables into shared
+//                memory with one bulk copy)
+// Every wait is bounded (about a second); a role that gives up stores a code in the
+// device watchdog word and leaves its loop.
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "scx_internal.h"
+#include "scx_tc.cuh"
+#include "scx_tc_host.h"
+
+namespace scx {
+namespace {
+
+constexpr int kLoadWarps = 4;
+constexpr int kE4Warps = 4;
+constexpr int kE5Warps = 8;
+constexpr int kE4Warp0 = kLoadWarps;             // 4
+constexpr int kE5Warp0 = kE4Warp0 + kE4Warps;    // 8
+constexpr int kMmaWarp = kE5Warp0 + kE5Warps;    // 16
+constexpr int kThreads = (kMmaWarp + 1) * 32;    // 544
+constexpr int kBarE4 = 2, kBarE5 = 3;            // named barriers
+constexpr int kKg = 64;                          // S4 K: (cos|sin) x 32 slots
+
+struct InvArgs {
+    const float2* in1;
+    const float2* in2;
+    long long ips;  // input plane stride (float2 units)
+    int irs;        // input row stride (float2 units)
+    float* y;
+    int Q, m1, m2;
+    const uint4* tab;  // G (hi, lo) then E (hi, lo)
+    uint32_t tab_bytes;
+    int* watchdog;
+};
+
+struct InvBars {
+    uint64_t yFull[2], yEmpty[2], d4Full, d4Empty, zFull, zEmpty, d5Full[2], d5Empty[2], drain, tab;
+};
+
+template <int H, int W, int N1P>
+struct InvCfg {
+    static constexpr int R2P = N1P / 2;            // ky rows per re/im block
+    static constexpr int G4 = 128 / N1P;           // planes per S4 group
+    static constexpr int G5 = 128 / W;             // planes per S5 chain
+    static constexpr int NZ = G4 / G5;             // S5 chains per group
+    static constexpr int K5 = G5 * N1P;            // S5 K (block-diagonal for W = 64)
+    static constexpr int K5P = (K5 + 63) / 64 * 64;                      // K-major rows span 64 K
+    static constexpr uint32_t YRB = 128u * kKg * 2u;                     // one Yr part, MN-major
+    static constexpr uint32_t GB = static_cast<uint32_t>(H) * kKg * 2u;  // one G part, K-major
+    static constexpr uint32_t EB = 128u * K5P * 2u;                      // one E part, K-major
+    static constexpr uint32_t ZB = static_cast<uint32_t>(H) * K5 * 2u;   // one Z part, MN-major
+    static constexpr uint32_t ZSBO = static_cast<uint32_t>(H / 64) * 1024u;  // Z K-group stride
+    static constexpr uint32_t OFF_YR = 0;                        // 2 buffers x (hi, lo)
+    static constexpr uint32_t OFF_G = OFF_YR + 4u * YRB;         // G hi, G lo
+    static constexpr uint32_t OFF_E = OFF_G + 2u * GB;           // E hi, E lo
+    static constexpr uint32_t OFF_Z = OFF_E + 2u * EB;           // NZ chains x (hi, lo)
+    static constexpr uint32_t SMEM = OFF_Z + 2u * NZ * ZB + 1024u;
+    static_assert(SMEM <= 227u * 1024u - 512u, "shared memory budget");
+    static constexpr uint32_t COL_D5 = static_cast<uint32_t>(H);  // D4 at 0
+    static constexpr uint32_t COLS = 3u * H;
+    static constexpr uint32_t TMEM_COLS = COLS <= 256 ? 256u : 512u;
+};
+
+template <int H, int W, int N1P>
+__global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a) {
+    using C = InvCfg<H, W, N1P>;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ InvBars bars;
+    __shared__ uint32_t tmem_base;
+    uint8_t* base = tc::align1024(smem_raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    const int Q = a.Q;
+    const int q0 = static_cast<int>(static_cast<long long>(blockIdx.x) * Q / gridDim.x);
+    const int q1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * Q / gridDim.x);
+    const int NG = (q1 - q0 + C::G4 - 1) / C::G4;  // S4 groups
+
+    if (warp == 0) {
+        tc::tmem_alloc(&tmem_base, C::TMEM_COLS);
+        tc::tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&bars.yFull[i], kLoadWarps);
+            tc::mbar_init(&bars.yEmpty[i], 1);
+            tc::mbar_init(&bars.d5Full[i], 1);
+            tc::mbar_init(&bars.d5Empty[i], 1);
+        }
+        tc::mbar_init(&bars.d4Full, 1);
+        tc::mbar_init(&bars.d4Empty, 1);
+        tc::mbar_init(&bars.zFull, 1);
+        tc::mbar_init(&bars.zEmpty, 1);
+        tc::mbar_init(&bars.drain, 1);
+        tc::mbar_init(&bars.tab, 1);
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_base;
+
+    if (warp < kLoadWarps) {
+        // ------------------------------------------------------------ loaders
+        // Element (p, s, ky) of a group feeds Yr rows (p, re, ky) and (p, im, ky) at
+        // K = s (cos) and 32 + s (sin).  Yr is MN-major (rows contiguous), so threads with
+        // consecutive ky write consecutive bf16 values.
+        const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
+        constexpr int PER = C::G4 * 32 * C::R2P;  // elements per group (slots padded to 32)
+        bool ok = true;
+        for (int t = 0; t < NG && ok; ++t) {
+            const int yb = t & 1;
+            ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.yEmpty[yb], ((t >> 1) & 1) ^ 1));
+            if (!ok) break;
+            uint8_t* yr_hi = base + C::OFF_YR + static_cast<uint32_t>(yb) * 2u * C::YRB;
+            uint8_t* yr_lo = yr_hi + C::YRB;
+            for (int e = tid; e < PER; e += kLoadWarps * 32) {
+                const int ky = e % C::R2P, rest = e / C::R2P;
+                const int s = rest % 32, p = rest / 32;
+                const int q = q0 + t * C::G4 + p;
+                float2 v = make_float2(0.f, 0.f);
+                if (q < q1 && s < S && ky < m2)
+                    v = s < m1 ? __ldg(a.in1 + static_cast<long long>(q) * a.ips + static_cast<long long>(s) * a.irs + ky)
+                               : __ldg(a.in2 + static_cast<long long>(q) * a.ips +
+                                       static_cast<long long>(s - m1) * a.irs + ky);
+                const int mre = p * N1P + ky, mim = mre + C::R2P;
+                const float vals[4] = {v.x, -v.y, v.y, v.x};
+                const int ms[4] = {mre, mre, mim, mim};
+                const int ks[4] = {s, 32 + s, s, 32 + s};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    __nv_bfloat16 hi, lo;
+                    tc::split2(vals[u], hi, lo);
+                    const int m = ms[u], k = ks[u];
+                    const uint32_t off = static_cast<uint32_t>(k >> 3) * 2048u + static_cast<uint32_t>(m >> 6) * 1024u +
+                                         static_cast<uint32_t>(k & 7) * 128u +
+                                         (static_cast<uint32_t>(((m & 63) >> 3) ^ (k & 7)) << 4) +
+                                         static_cast<uint32_t>(m & 7) * 2u;
+                    *reinterpret_cast<__nv_bfloat16*>(yr_hi + off) = hi;
+                    *reinterpret_cast<__nv_bfloat16*>(yr_lo + off) = lo;
+                }
+            }
+            tc::fence_async_smem();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars.yFull[yb]);
+        }
+        if (!ok && lane == 0) atomicExch(a.watchdog, 30);
+    } else if (warp < kE5Warp0) {
+        // ------------------------------------------------------------ E4
+        const int q = warp & 3;
+        const int e4tid = tid - kE4Warp0 * 32;  // 0..127
+        const int l = q * 32 + lane;            // D4 lane: (p, c)
+        const int p = l / N1P, c = l % N1P;
+        const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+        const int chain = p / C::G5, kz = (p % C::G5) * N1P + c;  // Z chain and its K row
+        bool ok = true;
+        for (int t = 0; t < NG; ++t) {
+            ok = tc::mbar_wait_bounded(&bars.d4Full, t & 1) && tc::mbar_wait_bounded(&bars.zEmpty, (t & 1) ^ 1);
+            if (tc::named_any(kBarE4, kE4Warps * 32, !ok)) {
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            uint8_t* z_hi = base + C::OFF_Z + static_cast<uint32_t>(chain) * 2u * C::ZB;
+            uint8_t* z_lo = z_hi + C::ZB;
+            const uint32_t krow = static_cast<uint32_t>(kz >> 3) * C::ZSBO + static_cast<uint32_t>(kz & 7) * 128u;
+#pragma unroll
+            for (int h0 = 0; h0 < H; h0 += 32) {
+                float v[32];
+                tc::tmem_ld32_nowait(tmem + lane_addr + static_cast<uint32_t>(h0), v);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int c8 = 0; c8 < 4; ++c8) {
+                    uint4 h4, l4;
+                    tc::split8(v + 8 * c8, h4, l4);
+                    const int hc = h0 + 8 * c8;  // first h of this 16-byte chunk
+                    const uint32_t off = krow + static_cast<uint32_t>(hc >> 6) * 1024u +
+                                         (static_cast<uint32_t>(((hc & 63) >> 3) ^ (kz & 7)) << 4);
+                    *reinterpret_cast<uint4*>(z_hi + off) = h4;
+                    *reinterpret_cast<uint4*>(z_lo + off) = l4;
+                }
+            }
+            tc::fence_before_sync();
+            tc::fence_async_smem();
+            tc::named_sync(kBarE4, kE4Warps * 32);
+            if (e4tid == 0) {
+                tc::mbar_arrive(&bars.d4Empty);
+                tc::mbar_arrive(&bars.zFull);
+            }
+        }
+        if (!ok && e4tid == 0) atomicExch(a.watchdog, 31);
+    } else if (warp < kMmaWarp) {
+        // ------------------------------------------------------------ E5
+        const int q = warp & 3, sub = (warp - kE5Warp0) >> 2;  // sub-partition, half of h
+        const int e5tid = tid - kE5Warp0 * 32;                  // 0..255
+        const int l = q * 32 + lane;
+        const int g = l / W, w = l % W;
+        const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+        constexpr int HH = H / 2;
+        bool ok = true;
+        int n = 0;  // S5 chains consumed
+        for (int t = 0; t < NG && ok; ++t) {
+            for (int j = 0; j < C::NZ; ++j, ++n) {
+                const int b = n & 1;
+                ok = tc::mbar_wait_bounded(&bars.d5Full[b], (n >> 1) & 1);
+                if (tc::named_any(kBarE5, kE5Warps * 32, !ok)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const int qp = q0 + t * C::G4 + j * C::G5 + g;  // warp-uniform plane
+                float* dst = a.y + (static_cast<size_t>(qp) * H + sub * HH) * W + w;
+                const uint32_t src = tmem + lane_addr + C::COL_D5 + static_cast<uint32_t>(b * H + sub * HH);
+#pragma unroll
+                for (int h0 = 0; h0 < HH; h0 += 32) {
+                    float v[32];
+                    tc::tmem_ld32_nowait(src + static_cast<uint32_t>(h0), v);
+                    tc::tmem_wait_ld();
+                    if (qp < q1) {
+#pragma unroll
+                        for (int k = 0; k < 32; ++k) __stcs(dst + static_cast<size_t>(h0 + k) * W, v[k]);
+                    }
+                }
+                tc::fence_before_sync();
+                tc::named_sync(kBarE5, kE5Warps * 32);
+                if (e5tid == 0) tc::mbar_arrive(&bars.d5Empty[b]);
+            }
+        }
+        if (!ok && e5tid == 0) atomicExch(a.watchdog, 32);
+    } else if (warp == kMmaWarp && lane == 0) {
+        // ------------------------------------------------------------ MMA issuer
+        const uint32_t sb = tc::smem_u32(base);
+        tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
+        tc::bulk_g2s(base + C::OFF_G, a.tab, a.tab_bytes, &bars.tab);
+        constexpr uint32_t id4 = tc::idesc_bf16(128, H) | tc::kIdescAMajorMN;
+        constexpr uint32_t id5 = tc::idesc_bf16(128, H) | tc::kIdescBMajorMN;
+        const uint32_t d4 = tmem, d5 = tmem + C::COL_D5;
+        const uint64_t dG[2] = {tc::desc_sw128(sb + C::OFF_G), tc::desc_sw128(sb + C::OFF_G + C::GB)};
+        const uint64_t dE[2] = {tc::desc_sw128(sb + C::OFF_E), tc::desc_sw128(sb + C::OFF_E + C::EB)};
+        bool ok = tc::mbar_wait_bounded(&bars.tab, 0);
+        int n = 0;
+        for (int t = 0; t < NG && ok; ++t) {
+            const int yb = t & 1;
+            // S4: parts (Yr_hi, G_hi), (Yr_hi, G_lo), (Yr_lo, G_hi), K = 64 each
+            ok = tc::mbar_wait_bounded(&bars.yFull[yb], (t >> 1) & 1) && tc::mbar_wait_bounded(&bars.d4Empty, (t & 1) ^ 1);
+            if (!ok) break;
+            tc::fence_after_sync();
+            const uint32_t yr = sb + C::OFF_YR + static_cast<uint32_t>(yb) * 2u * C::YRB;
+            const uint64_t dY[2] = {tc::desc_mn_sw128(yr, 1024u, 2048u), tc::desc_mn_sw128(yr + C::YRB, 1024u, 2048u)};
+#pragma unroll
+            for (int part = 0; part < 3; ++part) {
+                const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
+#pragma unroll
+                for (int ks = 0; ks < kKg / 16; ++ks) {
+                    const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4, bo = (static_cast<uint32_t>(ks) * 32u) >> 4;
+                    tc::mma_bf16(d4, dY[ap] + ao, dG[bp] + bo, id4, (part | ks) ? 1u : 0u);
+                }
+            }
+            tc::mma_commit(&bars.yEmpty[yb]);
+            tc::mma_commit(&bars.d4Full);
+            // S5 chains of this group once E4 has written Z
+            for (int j = 0; j < C::NZ && ok; ++j, ++n) {
+                const int b = n & 1;
+                if (j == 0) ok = tc::mbar_wait_bounded(&bars.zFull, t & 1);
+                if (ok) ok = tc::mbar_wait_bounded(&bars.d5Empty[b], ((n >> 1) & 1) ^ 1);
+                if (!ok) break;
+                tc::fence_after_sync();
+                const uint32_t zc = sb + C::OFF_Z + static_cast<uint32_t>(j) * 2u * C::ZB;
+                const uint64_t dZ[2] = {tc::desc_mn_sw128(zc, 1024u, C::ZSBO), tc::desc_mn_sw128(zc + C::ZB, 1024u, C::ZSBO)};
+                const uint32_t dd = d5 + static_cast<uint32_t>(b * H);
+#pragma unroll
+                for (int part = 0; part < 3; ++part) {
+                    const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
+#pragma unroll
+                    for (int ks = 0; ks < C::K5 / 16; ++ks) {
+                        const uint32_t ao = (static_cast<uint32_t>(ks >> 2) * 128u * 128u + (ks & 3) * 32u) >> 4;
+                        const uint32_t bo = (static_cast<uint32_t>(ks) * 2u * C::ZSBO) >> 4;
+                        tc::mma_bf16(dd, dE[ap] + ao, dZ[bp] + bo, id5, (part | ks) ? 1u : 0u);
+                    }
+                }
+                tc::mma_commit(&bars.d5Full[b]);
+                if (j == C::NZ - 1) tc::mma_commit(&bars.zEmpty);
+            }
+        }
+        if (!ok) atomicExch(a.watchdog, 33);
+        tc::mma_commit(&bars.drain);
+        tc::mbar_wait_bounded(&bars.drain, 0);
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+struct InvTable {
+    const uint4* data;
+    uint32_t bytes;
+};
+
+std::mutex g_mutex;
+std::map<std::tuple<int, int, int, int, int>, InvTable> g_tables;
+
+// G (H rows x 64, K-major) hi then lo, followed by E (128 rows x K5, K-major) hi then lo.
+cudaError_t get_inv_table(int H, int W, int m1, int m2, int N1P, const InvTable** out) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    const auto key = std::make_tuple(dev, H, W, m1, m2);
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_tables.find(key);
+    if (it != g_tables.end()) {
+        *out = &it->second;
+        return cudaSuccess;
+    }
+    const int S = 2 * m1, R2P = N1P / 2, G5 = 128 / W, K5 = G5 * N1P;
+    host::KMajor ghi(H, kKg), glo(H, kKg);
+    for (int s = 0; s < S; ++s) {
+        const int kx = host::slot_row(s, H, m1);
+        if (s < m1 && kx >= H - m1) continue;  // overwritten by corner 2
+        for (int h = 0; h < H; ++h) {
+            const double t = host::ang(kx, h, H);
+            uint16_t hi, lo;
+            host::bf16_split(std::cos(t), hi, lo);
+            ghi.set(h, s, hi);
+            glo.set(h, s, lo);
+            host::bf16_split(std::sin(t), hi, lo);
+            ghi.set(h, 32 + s, hi);
+            glo.set(h, 32 + s, lo);
+        }
+    }
+    host::KMajor ehi(128, K5), elo(128, K5);
+    const double inv_hw = 1.0 / (static_cast<double>(H) * static_cast<double>(W));
+    for (int g = 0; g < G5; ++g)
+        for (int w = 0; w < W; ++w)
+            for (int ky = 0; ky < m2; ++ky) {
+                const bool single = (ky == 0) || ((W % 2 == 0) && (ky == W / 2));
+                const double cw = (single ? 1.0 : 2.0) * inv_hw;
+                const double t = host::ang(ky, w, W);
+                uint16_t hi, lo;
+                host::bf16_split(cw * std::cos(t), hi, lo);
+                ehi.set(g * W + w, g * N1P + ky, hi);
+                elo.set(g * W + w, g * N1P + ky, lo);
+                host::bf16_split(-cw * std::sin(t), hi, lo);
+                ehi.set(g * W + w, g * N1P + R2P + ky, hi);
+                elo.set(g * W + w, g * N1P + R2P + ky, lo);
+            }
+    std::vector<uint16_t> buf(ghi.data);
+    for (const auto* part : {&glo, &ehi, &elo}) buf.insert(buf.end(), part->data.begin(), part->data.end());
+    const size_t bytes = buf.size() * 2;
+    void* d = nullptr;
+    err = cudaMalloc(&d, bytes);
+    if (err != cudaSuccess) return err;
+    err = cudaMemcpy(d, buf.data(), bytes, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        cudaFree(d);
+        return err;
+    }
+    InvTable t;
+    t.data = static_cast<const uint4*>(d);
+    t.bytes = static_cast<uint32_t>(bytes);
+    auto res = g_tables.emplace(key, t);
+    *out = &res.first->second;
+    return cudaSuccess;
+}
+
+template <int H, int W, int N1P>
+cudaError_t run_inv(const InvArgs& a, cudaStream_t stream) {
+    using C = InvCfg<H, W, N1P>;
+    if (a.tab_bytes != 2u * C::GB + 2u * C::EB) return cudaErrorInvalidValue;
+    auto kernel = dft_inv_tc_kernel<H, W, N1P>;
+    int per_sm = 1;
+    cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), C::SMEM, kThreads, &per_sm);
+    if (err != cudaSuccess) return err;
+    const int grid = std::max(1, std::min(a.Q, num_sms()));
+    kernel<<<grid, kThreads, C::SMEM, stream>>>(a);
+    return cudaGetLastError();
+}
+
+template <int H, int W>
+cudaError_t run_inv_n(const InvArgs& a, int N1P, cudaStream_t stream) {
+    return N1P == 32 ? run_inv<H, W, 32>(a, stream) : run_inv<H, W, 64>(a, stream);
+}
+
+}  // namespace
+
+bool tc_inv_supported(int H, int W, int m1, int m2) {
+    return (H == 64 || H == 128) && (W == 64 || W == 128) && m1 >= 1 && 2 * m1 <= 32 && m2 >= 1 && m2 <= 32 &&
+           m2 <= W / 2 + 1;
+}
+
+cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long ips, int irs, float* y, int Q, int H,
+                              int W, int m1, int m2, cudaStream_t stream) {
+    if (!tc_inv_supported(H, W, m1, m2) || Q <= 0 || (reinterpret_cast<uintptr_t>(y) & 3) != 0)
+        return cudaErrorInvalidValue;
+    const int N1P = m2 <= 16 ? 32 : 64;
+    const InvTable* t = nullptr;
+    cudaError_t e = get_inv_table(H, W, m1, m2, N1P, &t);
+    if (e != cudaSuccess) return e;
+    int* wd = nullptr;
+    e = device_watchdog(&wd);
+    if (e != cudaSuccess) return e;
+    InvArgs a;
+    a.in1 = in1;
+    a.in2 = in2;
+    a.ips = ips;
+    a.irs = irs;
+    a.y = y;
+    a.Q = Q;
+    a.m1 = m1;
+    a.m2 = m2;
+    a.tab = t->data;
+    a.tab_bytes = t->bytes;
+    a.watchdog = wd;
+    if (H == 64 && W == 64) return run_inv_n<64, 64>(a, N1P, stream);
+    if (H == 64 && W == 128) return run_inv_n<64, 128>(a, N1P, stream);
+    if (H == 128 && W == 64) return run_inv_n<128, 64>(a, N1P, stream);
+    return run_inv_n<128, 128>(a, N1P, stream);
+}
+
+}  // namespace scx

@@ -50,12 +50,13 @@ inline uint32_t kmajor_offset(int rows, int r, int k) {
            static_cast<uint32_t>((kk & 7) << 1);
 }
 
-// A bf16 operand image (rows x kdim, K-major SW128), filled element by element.
+// A bf16 operand image (rows x kdim, K-major SW128), filled element by element.  The
+// swizzle spans whole 128-byte rows, so K is padded to a multiple of 64 elements.
 struct KMajor {
     int rows, kdim;
     std::vector<uint16_t> data;
-    KMajor(int r, int k) : rows(r), kdim(k), data(static_cast<size_t>(r) * k, 0) {}
-    void set(int r, int k, uint16_t v) { data[kmajor_offset(rows, r, k) / 2] = v; }
+    KMajor(int r, int k) : rows(r), kdim(k), data(static_cast<size_t>(r) * round_up(k, 64), 0) {}
+    void set(int r, int k, uint16_t v) { data.at(kmajor_offset(rows, r, k) / 2) = v; }
     size_t bytes() const { return data.size() * 2; }
 };
 

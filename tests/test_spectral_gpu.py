@@ -316,6 +316,35 @@ def test_forward_corners_vs_f64(shape, cuda_device):
         assert err <= 2e-5, err
 
 
+INV_TC_SHAPES = [
+    (1, 3, 64, 64, 12, 12),      # 2 planes per S5 chain, the last group mostly empty
+    (1, 1, 128, 128, 16, 16),    # one plane
+    (2, 5, 128, 64, 16, 24),     # H != W, 64 spectrum rows per plane
+    (3, 3, 64, 128, 5, 32),      # m2 = 32
+    (4, 8, 128, 128, 7, 3),
+    (40, 32, 128, 128, 16, 16),  # several groups per CTA
+    (2, 151, 64, 64, 12, 12),    # odd plane count over all SMs
+]
+
+
+@pytest.mark.parametrize("shape", INV_TC_SHAPES)
+def test_inverse_corners_vs_f64(shape, cuda_device):
+    """Zero-padded inverse from the two corner spectra against numpy's float64 irfft2."""
+    import spectral_conv_ext
+
+    B, C, H, W, m1, m2 = shape
+    g = torch.Generator().manual_seed(5 * sum(shape))
+    c1 = torch.randn(B, C, m1, m2, 2, generator=g)
+    c2 = torch.randn(B, C, m1, m2, 2, generator=g)
+    y = spectral_conv_ext.irfft2_corners(c1.to(cuda_device), c2.to(cuda_device), H, W).cpu().numpy()
+    full = np.zeros((B, C, H, W // 2 + 1), dtype=np.complex128)
+    full[:, :, :m1, :m2] = c1[..., 0].numpy() + 1j * c1[..., 1].numpy()
+    full[:, :, H - m1:, :m2] = c2[..., 0].numpy() + 1j * c2[..., 1].numpy()
+    ref = np.fft.irfft2(full, s=(H, W))
+    err = np.abs(y - ref).max() / np.abs(ref).max()
+    assert err <= 2e-5, err
+
+
 def test_zz_watchdog_clean(cuda_device):
     """No tensor-core kernel gave up on a wait during this session."""
     import _scx

@@ -410,5 +410,15 @@ __device__ __forceinline__ void tmem_ld_cols_nowait(uint32_t taddr, float* v) {
     }
 }
 
+
+// 3-D tiled TMA load (no multicast) of the box at (c0, c1, c2) of `tmap` into shared memory;
+// completion counted on `bar` in bytes.  c0 * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0, int c1, int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_u32(dst)), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
 }  // namespace tc
 }  // namespace scx

@@ -137,6 +137,32 @@ def test_spectral_mul_entry_points(cuda_device):
     assert_close(torch.view_as_real(ref).numpy(), torch.view_as_real(yc).numpy(), 1e-6)
 
 
+@pytest.mark.parametrize("shape", [
+    (1, 3, 5, 12, 12),    # B = 1, last output-channel split ragged
+    (20, 32, 36, 16, 16),  # Cout not a power of two
+    (2, 4, 6, 7, 3),      # odd mode count: per-thread loads instead of TMA boxes
+    (20, 32, 32, 12, 12),  # FNO layer
+    (3, 64, 64, 32, 32),  # wide channels, many modes
+])
+def test_dual_mix_shapes(shape, cuda_device):
+    """Both corners of the mode mixing against a complex128 einsum, with every output
+    element written (NaN-poisoned outputs)."""
+    import spectral_conv_ext
+
+    B, Cin, Cout, m1, m2 = shape
+    g = torch.Generator().manual_seed(sum(shape))
+    xs = [torch.randn(B, Cin, m1, m2, dtype=torch.cfloat, generator=g) for _ in range(2)]
+    ws = [torch.randn(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g) for _ in range(2)]
+    xd = [torch.view_as_real(t.to(cuda_device)).contiguous() for t in xs]
+    wd = [torch.view_as_real(t.to(cuda_device)).contiguous() for t in ws]
+    ys = [torch.full((B, Cout, m1, m2, 2), float("nan"), device=cuda_device) for _ in range(2)]
+    spectral_conv_ext.spectral_mul_dual_out(xd[0], wd[0], xd[1], wd[1], ys[0], ys[1])
+    for x, w, y in zip(xs, ws, ys):
+        ref = torch.einsum("bixy,ioxy->boxy", x.to(torch.complex128), w.to(torch.complex128))
+        assert torch.isfinite(y).all()
+        assert_close(torch.view_as_real(ref).numpy(), y.cpu().numpy(), 1e-5)
+
+
 def test_spectral_mul_autograd_grads(cuda_device):
     """spectral_conv_combo/test_backward.py:27-54 cases."""
     import spectral_conv_ops

@@ -5,7 +5,7 @@
 // For every plane x[h][w] (H, W in {64, 128}) and corner slots s < 2*m1 <= 32 (row
 // kx_s = s for corner 1, H - 2*m1 + s for corner 2), ky < m2 <= 32:
 //
-//   S2  column DFT on the tensor core, A = x^T straight from TMEM:
+//   S2  column DFT on the tensor core, A = x^T from TMEM (two buffers):
 //         D2[(g,w)][j] = sum_h x_g[h][w] * F[j][h]       lanes (g,w): G1 = 128/W planes
 //       F rows j = 32*grp + 16*cs + i hold cos (cs = 0) / sin (cs = 1) of 2 pi kx_s h / H
 //       for slot s = 16*grp + i.  Each plane is read once from HBM by the TMA engine, each
@@ -18,14 +18,16 @@
 //   E1  X[s][ky] = (Cc + Ss) + i (Cs - Sc) from the cos row (lane i) and the sin row
 //       (lane i + 16) of slot s, exchanged with one shuffle; written to the corner arrays.
 //
-// Every product is bf16x3 (hi*hi + hi*lo + lo*hi) accumulated in fp32 TMEM: S2 issues
-// MMA(x_hi, [F_hi; F_lo]) + MMA(x_lo, F_hi) per K step and S1 the same with CS and TW.
+// Every product is bf16x3 (hi*hi + hi*lo + lo*hi) accumulated in fp32 TMEM: S2 chains
+// x_hi*F_hi, x_hi*F_lo and x_lo*F_hi along K into one 64-column accumulator; S1 issues
+// MMA(CS_hi, [TW_hi; TW_lo]) + MMA(CS_lo, TW_hi) per K step.
 //
 // Warp roles (persistent, one CTA per SM, planes split into contiguous balanced ranges):
-//   warp 17      lane 0 streams 32-row chunks of x into a shared-memory ring with 1-D bulk
-//                copies (about 100 KB in flight per SM, which is what HBM needs here)
-//   warps 0..7   converters: ring -> bf16 hi/lo -> the TMEM A operand, whose two K halves
-//                are refilled independently
+//   warp 17      lane 0 brings the twiddle tables in with one bulk copy, then streams 32-row
+//                chunks of x into a shared-memory ring with 1-D bulk copies (about 100 KB in
+//                flight per SM, which is what HBM needs here)
+//   warps 0..7   converters: ring -> bf16 hi/lo in registers -> the TMEM A operand
+//                (double-buffered), stored only while no A-in-TMEM MMA is in flight
 //   warps 8..15  epilogue: E2 for every column tile (D2 double-buffered in TMEM), E1 for
 //                every 2-plane tile
 //   warp 16      lane 0 issues every MMA
@@ -69,8 +71,8 @@ struct FwdArgs {
 
 struct FwdBars {
     uint64_t full[kMaxSlots], empty[kMaxSlots];  // x ring
-    uint64_t aFull[2], aEmpty[2];                // per K half of the A operand
-    uint64_t d2Full[2], d2Empty[2], csFull, csEmpty, d1Full, d1Empty, drain;
+    uint64_t aFull[2], aEmpty[2];                // A operand buffers
+    uint64_t d2Full[2], d2Empty[2], csFull, csEmpty, d1Full, d1Empty, drain, tab;
 };
 
 template <int H, int W, int R2>
@@ -79,7 +81,6 @@ struct FwdCfg {
     static constexpr int CT = 2 / G1;   // column tiles per 2-plane tile
     static constexpr int N1 = 2 * R2;   // S1 columns per TW part (cos block | -sin block)
     static constexpr int CPC = H / kChunkRows;  // ring chunks per column tile
-    static constexpr int CPH = CPC / 2;         // ring chunks per K half
     static constexpr uint32_t PLANE_CHUNK = static_cast<uint32_t>(kChunkRows) * W * 4u;
     static constexpr uint32_t SLOT = PLANE_CHUNK * G1;  // 16 KB
     static constexpr uint32_t CSB = 128u * W * 2u;      // one CS operand (hi or lo), MN-major
@@ -94,9 +95,9 @@ struct FwdCfg {
                                   : kMaxSlots;
     static constexpr uint32_t SMEM = OFF_RING + static_cast<uint32_t>(NS) * SLOT + 1024u;
     static_assert(NS >= 3, "x ring too small");
-    // TMEM columns: A (hi: H/2 packed columns | lo: H/2) | D2 x 2 (2*kJF each) | D1 (2*N1)
-    static constexpr uint32_t COL_D2 = static_cast<uint32_t>(H);
-    static constexpr uint32_t COL_D1 = COL_D2 + 4u * kJF;
+    // TMEM columns: A x 2 (H each: hi H/2 packed columns | lo H/2) | D2 x 2 (kJF each) | D1 (2*N1)
+    static constexpr uint32_t COL_D2 = 2u * H;
+    static constexpr uint32_t COL_D1 = COL_D2 + 2u * kJF;
     static constexpr uint32_t COLS = COL_D1 + 2u * N1;
     static constexpr uint32_t TMEM_COLS = COLS <= 256 ? 256u : 512u;
     static_assert(COLS <= 512, "TMEM budget");
@@ -119,7 +120,6 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
     const int NC = (p1 - p0 + C::G1 - 1) / C::G1;  // column tiles
     const int NT = (NC + C::CT - 1) / C::CT;        // 2-plane tiles
 
-    tc::copy_table(base + C::OFF_FB, a.tab, a.tab_bytes);
     if (warp == 0) {
         tc::tmem_alloc(&tmem_base, C::TMEM_COLS);
         tc::tmem_relinquish();
@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         tc::mbar_init(&bars.d1Full, 1);
         tc::mbar_init(&bars.d1Empty, 1);
         tc::mbar_init(&bars.drain, 1);
+        tc::mbar_init(&bars.tab, 1);
     }
     tc::fence_async_smem();
     tc::fence_before_sync();
@@ -156,42 +157,48 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         const int l = q * 32 + lane, g = l / W, w = l % W;
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
         const uint8_t* ring = base + C::OFF_RING;
-        const int NK = NC * C::CPC;
         bool ok = true;
-        for (int k = 0; k < NK && ok; ++k) {
-            const int c = k / C::CPC, ch = k % C::CPC, half = ch / C::CPH;
-            const int slot = k % C::NS, use = k / C::NS;
-            // A column tile is written only after every MMA of the previous one has completed
-            // (both K halves).  Refilling K half 0 while the MMAs of half 1, with the row DFT
-            // of the previous tile queued behind them, were still running corrupted about 1%
-            // of the planes on B200, although the MMAs of half 0 had completed.
-            if (ch == 0)
-                ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.aEmpty[0], (c & 1) ^ 1) &&
-                                                 tc::mbar_wait_bounded(&bars.aEmpty[1], (c & 1) ^ 1));
-            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.full[slot], use & 1));
-            if (!ok) break;
-            tc::fence_after_sync();  // the TMEM stores below stay behind the aEmpty wait
+        for (int c = 0; c < NC && ok; ++c) {
+            const int ab = c & 1;
             const bool live = p0 + c * C::G1 + g < p1;  // warp-uniform
-            const float* src = reinterpret_cast<const float*>(ring + static_cast<uint32_t>(slot) * C::SLOT +
-                                                              static_cast<uint32_t>(g) * C::PLANE_CHUNK) +
-                               (16 * hf) * W + w;
-            float v[16];
+            // read and split the whole column tile while the previous tile's MMAs run
+            uint32_t hi[C::CPC][8], lo[C::CPC][8];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = live ? src[j * W] : 0.f;
-            uint32_t hi[8], lo[8];
+            for (int ch = 0; ch < C::CPC; ++ch) {
+                const int k = c * C::CPC + ch, slot = k % C::NS, use = k / C::NS;
+                if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.full[slot], use & 1));
+                if (ok) {
+                    const float* src = reinterpret_cast<const float*>(ring + static_cast<uint32_t>(slot) * C::SLOT +
+                                                                      static_cast<uint32_t>(g) * C::PLANE_CHUNK) +
+                                       (16 * hf) * W + w;
+                    float v[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) tc::split_pair(v[2 * j], v[2 * j + 1], hi[j], lo[j]);
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&bars.empty[slot]);
-            const uint32_t col = tmem + lane_addr + static_cast<uint32_t>((ch * kChunkRows + 16 * hf) / 2);
-            tc::tmem_st8(col, hi);
-            tc::tmem_st8(col + H / 2, lo);
-            if (ch % C::CPH == C::CPH - 1) {
-                tc::tmem_wait_st();
-                tc::fence_before_sync();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&bars.aFull[half]);
+                    for (int j = 0; j < 16; ++j) v[j] = live ? src[j * W] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) tc::split_pair(v[2 * j], v[2 * j + 1], hi[ch][j], lo[ch][j]);
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&bars.empty[slot]);
+                }
             }
+            // TMEM stores only once no MMA reading A is in flight: buffer ab was last read by
+            // column tile c - 2 and the other buffer by c - 1.  Stores issued while the A-in-TMEM
+            // MMAs of the previous tile were still running (other columns, other buffer)
+            // corrupted about 1% of the planes on B200, so the two never overlap.
+            if (ok)
+                ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.aEmpty[ab], ((c >> 1) & 1) ^ 1) &&
+                                                 (c == 0 || tc::mbar_wait_bounded(&bars.aEmpty[ab ^ 1], ((c - 1) >> 1) & 1)));
+            if (!ok) break;
+            tc::fence_after_sync();
+#pragma unroll
+            for (int ch = 0; ch < C::CPC; ++ch) {
+                const uint32_t col = tmem + lane_addr + static_cast<uint32_t>(ab * H + (ch * kChunkRows + 16 * hf) / 2);
+                tc::tmem_st8(col, hi[ch]);
+                tc::tmem_st8(col + H / 2, lo[ch]);
+            }
+            tc::tmem_wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars.aFull[ab]);
         }
         if (!ok && lane == 0) atomicExch(a.watchdog, 20);
     } else if (warp < kMmaWarp) {
@@ -215,14 +222,11 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
             uint8_t* cs_lo = cs_hi + C::CSB;
             const uint32_t row_off = static_cast<uint32_t>(w >> 3) * 2048u + static_cast<uint32_t>(pit) * 1024u +
                                      static_cast<uint32_t>(w & 7) * 128u;
-            const uint32_t d2 = tmem + lane_addr + C::COL_D2 + static_cast<uint32_t>(b) * (2u * kJF) + 32u * sub;
-            float v[32], u[32];
+            const uint32_t d2 = tmem + lane_addr + C::COL_D2 + static_cast<uint32_t>(b) * kJF + 32u * sub;
+            float v[32];
             tc::tmem_ld32_nowait(d2, v);
-            tc::tmem_ld32_nowait(d2 + kJF, u);
             tc::tmem_wait_ld();
             tc::fence_before_sync();
-#pragma unroll
-            for (int k = 0; k < 32; ++k) v[k] += u[k];
 #pragma unroll
             for (int c8 = 0; c8 < 4; ++c8) {
                 uint4 h4, l4;
@@ -296,10 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         const uint64_t dTW = tc::desc_sw128(sb + C::OFF_TW);
         const uint64_t dCShi = tc::desc_mn_sw128(sb, 1024u, 2048u);
         const uint64_t dCSlo = tc::desc_mn_sw128(sb + C::CSB, 1024u, 2048u);
-        constexpr uint32_t idA = tc::idesc_bf16(128, 2 * kJF), idB = tc::idesc_bf16(128, kJF);
+        constexpr uint32_t idA = tc::idesc_bf16(128, kJF);
         constexpr uint32_t idC = tc::idesc_bf16(128, 2 * N1) | tc::kIdescAMajorMN;
         constexpr uint32_t idD = tc::idesc_bf16(128, N1) | tc::kIdescAMajorMN;
-        constexpr int KH = H / 32;  // K steps per A half
         const uint32_t d1 = tmem + C::COL_D1;
 
         auto s1 = [&](int i) -> bool {
@@ -318,26 +321,27 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
             return true;
         };
 
-        bool ok = true;
+        bool ok = tc::mbar_wait_bounded(&bars.tab, 0);
         for (int c = 0; c < NC && ok; ++c) {
-            const int i = c / C::CT, ct = c % C::CT, b = c & 1;
-            const uint32_t d2 = tmem + C::COL_D2 + static_cast<uint32_t>(b) * (2u * kJF);
-            ok = tc::mbar_wait_bounded(&bars.d2Empty[b], ((c >> 1) & 1) ^ 1);
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-                if (ok) ok = tc::mbar_wait_bounded(&bars.aFull[hf], c & 1);
-                if (!ok) break;
-                tc::fence_after_sync();
-#pragma unroll
-                for (int kk = 0; kk < KH; ++kk) {
-                    const int ks = hf * KH + kk;
-                    const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * kFRows * 128u + (ks & 3) * 32u) >> 4;
-                    tc::mma_ts(d2, tmem + 8u * ks, dFB + bo, idA, ks > 0 ? 1u : 0u);
-                    tc::mma_ts(d2, tmem + H / 2 + 8u * ks, dFB + bo, idB, 1u);
-                }
-                tc::mma_commit(&bars.aEmpty[hf]);
-            }
+            const int i = c / C::CT, ct = c % C::CT, b = c & 1, ab = c & 1;
+            const uint32_t d2 = tmem + C::COL_D2 + static_cast<uint32_t>(b) * kJF;
+            ok = tc::mbar_wait_bounded(&bars.d2Empty[b], ((c >> 1) & 1) ^ 1) &&
+                 tc::mbar_wait_bounded(&bars.aFull[ab], (c >> 1) & 1);
             if (!ok) break;
+            tc::fence_after_sync();
+            // bf16x3 chained along K: x_hi * F_hi, x_hi * F_lo (rows 64..127), x_lo * F_hi
+            const uint32_t ah = tmem + static_cast<uint32_t>(ab * H), al = ah + H / 2;
+#pragma unroll
+            for (int part = 0; part < 3; ++part) {
+                const uint32_t a0 = part == 2 ? al : ah;
+                const uint32_t brow = part == 1 ? (kJF / 8) * 1024u : 0u;
+#pragma unroll
+                for (int ks = 0; ks < H / 16; ++ks) {
+                    const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * kFRows * 128u + brow + (ks & 3) * 32u) >> 4;
+                    tc::mma_ts(d2, a0 + 8u * ks, dFB + bo, idA, (part | ks) ? 1u : 0u);
+                }
+            }
+            tc::mma_commit(&bars.aEmpty[ab]);
             tc::mma_commit(&bars.d2Full[b]);
             if (ct == 0 && i > 0) ok = s1(i - 1);
         }
@@ -351,6 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         // 1-D bulk copies of 32-row chunks of each live plane of a column tile into the ring.
         uint8_t* ring = base + C::OFF_RING;
         const int NK = NC * C::CPC;
+        tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
+        tc::bulk_g2s(base + C::OFF_FB, a.tab, a.tab_bytes, &bars.tab);
         for (int k = 0; k < NK; ++k) {
             const int c = k / C::CPC, ch = k % C::CPC;
             const int slot = k % C::NS, use = k / C::NS;
@@ -445,6 +451,7 @@ template <int H, int W, int R2>
 cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
     using C = FwdCfg<H, W, R2>;
     static_assert(C::SMEM <= 227u * 1024u - 512u, "shared memory budget");
+    if (a.tab_bytes != C::FB_BYTES + C::TW_BYTES) return cudaErrorInvalidValue;
     auto kernel = dft_fwd_tc_kernel<H, W, R2>;
     int per_sm = 1;
     cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), C::SMEM, kThreads, &per_sm);

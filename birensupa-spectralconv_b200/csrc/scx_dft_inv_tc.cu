@@ -132,32 +132,44 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
         // K = s (cos) and 32 + s (sin).  Yr is MN-major (rows contiguous), so threads with
         // consecutive ky write consecutive bf16 values.
         const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
-        constexpr int PER = C::G4 * 32 * C::R2P;  // elements per group (slots padded to 32)
+        constexpr int PER = C::G4 * 32 * C::R2P;       // elements per group (slots padded to 32)
+        constexpr int NPT = PER / (kLoadWarps * 32);   // elements per thread
+        static_assert(PER % (kLoadWarps * 32) == 0, "loader split");
         bool ok = true;
         for (int t = 0; t < NG && ok; ++t) {
             const int yb = t & 1;
+            // all loads of the group in flight before anything waits on them
+            float2 v[NPT];
+#pragma unroll
+            for (int u = 0; u < NPT; ++u) {
+                const int e = tid + u * kLoadWarps * 32;
+                const int ky = e % C::R2P, rest = e / C::R2P;
+                const int s = rest % 32, p = rest / 32;
+                const int q = q0 + t * C::G4 + p;
+                v[u] = make_float2(0.f, 0.f);
+                if (q < q1 && s < S && ky < m2)
+                    v[u] = s < m1 ? __ldg(a.in1 + static_cast<long long>(q) * a.ips + static_cast<long long>(s) * a.irs + ky)
+                                  : __ldg(a.in2 + static_cast<long long>(q) * a.ips +
+                                          static_cast<long long>(s - m1) * a.irs + ky);
+            }
             ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.yEmpty[yb], ((t >> 1) & 1) ^ 1));
             if (!ok) break;
             uint8_t* yr_hi = base + C::OFF_YR + static_cast<uint32_t>(yb) * 2u * C::YRB;
             uint8_t* yr_lo = yr_hi + C::YRB;
-            for (int e = tid; e < PER; e += kLoadWarps * 32) {
+#pragma unroll
+            for (int u = 0; u < NPT; ++u) {
+                const int e = tid + u * kLoadWarps * 32;
                 const int ky = e % C::R2P, rest = e / C::R2P;
                 const int s = rest % 32, p = rest / 32;
-                const int q = q0 + t * C::G4 + p;
-                float2 v = make_float2(0.f, 0.f);
-                if (q < q1 && s < S && ky < m2)
-                    v = s < m1 ? __ldg(a.in1 + static_cast<long long>(q) * a.ips + static_cast<long long>(s) * a.irs + ky)
-                               : __ldg(a.in2 + static_cast<long long>(q) * a.ips +
-                                       static_cast<long long>(s - m1) * a.irs + ky);
                 const int mre = p * N1P + ky, mim = mre + C::R2P;
-                const float vals[4] = {v.x, -v.y, v.y, v.x};
+                const float vals[4] = {v[u].x, -v[u].y, v[u].y, v[u].x};
                 const int ms[4] = {mre, mre, mim, mim};
                 const int ks[4] = {s, 32 + s, s, 32 + s};
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int r = 0; r < 4; ++r) {
                     __nv_bfloat16 hi, lo;
-                    tc::split2(vals[u], hi, lo);
-                    const int m = ms[u], k = ks[u];
+                    tc::split2(vals[r], hi, lo);
+                    const int m = ms[r], k = ks[r];
                     const uint32_t off = static_cast<uint32_t>(k >> 3) * 2048u + static_cast<uint32_t>(m >> 6) * 1024u +
                                          static_cast<uint32_t>(k & 7) * 128u +
                                          (static_cast<uint32_t>(((m & 63) >> 3) ^ (k & 7)) << 4) +

@@ -375,7 +375,10 @@ def ours(args) -> None:
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
-        scx_dist.init("nccl", timeout_s=300)
+        # NCCL's version banner would land on stdout ahead of the one JSON line
+        if os.environ.get("NCCL_DEBUG", "VERSION").upper() == "VERSION":
+            os.environ["NCCL_DEBUG"] = "WARN"
+        scx_dist.init("nccl", timeout_s=300, device=device)
     warmup = max(3, args.warmup)
     res = run_spectral(args.workload, args.steps, warmup, device, world, rank, with_e2e=True,
                        with_breakdown=True, sampler_gpu=local_rank if rank == 0 else None)

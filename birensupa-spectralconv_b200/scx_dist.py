@@ -32,13 +32,15 @@ def env_rank() -> tuple[int, int, int]:
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
-def init(backend: str, timeout_s: float = 120.0) -> None:
+def init(backend: str, timeout_s: float = 120.0, device: torch.device | None = None) -> None:
     """Process group over 127.0.0.1 defaults with a bounded timeout, so that ranks
-    waiting on a missing peer end with an error instead of hanging."""
+    waiting on a missing peer end with an error instead of hanging.  ``device`` binds an
+    NCCL group to this rank's GPU."""
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     os.environ.setdefault("MASTER_PORT", "29531")
     if not dist.is_initialized():
-        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=timeout_s))
+        kwargs = {"device_id": device} if device is not None and device.type == "cuda" else {}
+        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=timeout_s), **kwargs)
 
 
 def gather_batch(local: torch.Tensor, batch: int, dst: int = 0) -> torch.Tensor | None:

@@ -2,6 +2,7 @@
 // Argument validation mirrors the TORCH_CHECKs of spectral_conv/spectral_conv_ext.cpp:26-31,
 // 123-245 and the launcher checks of spectral_conv_combo/spectral_conv_ext.su:98-101, but
 // reports cudaErrorInvalidValue instead of throwing.
+#include <algorithm>
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
@@ -47,16 +48,52 @@ bool ffma_forced() {
 namespace scx {
 
 cudaError_t dft_fwd(const float* x, float2* out1, float2* out2, long long out_plane_stride, int out_row_stride,
-                    int P, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream) {
-    if (!ffma_forced() && tc_fwd_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
-        return launch_dft_fwd_tc(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, stream);
+                    int P, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream, float* scratch,
+                    size_t scratch_bytes) {
+    if (!ffma_forced()) {
+        if (tc_fwd_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+            return launch_dft_fwd_tc(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, stream);
+        if (scratch != nullptr && tc_split_supported(H, W, m1, m2) && scratch_bytes >= split_scratch_bytes(P, H, W) &&
+            ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scratch)) & 15) == 0) {
+            // fold each plane into four half-size parity sub-planes, then one tensor-core
+            // forward per parity class writing its rows/columns of the two corners
+            const int Hs = H / 2, Ws = W / 2;
+            cudaError_t e = launch_fold(x, scratch, P, Hs, Ws, stream);
+            for (int q = 0; q < 4 && e == cudaSuccess; ++q) {
+                const TcSub sub{H, W, q >> 1, q & 1, m1, m2};
+                const long long off = static_cast<long long>(sub.a) * out_row_stride + sub.b;
+                e = launch_dft_fwd_tc(scratch + static_cast<size_t>(q) * P * Hs * Ws, out1 + off, out2 + off,
+                                      out_plane_stride, 2 * out_row_stride, P, Hs, Ws, m1 / 2, m2 / 2, stream, &sub);
+            }
+            return e;
+        }
+    }
     return launch_dft_fwd(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, tw, stream);
 }
 
 cudaError_t dft_inv(const float2* in1, const float2* in2, long long in_plane_stride, int in_row_stride, float* y,
-                    int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream) {
-    if (!ffma_forced() && tc_inv_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(y) & 3) == 0)
-        return launch_dft_inv_tc(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, stream);
+                    int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream, float* scratch,
+                    size_t scratch_bytes) {
+    if (!ffma_forced()) {
+        if (tc_inv_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(y) & 3) == 0)
+            return launch_dft_inv_tc(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, stream);
+        if (scratch != nullptr && tc_split_supported(H, W, m1, m2) && scratch_bytes >= split_scratch_bytes(Q, H, W) &&
+            ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(scratch)) & 15) == 0) {
+            // one tensor-core inverse per parity class of the spectrum into half-size
+            // sub-planes, then unfold them into the quadrants of y
+            const int Hs = H / 2, Ws = W / 2;
+            cudaError_t e = cudaSuccess;
+            for (int q = 0; q < 4 && e == cudaSuccess; ++q) {
+                const TcSub sub{H, W, q >> 1, q & 1, m1, m2};
+                const long long off = static_cast<long long>(sub.a) * in_row_stride + sub.b;
+                e = launch_dft_inv_tc(in1 + off, in2 + off, in_plane_stride, 2 * in_row_stride,
+                                      scratch + static_cast<size_t>(q) * Q * Hs * Ws, Q, Hs, Ws, m1 / 2, m2 / 2, stream,
+                                      &sub);
+            }
+            if (e == cudaSuccess) e = launch_unfold(scratch, y, Q, Hs, Ws, stream);
+            return e;
+        }
+    }
     return launch_dft_inv(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, tw, stream);
 }
 
@@ -176,7 +213,12 @@ size_t scx_spectral_conv2d_workspace_size(int batch_size, int channels_in, int c
         return 0;
     const size_t corner_in = static_cast<size_t>(batch_size) * channels_in * modes1 * modes2;
     const size_t corner_out = static_cast<size_t>(batch_size) * channels_out * modes1 * modes2;
-    return 2 * (corner_in + corner_out) * sizeof(float2);
+    size_t bytes = 2 * (corner_in + corner_out) * sizeof(float2);
+    // folded tensor-core path: one set of planes of the larger side, after the spectra
+    if (scx::tc_split_supported(height, width, modes1, modes2))
+        bytes += scx::split_scratch_bytes(static_cast<long long>(batch_size) * std::max(channels_in, channels_out),
+                                          height, width);
+    return bytes;
 }
 
 int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* weights2, float* y,
@@ -202,13 +244,17 @@ int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* 
     float2* Y1 = X2 + ci;
     float2* Y2 = Y1 + co;
     const long long NM = static_cast<long long>(modes1) * modes2;
-    e = scx::dft_fwd(x, X1, X2, NM, modes2, batch_size * channels_in, height, width, modes1, modes2, *tw, s);
+    float* scratch = reinterpret_cast<float*>(Y2 + co);  // present when the folded path applies
+    const size_t scratch_bytes = need - 2 * (ci + co) * sizeof(float2);
+    e = scx::dft_fwd(x, X1, X2, NM, modes2, batch_size * channels_in, height, width, modes1, modes2, *tw, s,
+                     scratch_bytes ? scratch : nullptr, scratch_bytes);
     if (e != cudaSuccess) return e;
     e = scx::launch_mix(X1, X2, reinterpret_cast<const float2*>(weights1),
                         reinterpret_cast<const float2*>(weights2), Y1, Y2, 2, batch_size, channels_in,
                         channels_out, static_cast<int>(NM), s);
     if (e != cudaSuccess) return e;
-    return scx::dft_inv(Y1, Y2, NM, modes2, y, batch_size * channels_out, height, width, modes1, modes2, *tw, s);
+    return scx::dft_inv(Y1, Y2, NM, modes2, y, batch_size * channels_out, height, width, modes1, modes2, *tw, s,
+                        scratch_bytes ? scratch : nullptr, scratch_bytes);
 }
 
 }  // extern "C"

@@ -63,6 +63,7 @@ struct FwdArgs {
     float2* out2;
     long long ops;  // output plane stride (float2 units)
     int ors;        // output row stride (float2 units)
+    int oks;        // output ky stride (float2 units): 2 for a parity sub-problem of a folded plane
     int P, m1, m2;
     const uint4* tab;  // [F_hi; F_lo] then [TW_hi; TW_lo], both K-major SW128
     uint32_t tab_bytes;
@@ -278,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
                 const float Cc = cs ? ra : uc0, Cs = cs ? rb : us0;
                 const float Sc = cs ? uc1 : ra, Ss = cs ? us1 : rb;
                 const int ky = sub * QR + (cs ? HQ + k : k);
-                if (valid && ky < m2) dst[ky] = make_float2(Cc + Ss, Cs - Sc);
+                if (valid && ky < m2) dst[static_cast<long long>(ky) * a.oks] = make_float2(Cc + Ss, Cs - Sc);
             }
             tc::named_sync(kBarEpi, kEpiThreads);
             if (etid == 0) tc::mbar_arrive(&bars.d1Empty);
@@ -388,14 +389,17 @@ struct FwdTable {
 };
 
 std::mutex g_mutex;
-std::map<std::tuple<int, int, int, int, int>, FwdTable> g_tables;
+std::map<std::tuple<int, int, int, int, int, int>, FwdTable> g_tables;
 
-// [F_hi; F_lo] (kFRows x H) followed by [TW_hi; TW_lo] (2*N1 x W), K-major SW128 bf16.
-cudaError_t get_fwd_table(int H, int W, int m1, int m2, const FwdTable** out) {
+// [F_hi; F_lo] (kFRows x H) followed by [TW_hi; TW_lo] (2*N1 x W), K-major SW128 bf16.  With a
+// sub-problem description the rows hold the modes of that parity of the folded plane
+// (spectrum row kx, column ky of the full Hp x Wp plane; see TcSub).
+cudaError_t get_fwd_table(int H, int W, int m1, int m2, const TcSub* sub, const FwdTable** out) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
-    const auto key = std::make_tuple(dev, H, W, m1, m2);
+    const int sub_code = sub ? 1 + sub->a * 2 + sub->b + 4 * (sub->m1_full + 64 * sub->period_h) : 0;
+    const auto key = std::make_tuple(dev, H, W, m1, m2, sub_code);
     std::lock_guard<std::mutex> lock(g_mutex);
     auto it = g_tables.find(key);
     if (it != g_tables.end()) {
@@ -407,9 +411,10 @@ cudaError_t get_fwd_table(int H, int W, int m1, int m2, const FwdTable** out) {
     for (int j = 0; j < kJF; ++j) {
         const int grp = j / 32, cs = (j / 16) & 1, s = 16 * grp + (j & 15);
         if (s >= S) continue;
-        const int kx = host::slot_row(s, H, m1);
+        const int kx = sub ? sub_row(*sub, s, m1) : host::slot_row(s, H, m1);
+        const int Hp = sub ? sub->period_h : H;
         for (int h = 0; h < H; ++h) {
-            const double t = host::ang(kx, h, H);
+            const double t = host::ang(kx, h, Hp);
             uint16_t hi, lo;
             host::bf16_split(cs ? std::sin(t) : std::cos(t), hi, lo);
             fb.set(j, h, hi);
@@ -419,7 +424,7 @@ cudaError_t get_fwd_table(int H, int W, int m1, int m2, const FwdTable** out) {
     host::KMajor tw(2 * N1, W);
     for (int n = 0; n < m2; ++n)
         for (int w = 0; w < W; ++w) {
-            const double t = host::ang(n, w, W);
+            const double t = sub ? host::ang(2 * n + sub->b, w, sub->period_w) : host::ang(n, w, W);
             uint16_t hi, lo;
             host::bf16_split(std::cos(t), hi, lo);
             tw.set(n, w, hi);
@@ -480,11 +485,11 @@ bool tc_fwd_supported(int H, int W, int m1, int m2) {
 }
 
 cudaError_t launch_dft_fwd_tc(const float* x, float2* out1, float2* out2, long long ops, int ors, int P, int H,
-                              int W, int m1, int m2, cudaStream_t stream) {
+                              int W, int m1, int m2, cudaStream_t stream, const TcSub* sub) {
     if (!tc_fwd_supported(H, W, m1, m2) || P <= 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
         return cudaErrorInvalidValue;
     const FwdTable* t = nullptr;
-    cudaError_t e = get_fwd_table(H, W, m1, m2, &t);
+    cudaError_t e = get_fwd_table(H, W, m1, m2, sub, &t);
     if (e != cudaSuccess) return e;
     int* wd = nullptr;
     e = device_watchdog(&wd);
@@ -495,6 +500,7 @@ cudaError_t launch_dft_fwd_tc(const float* x, float2* out1, float2* out2, long l
     a.out2 = out2;
     a.ops = ops;
     a.ors = ors;
+    a.oks = sub ? 2 : 1;
     a.P = P;
     a.m1 = m1;
     a.m2 = m2;

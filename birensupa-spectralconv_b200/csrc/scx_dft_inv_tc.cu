@@ -53,6 +53,7 @@ struct InvArgs {
     const float2* in2;
     long long ips;  // input plane stride (float2 units)
     int irs;        // input row stride (float2 units)
+    int iks;        // input ky stride (float2 units): 2 for a parity sub-problem of a folded plane
     float* y;
     int Q, m1, m2;
     const uint4* tab;  // G (hi, lo) then E (hi, lo)
@@ -148,9 +149,10 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
                 const int q = q0 + t * C::G4 + p;
                 v[u] = make_float2(0.f, 0.f);
                 if (q < q1 && s < S && ky < m2)
-                    v[u] = s < m1 ? __ldg(a.in1 + static_cast<long long>(q) * a.ips + static_cast<long long>(s) * a.irs + ky)
+                    v[u] = s < m1 ? __ldg(a.in1 + static_cast<long long>(q) * a.ips + static_cast<long long>(s) * a.irs +
+                                          static_cast<long long>(ky) * a.iks)
                                   : __ldg(a.in2 + static_cast<long long>(q) * a.ips +
-                                          static_cast<long long>(s - m1) * a.irs + ky);
+                                          static_cast<long long>(s - m1) * a.irs + static_cast<long long>(ky) * a.iks);
             }
             ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.yEmpty[yb], ((t >> 1) & 1) ^ 1));
             if (!ok) break;
@@ -340,14 +342,16 @@ struct InvTable {
 };
 
 std::mutex g_mutex;
-std::map<std::tuple<int, int, int, int, int>, InvTable> g_tables;
+std::map<std::tuple<int, int, int, int, int, int>, InvTable> g_tables;
 
-// G (H rows x 64, K-major) hi then lo, followed by E (128 rows x K5, K-major) hi then lo.
-cudaError_t get_inv_table(int H, int W, int m1, int m2, int N1P, const InvTable** out) {
+// G (H rows x 64, K-major) hi then lo, followed by E (128 rows x K5, K-major) hi then lo.  With
+// a sub-problem description they hold the modes of that parity of a folded plane (TcSub).
+cudaError_t get_inv_table(int H, int W, int m1, int m2, int N1P, const TcSub* sub, const InvTable** out) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
-    const auto key = std::make_tuple(dev, H, W, m1, m2);
+    const int sub_code = sub ? 1 + sub->a * 2 + sub->b + 4 * (sub->m1_full + 64 * sub->period_h) : 0;
+    const auto key = std::make_tuple(dev, H, W, m1, m2, sub_code);
     std::lock_guard<std::mutex> lock(g_mutex);
     auto it = g_tables.find(key);
     if (it != g_tables.end()) {
@@ -356,11 +360,13 @@ cudaError_t get_inv_table(int H, int W, int m1, int m2, int N1P, const InvTable*
     }
     const int S = 2 * m1, R2P = N1P / 2, G5 = 128 / W, K5 = G5 * N1P;
     host::KMajor ghi(H, kKg), glo(H, kKg);
+    const int Hp = sub ? sub->period_h : H, Wp = sub ? sub->period_w : W;
     for (int s = 0; s < S; ++s) {
-        const int kx = host::slot_row(s, H, m1);
-        if (s < m1 && kx >= H - m1) continue;  // overwritten by corner 2
+        const int kx = sub ? sub_row(*sub, s, m1) : host::slot_row(s, H, m1);
+        const int m1f = sub ? sub->m1_full : m1;
+        if (s < m1 && kx >= Hp - m1f) continue;  // corner-1 row that corner 2 overwrites
         for (int h = 0; h < H; ++h) {
-            const double t = host::ang(kx, h, H);
+            const double t = host::ang(kx, h, Hp);
             uint16_t hi, lo;
             host::bf16_split(std::cos(t), hi, lo);
             ghi.set(h, s, hi);
@@ -371,13 +377,14 @@ cudaError_t get_inv_table(int H, int W, int m1, int m2, int N1P, const InvTable*
         }
     }
     host::KMajor ehi(128, K5), elo(128, K5);
-    const double inv_hw = 1.0 / (static_cast<double>(H) * static_cast<double>(W));
+    const double inv_hw = 1.0 / (static_cast<double>(Hp) * static_cast<double>(Wp));
     for (int g = 0; g < G5; ++g)
         for (int w = 0; w < W; ++w)
             for (int ky = 0; ky < m2; ++ky) {
-                const bool single = (ky == 0) || ((W % 2 == 0) && (ky == W / 2));
+                const int kyf = sub ? 2 * ky + sub->b : ky;  // column of the full spectrum
+                const bool single = (kyf == 0) || ((Wp % 2 == 0) && (kyf == Wp / 2));
                 const double cw = (single ? 1.0 : 2.0) * inv_hw;
-                const double t = host::ang(ky, w, W);
+                const double t = host::ang(kyf, w, Wp);
                 uint16_t hi, lo;
                 host::bf16_split(cw * std::cos(t), hi, lo);
                 ehi.set(g * W + w, g * N1P + ky, hi);
@@ -431,12 +438,12 @@ bool tc_inv_supported(int H, int W, int m1, int m2) {
 }
 
 cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long ips, int irs, float* y, int Q, int H,
-                              int W, int m1, int m2, cudaStream_t stream) {
+                              int W, int m1, int m2, cudaStream_t stream, const TcSub* sub) {
     if (!tc_inv_supported(H, W, m1, m2) || Q <= 0 || (reinterpret_cast<uintptr_t>(y) & 3) != 0)
         return cudaErrorInvalidValue;
     const int N1P = m2 <= 16 ? 32 : 64;
     const InvTable* t = nullptr;
-    cudaError_t e = get_inv_table(H, W, m1, m2, N1P, &t);
+    cudaError_t e = get_inv_table(H, W, m1, m2, N1P, sub, &t);
     if (e != cudaSuccess) return e;
     int* wd = nullptr;
     e = device_watchdog(&wd);
@@ -446,6 +453,7 @@ cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long ip
     a.in2 = in2;
     a.ips = ips;
     a.irs = irs;
+    a.iks = sub ? 2 : 1;
     a.y = y;
     a.Q = Q;
     a.m1 = m1;

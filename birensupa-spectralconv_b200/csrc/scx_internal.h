@@ -60,23 +60,53 @@ cudaError_t launch_dft_inv(const float2* in1, const float2* in2,
                            float* y, int Q, int H, int W, int m1, int m2,
                            const Twiddles& tw, cudaStream_t stream);
 
+// A parity sub-problem of a folded plane.  A plane of Hp x Wp = 2H x 2W samples is folded
+// into four H x W planes q = 2a + b, sum over quadrants (alpha, beta) of
+// (-1)^(a alpha + b beta) x[h + H alpha][w + W beta]; the spectrum of sub-plane q against
+// the period-Hp / period-Wp twiddles is the full spectrum at the rows kx = a (mod 2) and the
+// columns ky = b (mod 2).  A sub-problem's m1 slots per corner are the full corner rows
+// 2t + a (t < m1_full / 2), and its m2 columns are ky = 2j + b.
+struct TcSub {
+    int period_h, period_w, a, b, m1_full, m2_full;
+};
+
+// Full-spectrum row of sub-problem slot s (m1s slots per corner).
+inline int sub_row(const TcSub& sp, int s, int m1s) {
+    const int corner = s < m1s ? 0 : 1, r = 2 * (s - corner * m1s) + sp.a;
+    return corner == 0 ? r : sp.period_h - sp.m1_full + r;
+}
+
 // Tensor-core (tcgen05) truncated DFT kernels for the shapes tc_fwd_supported /
 // tc_inv_supported accept.  Their operand tables are built per shape on first use
 // (cudaMalloc + synchronous copy, so the first call must not happen inside stream capture).
 bool tc_fwd_supported(int H, int W, int m1, int m2);
 bool tc_inv_supported(int H, int W, int m1, int m2);
+// With `sub`, the kernels run one parity sub-problem of folded planes: H, W, m1, m2 are the
+// sub-plane's, and the spectrum columns are read / written with a stride of 2.
 cudaError_t launch_dft_fwd_tc(const float* x, float2* out1, float2* out2, long long out_plane_stride,
-                              int out_row_stride, int P, int H, int W, int m1, int m2, cudaStream_t stream);
+                              int out_row_stride, int P, int H, int W, int m1, int m2, cudaStream_t stream,
+                              const TcSub* sub = nullptr);
 cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long in_plane_stride,
                               int in_row_stride, float* y, int Q, int H, int W, int m1, int m2,
-                              cudaStream_t stream);
+                              cudaStream_t stream, const TcSub* sub = nullptr);
+
+// Folded tensor-core path for 256 x 256 planes (even m1 <= 32, even m2 <= 64): fold, four
+// sub-problem DFTs, and on the inverse side four sub-problem DFTs then unfold.  `scratch`
+// holds P planes of floats (split_scratch_bytes).
+bool tc_split_supported(int H, int W, int m1, int m2);
+size_t split_scratch_bytes(long long P, int H, int W);
+cudaError_t launch_fold(const float* x, float* xs, int P, int Hs, int Ws, cudaStream_t stream);
+cudaError_t launch_unfold(const float* zs, float* y, int P, int Hs, int Ws, cudaStream_t stream);
 
 // Forward / inverse truncated DFT through the fastest kernel for the shape: the
 // tensor-core kernels where supported (unless SCX_VARIANT=ffma), else the FFMA kernels.
+// `scratch` (optional) enables the folded path for shapes that need it.
 cudaError_t dft_fwd(const float* x, float2* out1, float2* out2, long long out_plane_stride, int out_row_stride,
-                    int P, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream);
+                    int P, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream,
+                    float* scratch = nullptr, size_t scratch_bytes = 0);
 cudaError_t dft_inv(const float2* in1, const float2* in2, long long in_plane_stride, int in_row_stride, float* y,
-                    int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream);
+                    int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream,
+                    float* scratch = nullptr, size_t scratch_bytes = 0);
 
 // Device watchdog word of the current device (allocated and zeroed on first use, never
 // freed): the tensor-core kernels store a non-zero code there when they give up on a wait.

@@ -380,6 +380,25 @@ def test_inverse_corners_vs_f64(shape, cuda_device):
     assert err <= 2e-5, err
 
 
+@pytest.mark.parametrize("shape", [
+    (2, 3, 4, 256, 256, 8, 12),    # folded tensor-core path, small modes
+    (1, 2, 2, 256, 256, 32, 64),   # m1 = 32, m2 = 64: 16 slots and 32 columns per parity class
+    (2, 2, 3, 128, 128, 24, 20),   # 2*m1 > 32 at 128: folded into 64 x 64 sub-planes
+    (3, 4, 2, 256, 128, 16, 16),   # non-square folded plane
+])
+def test_folded_path_vs_f64_oracle(shape, cuda_device):
+    """Planes folded into four parity sub-planes (fused forward with its workspace)."""
+    B, Cin, Cout, H, W, m1, m2 = shape
+    g = torch.Generator().manual_seed(sum(shape) + 1)
+    x = torch.randn(B, Cin, H, W, generator=g)
+    scale = 1.0 / (Cin * Cout)
+    w1 = scale * torch.rand(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g)
+    w2 = scale * torch.rand(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g)
+    y = run_device(x, w1, w2, m1, m2, cuda_device).cpu().numpy()
+    ref = oracle.spectral_conv2d_f64(x.numpy(), w1.numpy(), w2.numpy(), m1, m2)
+    assert_close(ref, y)
+
+
 def test_zz_watchdog_clean(cuda_device):
     """No tensor-core kernel gave up on a wait during this session."""
     import _scx

@@ -98,7 +98,7 @@ __global__ void __launch_bounds__(kThreads) mix_smem_kernel(const MixArgs a) {
 
 struct MixTmaArgs {
     float2* y[2];
-    int B, Cin, Cout, NM, OC, TM;
+    int B, Cin, Cout, NM, OC, TM, BB, n_os;  // BB batch items per CTA; n_os output-channel splits
     uint32_t x_bytes, w_bytes, w_off;  // box bytes, byte offset of the weight tile
     int* watchdog;
 };
@@ -106,6 +106,7 @@ struct MixTmaArgs {
 // x_c viewed as [B][Cin][2*NM] floats, w_c as [Cin][Cout][2*NM]; boxes (2*TM, Cin, B) and
 // (2*TM, OC, Cin) land in shared memory in exactly the [B][Cin][TM] / [Cin][OC][TM] float2
 // order the accumulation loop reads (no swizzle).  Modes past NM read as zero.
+template <int TM>
 __global__ void __launch_bounds__(kThreads) mix_tma_kernel(const __grid_constant__ CUtensorMap tx0,
                                                            const __grid_constant__ CUtensorMap tx1,
                                                            const __grid_constant__ CUtensorMap tw0,
@@ -113,49 +114,56 @@ __global__ void __launch_bounds__(kThreads) mix_tma_kernel(const __grid_constant
                                                            const MixTmaArgs a) {
     extern __shared__ uint8_t mix_raw[];
     __shared__ uint64_t bar;
+    __shared__ int tiles_ok;
     uint8_t* base = tc::align1024(mix_raw);
     const int corner = blockIdx.y;
-    const int TM = a.TM;
     const int k0 = blockIdx.x * TM;
-    const int o_base = blockIdx.z * a.OC;
+    const int o_base = (blockIdx.z % a.n_os) * a.OC, b_base = (blockIdx.z / a.n_os) * a.BB;
     if (threadIdx.x == 0) {
         tc::mbar_init(&bar, 1);
         tc::fence_async_smem();
         tc::mbar_arrive_expect_tx(&bar, a.x_bytes + a.w_bytes);
-        tc::tma_load_3d(base, corner ? &tx1 : &tx0, 2 * k0, 0, 0, &bar);
+        tc::tma_load_3d(base, corner ? &tx1 : &tx0, 2 * k0, 0, b_base, &bar);
         tc::tma_load_3d(base + a.w_off, corner ? &tw1 : &tw0, 2 * k0, o_base, 0, &bar);
+        // one thread waits for the tiles while the others park at the barrier
+        tiles_ok = tc::mbar_wait_bounded(&bar, 0) ? 1 : 0;
+        if (!tiles_ok) atomicExch(a.watchdog, 40);
     }
     __syncthreads();
-    if (!tc::mbar_wait_bounded(&bar, 0)) {
-        if (threadIdx.x == 0) atomicExch(a.watchdog, 40);
-        return;
-    }
-    const float2* Xs = reinterpret_cast<const float2*>(base);            // [B][Cin][TM]
+    if (!tiles_ok) return;
+    const float2* Xs = reinterpret_cast<const float2*>(base);            // [BB][Cin][TM]
     const float2* Ws = reinterpret_cast<const float2*>(base + a.w_off);  // [Cin][OCs][TM]
-    const int B = a.B, Cin = a.Cin, OCs = a.OC, OC = min(a.OC, a.Cout - o_base);
+    const int BBs = a.BB, B = min(a.BB, a.B - b_base), Cin = a.Cin, OCs = a.OC, OC = min(a.OC, a.Cout - o_base);
     const int tm = min(TM, a.NM - k0);
     float2* __restrict__ Y = a.y[corner];
     const int nog = (OC + kOT - 1) / kOT;
     const int nbg = (B + kBT - 1) / kBT;
     const int ntiles = tm * nog * nbg;
+    const int wstride = OCs * TM;  // float2 between consecutive input channels of a weight column
     for (int t = threadIdx.x; t < ntiles; t += kThreads) {
         const int kk = t % tm;
         const int rest = t / tm;
         const int og = rest % nog, bg = rest / nog;
         const int o0 = og * kOT, b0 = bg * kBT;
+        // operand columns; rows past the staged tile are clamped (their products are never stored)
+        const float2* wp[kOT];
+        const float2* xp[kBT];
+#pragma unroll
+        for (int p = 0; p < kOT; ++p) wp[p] = Ws + min(o0 + p, OCs - 1) * TM + kk;
+#pragma unroll
+        for (int q = 0; q < kBT; ++q) xp[q] = Xs + static_cast<size_t>(min(b0 + q, BBs - 1)) * Cin * TM + kk;
         float2 acc[kOT][kBT];
 #pragma unroll
         for (int p = 0; p < kOT; ++p)
 #pragma unroll
             for (int q = 0; q < kBT; ++q) acc[p][q] = make_float2(0.f, 0.f);
+#pragma unroll 4
         for (int i = 0; i < Cin; ++i) {
             float2 wv[kOT], xv[kBT];
 #pragma unroll
-            for (int p = 0; p < kOT; ++p)
-                wv[p] = (o0 + p < OC) ? Ws[(i * OCs + o0 + p) * TM + kk] : make_float2(0.f, 0.f);
+            for (int p = 0; p < kOT; ++p) wv[p] = wp[p][i * wstride];
 #pragma unroll
-            for (int q = 0; q < kBT; ++q)
-                xv[q] = (b0 + q < B) ? Xs[((b0 + q) * Cin + i) * TM + kk] : make_float2(0.f, 0.f);
+            for (int q = 0; q < kBT; ++q) xv[q] = xp[q][i * TM];
 #pragma unroll
             for (int p = 0; p < kOT; ++p)
 #pragma unroll
@@ -169,7 +177,7 @@ __global__ void __launch_bounds__(kThreads) mix_tma_kernel(const __grid_constant
 #pragma unroll
             for (int q = 0; q < kBT; ++q)
                 if (o0 + p < OC && b0 + q < B)
-                    Y[(static_cast<size_t>(b0 + q) * a.Cout + o_base + o0 + p) * a.NM + k0 + kk] = acc[p][q];
+                    Y[(static_cast<size_t>(b_base + b0 + q) * a.Cout + o_base + o0 + p) * a.NM + k0 + kk] = acc[p][q];
     }
 }
 
@@ -217,12 +225,12 @@ cudaError_t launch_mix_tma(const float2* x1, const float2* x2, const float2* w1,
     const long long want = 2LL * num_sms();
     const int TM = (static_cast<long long>(ncorner) * (NM / 4) >= want) ? 4 : 2;
     const long long tiles = static_cast<long long>(ncorner) * ((NM + TM - 1) / TM);
-    int split = 1;
-    while (split < Cout && (tiles * split < want ||
-                            static_cast<long long>(Cin) * ((Cout + split - 1) / split) * TM * 8 > 64 * 1024))
-        split *= 2;
-    const int OC = (Cout + split - 1) / split;
-    if (OC > 256) return cudaErrorNotSupported;
+    int os = 1;
+    const int bs = 1;
+    while (os < Cout && (tiles * os < want || static_cast<long long>(Cin) * ((Cout + os - 1) / os) * TM * 8 > 64 * 1024))
+        os *= 2;
+    const int OC = (Cout + os - 1) / os, BB = (B + bs - 1) / bs;
+    if (OC > 256 || BB > 256) return cudaErrorNotSupported;
     MixTmaArgs a;
     a.y[0] = y1;
     a.y[1] = y2;
@@ -232,7 +240,10 @@ cudaError_t launch_mix_tma(const float2* x1, const float2* x2, const float2* w1,
     a.NM = NM;
     a.OC = OC;
     a.TM = TM;
-    a.x_bytes = static_cast<uint32_t>(B) * Cin * TM * 8u;
+    a.BB = BB;
+    a.n_os = (Cout + OC - 1) / OC;
+    const int n_bs = (B + BB - 1) / BB;
+    a.x_bytes = static_cast<uint32_t>(BB) * Cin * TM * 8u;
     a.w_bytes = static_cast<uint32_t>(Cin) * OC * TM * 8u;
     a.w_off = (a.x_bytes + 127u) / 128u * 128u;
     const size_t smem = a.w_off + a.w_bytes + 1024;
@@ -245,16 +256,19 @@ cudaError_t launch_mix_tma(const float2* x1, const float2* x2, const float2* w1,
     const float2* ws[2] = {w1, w2};
     for (int c = 0; c < 2; ++c) {
         const int src = c < nc ? c : 0;  // an unused second corner repeats the first map
-        if (!encode3d(&tx[c], xs[src], 2ull * NM, Cin, B, 2u * TM, Cin, B) ||
+        if (!encode3d(&tx[c], xs[src], 2ull * NM, Cin, B, 2u * TM, Cin, BB) ||
             !encode3d(&tw[c], ws[src], 2ull * NM, Cout, Cin, 2u * TM, OC, Cin))
             return cudaErrorNotSupported;
     }
     int per_sm = 1;
-    e = prepare_kernel(reinterpret_cast<const void*>(mix_tma_kernel), smem, kThreads, &per_sm);
-    if (e != cudaSuccess) return e;
-    const dim3 grid((NM + TM - 1) / TM, ncorner, (Cout + OC - 1) / OC);
-    mix_tma_kernel<<<grid, kThreads, smem, stream>>>(tx[0], tx[1], tw[0], tw[1], a);
-    return cudaGetLastError();
+    const dim3 grid((NM + TM - 1) / TM, ncorner, a.n_os * n_bs);
+    auto run = [&](auto kernel) -> cudaError_t {
+        cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), smem, kThreads, &per_sm);
+        if (err != cudaSuccess) return err;
+        kernel<<<grid, kThreads, smem, stream>>>(tx[0], tx[1], tw[0], tw[1], a);
+        return cudaGetLastError();
+    };
+    return TM == 4 ? run(mix_tma_kernel<4>) : run(mix_tma_kernel<2>);
 }
 
 }  // namespace

@@ -5,7 +5,7 @@
 // For every plane x[h][w] (H, W in {64, 128}) and corner slots s < 2*m1 <= 32 (row
 // kx_s = s for corner 1, H - 2*m1 + s for corner 2), ky < m2 <= 32:
 //
-//   S2  column DFT on the tensor core, A = x^T from TMEM (two buffers):
+//   S2  column DFT on the tensor core, A = x^T from TMEM:
 //         D2[(g,w)][j] = sum_h x_g[h][w] * F[j][h]       lanes (g,w): G1 = 128/W planes
 //       F rows j = 32*grp + 16*cs + i hold cos (cs = 0) / sin (cs = 1) of 2 pi kx_s h / H
 //       for slot s = 16*grp + i.  Each plane is read once from HBM by the TMA engine, each
@@ -18,19 +18,23 @@
 //   E1  X[s][ky] = (Cc + Ss) + i (Cs - Sc) from the cos row (lane i) and the sin row
 //       (lane i + 16) of slot s, exchanged with one shuffle; written to the corner arrays.
 //
-// Every product is bf16x3 (hi*hi + hi*lo + lo*hi) accumulated in fp32 TMEM: S2 chains
-// x_hi*F_hi, x_hi*F_lo and x_lo*F_hi along K into one 64-column accumulator; S1 issues
-// MMA(CS_hi, [TW_hi; TW_lo]) + MMA(CS_lo, TW_hi) per K step.
+// Every product is bf16x3 (hi*hi + hi*lo + lo*hi) accumulated in fp32 TMEM.  A tcgen05.mma
+// issued by one thread costs about 110 SM cycles whatever its N up to 128 (measured on B200),
+// while the tensor core finishes an M128 N64 K16 product in about 35 when several threads
+// issue, so S2 is split over two issuing warps with accumulators of their own, added by the
+// epilogue in a fixed order, and S1 has a third:
+//   S2P  x_hi * [F_hi; F_lo]  (N = 128)    S2Q  x_lo * F_hi  (N = 64)
+//   S1   CS_hi * [TW_hi; TW_lo] and CS_lo * TW_hi, both into D1, in that order per K step
 //
 // Warp roles (persistent, one CTA per SM, planes split into contiguous balanced ranges):
-//   warp 17      lane 0 brings the twiddle tables in with one bulk copy, then streams 32-row
-//                chunks of x into a shared-memory ring with 1-D bulk copies (about 100 KB in
-//                flight per SM, which is what HBM needs here)
-//   warps 0..7   converters: ring -> bf16 hi/lo in registers -> the TMEM A operand
-//                (double-buffered), stored only while no A-in-TMEM MMA is in flight
-//   warps 8..15  epilogue: E2 for every column tile (D2 double-buffered in TMEM), E1 for
-//                every 2-plane tile
-//   warp 16      lane 0 issues every MMA
+//   warp 19      lane 0 initialises the barriers, starts the table and the first ring loads
+//                before the setup barrier, then streams 32-row chunks of x into a shared-memory
+//                ring with 1-D bulk copies (about 100 KB in flight per SM)
+//   warps 0..7   converters: ring -> bf16 hi/lo in registers -> the TMEM A operand, stored
+//                only while no A-in-TMEM MMA is in flight (stores issued while such MMAs ran
+//                corrupted about 1% of the planes on B200, even into other columns)
+//   warps 8..15  epilogue: E2 for every column tile, E1 for every 2-plane tile
+//   warps 16..18 lane 0 of each issues the S2P, S2Q and S1 MMAs
 // All hand-offs are mbarriers; every wait is bounded (about a second): a role that gives up
 // stores a code in the device watchdog word and leaves its loop, so the kernel returns.
 #include <algorithm>
@@ -47,9 +51,9 @@ namespace {
 
 constexpr int kConvWarps = 8;                      // 2 per TMEM sub-partition
 constexpr int kEpiWarps = 8;                       // 2 per TMEM sub-partition
-constexpr int kMmaWarp = kConvWarps + kEpiWarps;   // 16
-constexpr int kTmaWarp = kMmaWarp + 1;             // 17
-constexpr int kThreads = (kTmaWarp + 1) * 32;      // 576
+constexpr int kMmaWarp = kConvWarps + kEpiWarps;   // 16..18: S2P, S2Q, S1
+constexpr int kTmaWarp = kMmaWarp + 3;             // 19
+constexpr int kThreads = (kTmaWarp + 1) * 32;      // 640
 constexpr int kBarEpi = 1;                         // named barrier of the epilogue warps
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kJF = 64;                            // column-DFT rows per plane (2 groups x 32)
@@ -72,8 +76,9 @@ struct FwdArgs {
 
 struct FwdBars {
     uint64_t full[kMaxSlots], empty[kMaxSlots];  // x ring
-    uint64_t aFull[2], aEmpty[2];                // A operand buffers
-    uint64_t d2Full[2], d2Empty[2], csFull, csEmpty, d1Full, d1Empty, drain, tab;
+    uint64_t aFull, aEmpty;                      // A operand (TMEM)
+    uint64_t d2Full, d2Empty, csFull, csEmpty, d1Full, d1Empty, tab;
+    uint64_t drain[3];
 };
 
 template <int H, int W, int R2>
@@ -96,9 +101,11 @@ struct FwdCfg {
                                   : kMaxSlots;
     static constexpr uint32_t SMEM = OFF_RING + static_cast<uint32_t>(NS) * SLOT + 1024u;
     static_assert(NS >= 3, "x ring too small");
-    // TMEM columns: A x 2 (H each: hi H/2 packed columns | lo H/2) | D2 x 2 (kJF each) | D1 (2*N1)
-    static constexpr uint32_t COL_D2 = 2u * H;
-    static constexpr uint32_t COL_D1 = COL_D2 + 2u * kJF;
+    // TMEM columns: A (H: hi H/2 packed columns | lo H/2) | D2P (kFRows: F_hi part | F_lo part)
+    // | D2Q (kJF) | D1 (2*N1: TW_hi part | TW_lo part)
+    static constexpr uint32_t COL_D2P = H;
+    static constexpr uint32_t COL_D2Q = COL_D2P + kFRows;
+    static constexpr uint32_t COL_D1 = COL_D2Q + kJF;
     static constexpr uint32_t COLS = COL_D1 + 2u * N1;
     static constexpr uint32_t TMEM_COLS = COLS <= 256 ? 256u : 512u;
     static_assert(COLS <= 512, "TMEM budget");
@@ -120,30 +127,46 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
     const int p1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * P / gridDim.x);
     const int NC = (p1 - p0 + C::G1 - 1) / C::G1;  // column tiles
     const int NT = (NC + C::CT - 1) / C::CT;        // 2-plane tiles
+    const int NK = NC * C::CPC;                     // ring chunks
+
+    // the producer's loads of chunk k: every live plane of its column tile
+    auto issue_chunk = [&](int k) {
+        const int c = k / C::CPC, ch = k % C::CPC, slot = k % C::NS;
+        const int pa = p0 + c * C::G1, np = min(C::G1, p1 - pa);
+        uint8_t* ring = base + C::OFF_RING;
+        tc::mbar_arrive_expect_tx(&bars.full[slot], static_cast<uint32_t>(np) * C::PLANE_CHUNK);
+        for (int g = 0; g < np; ++g)
+            tc::bulk_g2s(ring + static_cast<uint32_t>(slot) * C::SLOT + static_cast<uint32_t>(g) * C::PLANE_CHUNK,
+                         a.x + (static_cast<size_t>(pa + g) * H + ch * kChunkRows) * W, C::PLANE_CHUNK,
+                         &bars.full[slot]);
+    };
+    const int k_first = min(NK, C::NS);  // chunks issued before the setup barrier
 
     if (warp == 0) {
         tc::tmem_alloc(&tmem_base, C::TMEM_COLS);
         tc::tmem_relinquish();
     }
-    if (tid == 0) {
+    if (warp == kTmaWarp && lane == 0) {
         for (int i = 0; i < kMaxSlots; ++i) {
             tc::mbar_init(&bars.full[i], 1);
             tc::mbar_init(&bars.empty[i], kConvWarps);
         }
-        for (int i = 0; i < 2; ++i) {
-            tc::mbar_init(&bars.aFull[i], kConvWarps);
-            tc::mbar_init(&bars.aEmpty[i], 1);
-            tc::mbar_init(&bars.d2Full[i], 1);
-            tc::mbar_init(&bars.d2Empty[i], 1);
-        }
+        tc::mbar_init(&bars.aFull, kConvWarps);
+        tc::mbar_init(&bars.aEmpty, 2);
+        tc::mbar_init(&bars.d2Full, 2);
+        tc::mbar_init(&bars.d2Empty, 1);
         tc::mbar_init(&bars.csFull, 1);
         tc::mbar_init(&bars.csEmpty, 1);
         tc::mbar_init(&bars.d1Full, 1);
         tc::mbar_init(&bars.d1Empty, 1);
-        tc::mbar_init(&bars.drain, 1);
         tc::mbar_init(&bars.tab, 1);
+        for (int i = 0; i < 3; ++i) tc::mbar_init(&bars.drain[i], 1);
+        tc::fence_async_smem();
+        // the ring starts empty: the first NS chunks need no slot wait
+        for (int k = 0; k < k_first; ++k) issue_chunk(k);
+        tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
+        tc::bulk_g2s(base + C::OFF_FB, a.tab, a.tab_bytes, &bars.tab);
     }
-    tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -160,7 +183,6 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         const uint8_t* ring = base + C::OFF_RING;
         bool ok = true;
         for (int c = 0; c < NC && ok; ++c) {
-            const int ab = c & 1;
             const bool live = p0 + c * C::G1 + g < p1;  // warp-uniform
             // read and split the whole column tile while the previous tile's MMAs run
             uint32_t hi[C::CPC][8], lo[C::CPC][8];
@@ -181,25 +203,20 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
                     if (lane == 0) tc::mbar_arrive(&bars.empty[slot]);
                 }
             }
-            // TMEM stores only once no MMA reading A is in flight: buffer ab was last read by
-            // column tile c - 2 and the other buffer by c - 1.  Stores issued while the A-in-TMEM
-            // MMAs of the previous tile were still running (other columns, other buffer)
-            // corrupted about 1% of the planes on B200, so the two never overlap.
-            if (ok)
-                ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.aEmpty[ab], ((c >> 1) & 1) ^ 1) &&
-                                                 (c == 0 || tc::mbar_wait_bounded(&bars.aEmpty[ab ^ 1], ((c - 1) >> 1) & 1)));
+            // the S2 MMAs of tile c - 1 (both issuers) have completed
+            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.aEmpty, (c & 1) ^ 1));
             if (!ok) break;
             tc::fence_after_sync();
 #pragma unroll
             for (int ch = 0; ch < C::CPC; ++ch) {
-                const uint32_t col = tmem + lane_addr + static_cast<uint32_t>(ab * H + (ch * kChunkRows + 16 * hf) / 2);
+                const uint32_t col = tmem + lane_addr + static_cast<uint32_t>((ch * kChunkRows + 16 * hf) / 2);
                 tc::tmem_st8(col, hi[ch]);
                 tc::tmem_st8(col + H / 2, lo[ch]);
             }
             tc::tmem_wait_st();
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&bars.aFull[ab]);
+            if (lane == 0) tc::mbar_arrive(&bars.aFull);
         }
         if (!ok && lane == 0) atomicExch(a.watchdog, 20);
     } else if (warp < kMmaWarp) {
@@ -210,10 +227,11 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
         const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
 
-        // E2: D2 of column tile c -> CS operand rows of its planes (this warp: j in [32 sub, 32 sub + 32))
+        // E2: D2 of column tile c -> CS operand rows of its planes (this warp: j in [32 sub, 32 sub + 32)).
+        // D2[j] = P[j] + (P[64 + j] + Q[j]): x_hi F_hi, then the two correction products.
         auto e2 = [&](int c) -> bool {
-            const int i = c / C::CT, ct = c % C::CT, b = c & 1;
-            bool ok = tc::mbar_wait_bounded(&bars.d2Full[b], (c >> 1) & 1);
+            const int i = c / C::CT, ct = c % C::CT;
+            bool ok = tc::mbar_wait_bounded(&bars.d2Full, c & 1);
             if (ok && ct == 0) ok = tc::mbar_wait_bounded(&bars.csEmpty, (i & 1) ^ 1);
             if (tc::named_any(kBarEpi, kEpiThreads, !ok)) return false;
             tc::fence_after_sync();
@@ -223,23 +241,31 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
             uint8_t* cs_lo = cs_hi + C::CSB;
             const uint32_t row_off = static_cast<uint32_t>(w >> 3) * 2048u + static_cast<uint32_t>(pit) * 1024u +
                                      static_cast<uint32_t>(w & 7) * 128u;
-            const uint32_t d2 = tmem + lane_addr + C::COL_D2 + static_cast<uint32_t>(b) * kJF + 32u * sub;
-            float v[32];
-            tc::tmem_ld32_nowait(d2, v);
-            tc::tmem_wait_ld();
-            tc::fence_before_sync();
+            const uint32_t dp = tmem + lane_addr + C::COL_D2P + 32u * sub;
+            const uint32_t dq = tmem + lane_addr + C::COL_D2Q + 32u * sub;
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-                uint4 h4, l4;
-                tc::split8(v + 8 * c8, h4, l4);
-                const uint32_t off = row_off + (static_cast<uint32_t>((sub * 4 + c8) ^ (w & 7)) << 4);
-                *reinterpret_cast<uint4*>(cs_hi + off) = h4;
-                *reinterpret_cast<uint4*>(cs_lo + off) = l4;
+            for (int half = 0; half < 2; ++half) {
+                float ph[16], pl[16], pq[16];
+                tc::tmem_ld_cols_nowait<16>(dp + 16u * half, ph);
+                tc::tmem_ld_cols_nowait<16>(dp + kJF + 16u * half, pl);
+                tc::tmem_ld_cols_nowait<16>(dq + 16u * half, pq);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int k = 0; k < 16; ++k) ph[k] += pl[k] + pq[k];
+#pragma unroll
+                for (int c8 = 0; c8 < 2; ++c8) {
+                    uint4 h4, l4;
+                    tc::split8(ph + 8 * c8, h4, l4);
+                    const uint32_t off = row_off + (static_cast<uint32_t>((sub * 4 + half * 2 + c8) ^ (w & 7)) << 4);
+                    *reinterpret_cast<uint4*>(cs_hi + off) = h4;
+                    *reinterpret_cast<uint4*>(cs_lo + off) = l4;
+                }
             }
+            tc::fence_before_sync();
             tc::fence_async_smem();
             tc::named_sync(kBarEpi, kEpiThreads);
             if (etid == 0) {
-                tc::mbar_arrive(&bars.d2Empty[b]);
+                tc::mbar_arrive(&bars.d2Empty);
                 if (ct == C::CT - 1 || c == NC - 1) tc::mbar_arrive(&bars.csFull);
             }
             return true;
@@ -248,19 +274,28 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         // E1: D1 of tile i -> corner spectra.  Lane l holds CS row l: plane l / 64, slot
         // group (l / 32) % 2, cos (lanes 0..15) or sin (lanes 16..31) row of slot 16*group + lane%16.
         // Warp set `sub` finishes ky in [sub*QR, sub*QR + QR): the cos lane the first HQ of
-        // them, the sin lane the rest, after one exchange of partial sums.
+        // them, the sin lane the rest, after one exchange of partial sums.  Each TW product is
+        // the TW_hi part plus the TW_lo part.
         auto e1 = [&](int i) -> bool {
             constexpr int QR = R2 / 2, HQ = QR / 2;
             const bool ok = tc::mbar_wait_bounded(&bars.d1Full, i & 1);
             if (tc::named_any(kBarEpi, kEpiThreads, !ok)) return false;
             tc::fence_after_sync();
             const uint32_t d1 = tmem + lane_addr + C::COL_D1 + static_cast<uint32_t>(sub * QR);
-            float ch[QR], cl[QR], sh[QR], sl[QR];
-            tc::tmem_ld_cols_nowait<QR>(d1, ch);
-            tc::tmem_ld_cols_nowait<QR>(d1 + N1, cl);
-            tc::tmem_ld_cols_nowait<QR>(d1 + R2, sh);
-            tc::tmem_ld_cols_nowait<QR>(d1 + N1 + R2, sl);
-            tc::tmem_wait_ld();
+            float uc[QR], us[QR];
+            {
+                float t0[QR], t1[QR];
+                tc::tmem_ld_cols_nowait<QR>(d1, uc);
+                tc::tmem_ld_cols_nowait<QR>(d1 + N1, t0);
+                tc::tmem_ld_cols_nowait<QR>(d1 + R2, us);
+                tc::tmem_ld_cols_nowait<QR>(d1 + N1 + R2, t1);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int k = 0; k < QR; ++k) {
+                    uc[k] += t0[k];
+                    us[k] += t1[k];
+                }
+            }
             tc::fence_before_sync();
             const int pit = l >> 6, grp = (l >> 5) & 1, cs = lane >> 4, si = lane & 15;
             const int s = 16 * grp + si;
@@ -272,8 +307,8 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
                               : a.out2 + static_cast<long long>(p) * a.ops + static_cast<long long>(s - m1) * a.ors);
 #pragma unroll
             for (int k = 0; k < HQ; ++k) {
-                const float uc0 = ch[k] + cl[k], us0 = sh[k] + sl[k];
-                const float uc1 = ch[HQ + k] + cl[HQ + k], us1 = sh[HQ + k] + sl[HQ + k];
+                const float uc0 = uc[k], us0 = us[k];
+                const float uc1 = uc[HQ + k], us1 = us[HQ + k];
                 const float ra = __shfl_xor_sync(0xffffffffu, cs ? uc0 : uc1, 16);
                 const float rb = __shfl_xor_sync(0xffffffffu, cs ? us0 : us1, 16);
                 const float Cc = cs ? ra : uc0, Cs = cs ? rb : us0;
@@ -294,85 +329,69 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         }
         if (ok && NT > 0) ok = e1(NT - 1);
         if (!ok && etid == 0) atomicExch(a.watchdog, 21);
-    } else if (warp == kMmaWarp && lane == 0) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp < kTmaWarp && lane == 0) {
+        // ------------------------------------------------------------ MMA issuers
+        const int role = warp - kMmaWarp;  // 0 S2P, 1 S2Q, 2 S1
         const uint32_t sb = tc::smem_u32(base);
-        const uint64_t dFB = tc::desc_sw128(sb + C::OFF_FB);
-        const uint64_t dTW = tc::desc_sw128(sb + C::OFF_TW);
-        const uint64_t dCShi = tc::desc_mn_sw128(sb, 1024u, 2048u);
-        const uint64_t dCSlo = tc::desc_mn_sw128(sb + C::CSB, 1024u, 2048u);
-        constexpr uint32_t idA = tc::idesc_bf16(128, kJF);
-        constexpr uint32_t idC = tc::idesc_bf16(128, 2 * N1) | tc::kIdescAMajorMN;
-        constexpr uint32_t idD = tc::idesc_bf16(128, N1) | tc::kIdescAMajorMN;
-        const uint32_t d1 = tmem + C::COL_D1;
-
-        auto s1 = [&](int i) -> bool {
-            if (!tc::mbar_wait_bounded(&bars.csFull, i & 1)) return false;
-            if (!tc::mbar_wait_bounded(&bars.d1Empty, (i & 1) ^ 1)) return false;
-            tc::fence_after_sync();
-#pragma unroll
-            for (int ks = 0; ks < W / 16; ++ks) {
-                const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4;
-                const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * (2u * N1) * 128u + (ks & 3) * 32u) >> 4;
-                tc::mma_bf16(d1, dCShi + ao, dTW + bo, idC, ks > 0 ? 1u : 0u);
-                tc::mma_bf16(d1, dCSlo + ao, dTW + bo, idD, 1u);
-            }
-            tc::mma_commit(&bars.csEmpty);
-            tc::mma_commit(&bars.d1Full);
-            return true;
-        };
-
         bool ok = tc::mbar_wait_bounded(&bars.tab, 0);
-        for (int c = 0; c < NC && ok; ++c) {
-            const int i = c / C::CT, ct = c % C::CT, b = c & 1, ab = c & 1;
-            const uint32_t d2 = tmem + C::COL_D2 + static_cast<uint32_t>(b) * kJF;
-            ok = tc::mbar_wait_bounded(&bars.d2Empty[b], ((c >> 1) & 1) ^ 1) &&
-                 tc::mbar_wait_bounded(&bars.aFull[ab], (c >> 1) & 1);
-            if (!ok) break;
-            tc::fence_after_sync();
-            // bf16x3 chained along K: x_hi * F_hi, x_hi * F_lo (rows 64..127), x_lo * F_hi
-            const uint32_t ah = tmem + static_cast<uint32_t>(ab * H), al = ah + H / 2;
-#pragma unroll
-            for (int part = 0; part < 3; ++part) {
-                const uint32_t a0 = part == 2 ? al : ah;
-                const uint32_t brow = part == 1 ? (kJF / 8) * 1024u : 0u;
+        if (role < 2) {
+            // S2: column DFT of every column tile, A = x^T from TMEM (hi or lo half)
+            const uint64_t dFB = tc::desc_sw128(sb + C::OFF_FB);
+            const uint32_t id = role == 0 ? tc::idesc_bf16(128, kFRows) : tc::idesc_bf16(128, kJF);
+            const uint32_t d = tmem + (role == 0 ? C::COL_D2P : C::COL_D2Q);
+            const uint32_t a0 = tmem + (role == 0 ? 0u : static_cast<uint32_t>(H / 2));
+            for (int c = 0; c < NC && ok; ++c) {
+                ok = tc::mbar_wait_bounded(&bars.d2Empty, (c & 1) ^ 1) && tc::mbar_wait_bounded(&bars.aFull, c & 1);
+                if (!ok) break;
+                tc::fence_after_sync();
 #pragma unroll
                 for (int ks = 0; ks < H / 16; ++ks) {
-                    const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * kFRows * 128u + brow + (ks & 3) * 32u) >> 4;
-                    tc::mma_ts(d2, a0 + 8u * ks, dFB + bo, idA, (part | ks) ? 1u : 0u);
+                    const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * kFRows * 128u + (ks & 3) * 32u) >> 4;
+                    tc::mma_ts(d, a0 + 8u * ks, dFB + bo, id, ks > 0 ? 1u : 0u);
                 }
+                tc::mma_commit(&bars.aEmpty);
+                tc::mma_commit(&bars.d2Full);
             }
-            tc::mma_commit(&bars.aEmpty[ab]);
-            tc::mma_commit(&bars.d2Full[b]);
-            if (ct == 0 && i > 0) ok = s1(i - 1);
+        } else {
+            // S1: row DFT of every 2-plane tile, A = CS hi / lo from shared memory
+            const uint64_t dTW = tc::desc_sw128(sb + C::OFF_TW);
+            const uint64_t dCShi = tc::desc_mn_sw128(sb, 1024u, 2048u);
+            const uint64_t dCSlo = tc::desc_mn_sw128(sb + C::CSB, 1024u, 2048u);
+            constexpr uint32_t idC = tc::idesc_bf16(128, 2 * N1) | tc::kIdescAMajorMN;
+            constexpr uint32_t idD = tc::idesc_bf16(128, N1) | tc::kIdescAMajorMN;
+            const uint32_t d = tmem + C::COL_D1;
+            for (int i = 0; i < NT && ok; ++i) {
+                ok = tc::mbar_wait_bounded(&bars.csFull, i & 1) && tc::mbar_wait_bounded(&bars.d1Empty, (i & 1) ^ 1);
+                if (!ok) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int ks = 0; ks < W / 16; ++ks) {
+                    const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4;
+                    const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * (2u * N1) * 128u + (ks & 3) * 32u) >> 4;
+                    tc::mma_bf16(d, dCShi + ao, dTW + bo, idC, ks > 0 ? 1u : 0u);
+                    tc::mma_bf16(d, dCSlo + ao, dTW + bo, idD, 1u);
+                }
+                tc::mma_commit(&bars.csEmpty);
+                tc::mma_commit(&bars.d1Full);
+            }
         }
-        if (ok && NT > 0) ok = s1(NT - 1);
         if (!ok) atomicExch(a.watchdog, 22);
-        // every MMA issued above has completed before TMEM is released
-        tc::mma_commit(&bars.drain);
-        tc::mbar_wait_bounded(&bars.drain, 0);
+        // every MMA this thread issued has completed before TMEM is released
+        tc::mma_commit(&bars.drain[role]);
+        tc::mbar_wait_bounded(&bars.drain[role], 0);
     } else if (warp == kTmaWarp && lane == 0) {
         // ------------------------------------------------------------ TMA producer
-        // 1-D bulk copies of 32-row chunks of each live plane of a column tile into the ring.
-        uint8_t* ring = base + C::OFF_RING;
-        const int NK = NC * C::CPC;
-        tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
-        tc::bulk_g2s(base + C::OFF_FB, a.tab, a.tab_bytes, &bars.tab);
-        for (int k = 0; k < NK; ++k) {
-            const int c = k / C::CPC, ch = k % C::CPC;
+        for (int k = k_first; k < NK; ++k) {
             const int slot = k % C::NS, use = k / C::NS;
             if (!tc::mbar_wait_bounded(&bars.empty[slot], (use & 1) ^ 1)) {
                 atomicExch(a.watchdog, 23);
                 break;
             }
-            const int pa = p0 + c * C::G1, np = min(C::G1, p1 - pa);
-            tc::mbar_arrive_expect_tx(&bars.full[slot], static_cast<uint32_t>(np) * C::PLANE_CHUNK);
-            for (int g = 0; g < np; ++g)
-                tc::bulk_g2s(ring + static_cast<uint32_t>(slot) * C::SLOT + static_cast<uint32_t>(g) * C::PLANE_CHUNK,
-                             a.x + (static_cast<size_t>(pa + g) * H + ch * kChunkRows) * W, C::PLANE_CHUNK,
-                             &bars.full[slot]);
+            issue_chunk(k);
         }
     }
+    // lanes that skipped a single-lane role rejoin their warp before the CTA barrier
+    __syncwarp();
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) {

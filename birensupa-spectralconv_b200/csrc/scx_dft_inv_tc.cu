@@ -20,10 +20,13 @@
 //
 // Every product is bf16x3 (hi*hi + hi*lo + lo*hi) chained along K into one fp32
 // accumulator.  Warp roles (persistent, one CTA per SM, contiguous balanced plane ranges):
-//   warps 0..3   loaders: corner spectra -> Yr operand (MN-major, double-buffered)
+//   warps 0..3   loaders: corner spectra -> Yr operand (MN-major, double-buffered); the first
+//                group's loads are issued before the setup barrier
 //   warps 4..7   E4;  warps 8..15  E5 (two per TMEM sub-partition, halves of h)
-//   warp 16      lane 0 issues every MMA (and first brings the twiddle tables into shared
-//                memory with one bulk copy)
+//   warp 16      lane 0 brings the twiddle tables into shared memory with one bulk copy and
+//                issues the S4 MMAs
+//   warp 17      lane 0 issues the S5 MMAs.  A tcgen05.mma costs its issuing thread about
+//                110 SM cycles, so S4 of the next group runs while S5 chains are issued.
 // Every wait is bounded (about a second); a role that gives up stores a code in the
 // device watchdog word and leaves its loop.
 #include <algorithm>
@@ -43,8 +46,8 @@ constexpr int kE4Warps = 4;
 constexpr int kE5Warps = 8;
 constexpr int kE4Warp0 = kLoadWarps;             // 4
 constexpr int kE5Warp0 = kE4Warp0 + kE4Warps;    // 8
-constexpr int kMmaWarp = kE5Warp0 + kE5Warps;    // 16
-constexpr int kThreads = (kMmaWarp + 1) * 32;    // 544
+constexpr int kMmaWarp = kE5Warp0 + kE5Warps;    // 16 (S4), 17 (S5)
+constexpr int kThreads = (kMmaWarp + 2) * 32;    // 576
 constexpr int kBarE4 = 2, kBarE5 = 3;            // named barriers
 constexpr int kKg = 64;                          // S4 K: (cos|sin) x 32 slots
 
@@ -62,7 +65,7 @@ struct InvArgs {
 };
 
 struct InvBars {
-    uint64_t yFull[2], yEmpty[2], d4Full, d4Empty, zFull, zEmpty, d5Full[2], d5Empty[2], drain, tab;
+    uint64_t yFull[2], yEmpty[2], d4Full, d4Empty, zFull, zEmpty, d5Full[2], d5Empty[2], drain[2], tab;
 };
 
 template <int H, int W, int N1P>
@@ -103,6 +106,31 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
     const int q1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * Q / gridDim.x);
     const int NG = (q1 - q0 + C::G4 - 1) / C::G4;  // S4 groups
 
+    // loaders: the spectra of one group, 8 consecutive ky per unit, in registers
+    constexpr int kKB = C::R2P / 8;                                   // ky blocks per slot
+    constexpr int kUnitsPT = C::G4 * 32 * kKB / (kLoadWarps * 32);    // units per loader thread
+    static_assert(C::G4 * 32 * kKB % (kLoadWarps * 32) == 0, "loader split");
+    float2 v[kUnitsPT][8];
+    auto load_group = [&](int t) {
+        const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
+#pragma unroll
+        for (int u = 0; u < kUnitsPT; ++u) {
+            const int e = tid + u * kLoadWarps * 32;
+            const int kb = e % kKB, rest = e / kKB;
+            const int ss = rest % 32, p = rest / 32;
+            const int q = q0 + t * C::G4 + p;
+            const bool live = q < q1 && ss < S;
+            const float2* src = ss < m1 ? a.in1 + static_cast<long long>(q) * a.ips + static_cast<long long>(ss) * a.irs
+                                        : a.in2 + static_cast<long long>(q) * a.ips + static_cast<long long>(ss - m1) * a.irs;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int ky = kb * 8 + i;
+                v[u][i] = (live && ky < m2) ? __ldg(src + static_cast<long long>(ky) * a.iks) : make_float2(0.f, 0.f);
+            }
+        }
+    };
+    if (warp < kLoadWarps && NG > 0) load_group(0);  // in flight during the setup below
+
     if (warp == 0) {
         tc::tmem_alloc(&tmem_base, C::TMEM_COLS);
         tc::tmem_relinquish();
@@ -118,7 +146,8 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
         tc::mbar_init(&bars.d4Empty, 1);
         tc::mbar_init(&bars.zFull, 1);
         tc::mbar_init(&bars.zEmpty, 1);
-        tc::mbar_init(&bars.drain, 1);
+        tc::mbar_init(&bars.drain[0], 1);
+        tc::mbar_init(&bars.drain[1], 1);
         tc::mbar_init(&bars.tab, 1);
     }
     tc::fence_async_smem();
@@ -129,60 +158,45 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
 
     if (warp < kLoadWarps) {
         // ------------------------------------------------------------ loaders
-        // Element (p, s, ky) of a group feeds Yr rows (p, re, ky) and (p, im, ky) at
-        // K = s (cos) and 32 + s (sin).  Yr is MN-major (rows contiguous), so threads with
-        // consecutive ky write consecutive bf16 values.
-        const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
-        constexpr int PER = C::G4 * 32 * C::R2P;       // elements per group (slots padded to 32)
-        constexpr int NPT = PER / (kLoadWarps * 32);   // elements per thread
-        static_assert(PER % (kLoadWarps * 32) == 0, "loader split");
+        // Unit (p, s, kb) = 8 consecutive ky of slot s of group plane p feeds four 16-byte
+        // vectors of Yr (MN-major, rows contiguous): rows (p, re, ky) at K = s [Y_re] and
+        // K = 32 + s [-Y_im], rows (p, im, ky) at K = s [Y_im] and K = 32 + s [Y_re].
+        uint8_t* yr0 = base + C::OFF_YR;
         bool ok = true;
         for (int t = 0; t < NG && ok; ++t) {
             const int yb = t & 1;
-            // all loads of the group in flight before anything waits on them
-            float2 v[NPT];
-#pragma unroll
-            for (int u = 0; u < NPT; ++u) {
-                const int e = tid + u * kLoadWarps * 32;
-                const int ky = e % C::R2P, rest = e / C::R2P;
-                const int s = rest % 32, p = rest / 32;
-                const int q = q0 + t * C::G4 + p;
-                v[u] = make_float2(0.f, 0.f);
-                if (q < q1 && s < S && ky < m2)
-                    v[u] = s < m1 ? __ldg(a.in1 + static_cast<long long>(q) * a.ips + static_cast<long long>(s) * a.irs +
-                                          static_cast<long long>(ky) * a.iks)
-                                  : __ldg(a.in2 + static_cast<long long>(q) * a.ips +
-                                          static_cast<long long>(s - m1) * a.irs + static_cast<long long>(ky) * a.iks);
-            }
             ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.yEmpty[yb], ((t >> 1) & 1) ^ 1));
             if (!ok) break;
-            uint8_t* yr_hi = base + C::OFF_YR + static_cast<uint32_t>(yb) * 2u * C::YRB;
+            uint8_t* yr_hi = yr0 + static_cast<uint32_t>(yb) * 2u * C::YRB;
             uint8_t* yr_lo = yr_hi + C::YRB;
 #pragma unroll
-            for (int u = 0; u < NPT; ++u) {
+            for (int u = 0; u < kUnitsPT; ++u) {
                 const int e = tid + u * kLoadWarps * 32;
-                const int ky = e % C::R2P, rest = e / C::R2P;
-                const int s = rest % 32, p = rest / 32;
-                const int mre = p * N1P + ky, mim = mre + C::R2P;
-                const float vals[4] = {v[u].x, -v[u].y, v[u].y, v[u].x};
-                const int ms[4] = {mre, mre, mim, mim};
-                const int ks[4] = {s, 32 + s, s, 32 + s};
+                const int kb = e % kKB, rest = e / kKB;
+                const int ss = rest % 32, p = rest / 32;
+                uint32_t re_hi[4], re_lo[4], im_hi[4], im_lo[4];
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    __nv_bfloat16 hi, lo;
-                    tc::split2(vals[r], hi, lo);
-                    const int m = ms[r], k = ks[r];
+                for (int i = 0; i < 4; ++i) {
+                    tc::split_pair(v[u][2 * i].x, v[u][2 * i + 1].x, re_hi[i], re_lo[i]);
+                    tc::split_pair(v[u][2 * i].y, v[u][2 * i + 1].y, im_hi[i], im_lo[i]);
+                }
+                const int mre = p * N1P + kb * 8, mim = mre + C::R2P;
+                auto put = [&](int m, int k, const uint32_t* hi, const uint32_t* lo, uint32_t neg) {
                     const uint32_t off = static_cast<uint32_t>(k >> 3) * 2048u + static_cast<uint32_t>(m >> 6) * 1024u +
                                          static_cast<uint32_t>(k & 7) * 128u +
-                                         (static_cast<uint32_t>(((m & 63) >> 3) ^ (k & 7)) << 4) +
-                                         static_cast<uint32_t>(m & 7) * 2u;
-                    *reinterpret_cast<__nv_bfloat16*>(yr_hi + off) = hi;
-                    *reinterpret_cast<__nv_bfloat16*>(yr_lo + off) = lo;
-                }
+                                         (static_cast<uint32_t>(((m & 63) >> 3) ^ (k & 7)) << 4);
+                    *reinterpret_cast<uint4*>(yr_hi + off) = make_uint4(hi[0] ^ neg, hi[1] ^ neg, hi[2] ^ neg, hi[3] ^ neg);
+                    *reinterpret_cast<uint4*>(yr_lo + off) = make_uint4(lo[0] ^ neg, lo[1] ^ neg, lo[2] ^ neg, lo[3] ^ neg);
+                };
+                put(mre, ss, re_hi, re_lo, 0u);
+                put(mre, 32 + ss, im_hi, im_lo, 0x80008000u);  // -Y_im: bf16 sign bits
+                put(mim, ss, im_hi, im_lo, 0u);
+                put(mim, 32 + ss, re_hi, re_lo, 0u);
             }
             tc::fence_async_smem();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&bars.yFull[yb]);
+            if (t + 1 < NG) load_group(t + 1);
         }
         if (!ok && lane == 0) atomicExch(a.watchdog, 30);
     } else if (warp < kE5Warp0) {
@@ -267,65 +281,77 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
             }
         }
         if (!ok && e5tid == 0) atomicExch(a.watchdog, 32);
-    } else if (warp == kMmaWarp && lane == 0) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp >= kMmaWarp && lane == 0) {
+        // ------------------------------------------------------------ MMA issuers
+        const int role = warp - kMmaWarp;  // 0: S4 (and the table copy), 1: S5
         const uint32_t sb = tc::smem_u32(base);
-        tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
-        tc::bulk_g2s(base + C::OFF_G, a.tab, a.tab_bytes, &bars.tab);
-        constexpr uint32_t id4 = tc::idesc_bf16(128, H) | tc::kIdescAMajorMN;
-        constexpr uint32_t id5 = tc::idesc_bf16(128, H) | tc::kIdescBMajorMN;
-        const uint32_t d4 = tmem, d5 = tmem + C::COL_D5;
-        const uint64_t dG[2] = {tc::desc_sw128(sb + C::OFF_G), tc::desc_sw128(sb + C::OFF_G + C::GB)};
-        const uint64_t dE[2] = {tc::desc_sw128(sb + C::OFF_E), tc::desc_sw128(sb + C::OFF_E + C::EB)};
+        if (role == 0) {
+            tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
+            tc::bulk_g2s(base + C::OFF_G, a.tab, a.tab_bytes, &bars.tab);
+        }
         bool ok = tc::mbar_wait_bounded(&bars.tab, 0);
-        int n = 0;
-        for (int t = 0; t < NG && ok; ++t) {
-            const int yb = t & 1;
+        if (role == 0) {
             // S4: parts (Yr_hi, G_hi), (Yr_hi, G_lo), (Yr_lo, G_hi), K = 64 each
-            ok = tc::mbar_wait_bounded(&bars.yFull[yb], (t >> 1) & 1) && tc::mbar_wait_bounded(&bars.d4Empty, (t & 1) ^ 1);
-            if (!ok) break;
-            tc::fence_after_sync();
-            const uint32_t yr = sb + C::OFF_YR + static_cast<uint32_t>(yb) * 2u * C::YRB;
-            const uint64_t dY[2] = {tc::desc_mn_sw128(yr, 1024u, 2048u), tc::desc_mn_sw128(yr + C::YRB, 1024u, 2048u)};
-#pragma unroll
-            for (int part = 0; part < 3; ++part) {
-                const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
-#pragma unroll
-                for (int ks = 0; ks < kKg / 16; ++ks) {
-                    const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4, bo = (static_cast<uint32_t>(ks) * 32u) >> 4;
-                    tc::mma_bf16(d4, dY[ap] + ao, dG[bp] + bo, id4, (part | ks) ? 1u : 0u);
-                }
-            }
-            tc::mma_commit(&bars.yEmpty[yb]);
-            tc::mma_commit(&bars.d4Full);
-            // S5 chains of this group once E4 has written Z
-            for (int j = 0; j < C::NZ && ok; ++j, ++n) {
-                const int b = n & 1;
-                if (j == 0) ok = tc::mbar_wait_bounded(&bars.zFull, t & 1);
-                if (ok) ok = tc::mbar_wait_bounded(&bars.d5Empty[b], ((n >> 1) & 1) ^ 1);
+            constexpr uint32_t id4 = tc::idesc_bf16(128, H) | tc::kIdescAMajorMN;
+            const uint64_t dG[2] = {tc::desc_sw128(sb + C::OFF_G), tc::desc_sw128(sb + C::OFF_G + C::GB)};
+            for (int t = 0; t < NG && ok; ++t) {
+                const int yb = t & 1;
+                ok = tc::mbar_wait_bounded(&bars.yFull[yb], (t >> 1) & 1) &&
+                     tc::mbar_wait_bounded(&bars.d4Empty, (t & 1) ^ 1);
                 if (!ok) break;
                 tc::fence_after_sync();
-                const uint32_t zc = sb + C::OFF_Z + static_cast<uint32_t>(j) * 2u * C::ZB;
-                const uint64_t dZ[2] = {tc::desc_mn_sw128(zc, 1024u, C::ZSBO), tc::desc_mn_sw128(zc + C::ZB, 1024u, C::ZSBO)};
-                const uint32_t dd = d5 + static_cast<uint32_t>(b * H);
+                const uint32_t yr = sb + C::OFF_YR + static_cast<uint32_t>(yb) * 2u * C::YRB;
+                const uint64_t dY[2] = {tc::desc_mn_sw128(yr, 1024u, 2048u), tc::desc_mn_sw128(yr + C::YRB, 1024u, 2048u)};
 #pragma unroll
                 for (int part = 0; part < 3; ++part) {
                     const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
 #pragma unroll
-                    for (int ks = 0; ks < C::K5 / 16; ++ks) {
-                        const uint32_t ao = (static_cast<uint32_t>(ks >> 2) * 128u * 128u + (ks & 3) * 32u) >> 4;
-                        const uint32_t bo = (static_cast<uint32_t>(ks) * 2u * C::ZSBO) >> 4;
-                        tc::mma_bf16(dd, dE[ap] + ao, dZ[bp] + bo, id5, (part | ks) ? 1u : 0u);
+                    for (int ks = 0; ks < kKg / 16; ++ks) {
+                        const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4, bo = (static_cast<uint32_t>(ks) * 32u) >> 4;
+                        tc::mma_bf16(tmem, dY[ap] + ao, dG[bp] + bo, id4, (part | ks) ? 1u : 0u);
                     }
                 }
-                tc::mma_commit(&bars.d5Full[b]);
-                if (j == C::NZ - 1) tc::mma_commit(&bars.zEmpty);
+                tc::mma_commit(&bars.yEmpty[yb]);
+                tc::mma_commit(&bars.d4Full);
+            }
+        } else {
+            // S5 chains of each group once E4 has written its Z
+            constexpr uint32_t id5 = tc::idesc_bf16(128, H) | tc::kIdescBMajorMN;
+            const uint32_t d5 = tmem + C::COL_D5;
+            const uint64_t dE[2] = {tc::desc_sw128(sb + C::OFF_E), tc::desc_sw128(sb + C::OFF_E + C::EB)};
+            int n = 0;
+            for (int t = 0; t < NG && ok; ++t) {
+                for (int j = 0; j < C::NZ && ok; ++j, ++n) {
+                    const int b = n & 1;
+                    if (j == 0) ok = tc::mbar_wait_bounded(&bars.zFull, t & 1);
+                    if (ok) ok = tc::mbar_wait_bounded(&bars.d5Empty[b], ((n >> 1) & 1) ^ 1);
+                    if (!ok) break;
+                    tc::fence_after_sync();
+                    const uint32_t zc = sb + C::OFF_Z + static_cast<uint32_t>(j) * 2u * C::ZB;
+                    const uint64_t dZ[2] = {tc::desc_mn_sw128(zc, 1024u, C::ZSBO), tc::desc_mn_sw128(zc + C::ZB, 1024u, C::ZSBO)};
+                    const uint32_t dd = d5 + static_cast<uint32_t>(b * H);
+#pragma unroll
+                    for (int part = 0; part < 3; ++part) {
+                        const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
+#pragma unroll
+                        for (int ks = 0; ks < C::K5 / 16; ++ks) {
+                            const uint32_t ao = (static_cast<uint32_t>(ks >> 2) * 128u * 128u + (ks & 3) * 32u) >> 4;
+                            const uint32_t bo = (static_cast<uint32_t>(ks) * 2u * C::ZSBO) >> 4;
+                            tc::mma_bf16(dd, dE[ap] + ao, dZ[bp] + bo, id5, (part | ks) ? 1u : 0u);
+                        }
+                    }
+                    tc::mma_commit(&bars.d5Full[b]);
+                    if (j == C::NZ - 1) tc::mma_commit(&bars.zEmpty);
+                }
             }
         }
         if (!ok) atomicExch(a.watchdog, 33);
-        tc::mma_commit(&bars.drain);
-        tc::mbar_wait_bounded(&bars.drain, 0);
+        // every MMA this thread issued has completed before TMEM is released
+        tc::mma_commit(&bars.drain[role]);
+        tc::mbar_wait_bounded(&bars.drain[role], 0);
     }
+    // lanes that skipped a single-lane role rejoin their warp before the CTA barrier
+    __syncwarp();
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) {

@@ -55,14 +55,17 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
+// The thread may sleep in the instruction until the phase completes, for at most about
+// 20 us per call (the suspend-time hint, in ns); without the hint it returns after a short
+// system-dependent limit and a waiting warp spends issue slots on the retry loop.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
         : "memory");
     return ok != 0;
 }
@@ -271,19 +274,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
 
 // 8 floats -> one 16-byte unit of bf16 high parts and one of low parts.
 __device__ __forceinline__ void split8(const float* v, uint4& hi, uint4& lo) {
-    __nv_bfloat16 h[8], l[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) split2(v[i], h[i], l[i]);
-    uint32_t hw[4], lw[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        hw[i] = static_cast<uint32_t>(__bfloat16_as_ushort(h[2 * i])) |
-                (static_cast<uint32_t>(__bfloat16_as_ushort(h[2 * i + 1])) << 16);
-        lw[i] = static_cast<uint32_t>(__bfloat16_as_ushort(l[2 * i])) |
-                (static_cast<uint32_t>(__bfloat16_as_ushort(l[2 * i + 1])) << 16);
-    }
-    hi = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-    lo = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    split_pair(v[0], v[1], hi.x, lo.x);
+    split_pair(v[2], v[3], hi.y, lo.y);
+    split_pair(v[4], v[5], hi.z, lo.z);
+    split_pair(v[6], v[7], hi.w, lo.w);
 }
 
 

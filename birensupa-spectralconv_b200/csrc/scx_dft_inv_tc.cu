@@ -21,8 +21,11 @@
 // Every product is bf16x3 (hi*hi + hi*lo + lo*hi) chained along K into one fp32
 // accumulator.  Warp roles (persistent, one CTA per SM, contiguous balanced plane ranges):
 //   warps 0..3   loaders: corner spectra -> Yr operand (MN-major, double-buffered); the first
-//                group's loads are issued before the setup barrier
-//   warps 4..7   E4;  warps 8..15  E5 (two per TMEM sub-partition, halves of h)
+//                group's loads are issued before the setup barrier.  They also run E4 for the
+//                upper half of h.
+//   warps 4..7   E4 for the lower half of h; each warp hands its S5 chain's Z over alone, so
+//                the next group's E4 for a chain waits only for that chain's S5
+//   warps 8..15  E5 (two per TMEM sub-partition, halves of h)
 //   warp 16      lane 0 brings the twiddle tables into shared memory with one bulk copy and
 //                issues the S4 MMAs
 //   warp 17      lane 0 issues the S5 MMAs.  A tcgen05.mma costs its issuing thread about
@@ -48,7 +51,7 @@ constexpr int kE4Warp0 = kLoadWarps;             // 4
 constexpr int kE5Warp0 = kE4Warp0 + kE4Warps;    // 8
 constexpr int kMmaWarp = kE5Warp0 + kE5Warps;    // 16 (S4), 17 (S5)
 constexpr int kThreads = (kMmaWarp + 2) * 32;    // 576
-constexpr int kBarE4 = 2, kBarE5 = 3;            // named barriers
+constexpr int kBarE5 = 3;                        // named barrier of the E5 warps
 constexpr int kKg = 64;                          // S4 K: (cos|sin) x 32 slots
 
 struct InvArgs {
@@ -65,7 +68,7 @@ struct InvArgs {
 };
 
 struct InvBars {
-    uint64_t yFull[2], yEmpty[2], d4Full, d4Empty, zFull, zEmpty, d5Full[2], d5Empty[2], drain[2], tab;
+    uint64_t yFull[2], yEmpty[2], d4Full, d4Empty, zFull[4], zEmpty[4], d5Full[2], d5Empty[2], drain[2], tab;
 };
 
 template <int H, int W, int N1P>
@@ -74,6 +77,7 @@ struct InvCfg {
     static constexpr int G4 = 128 / N1P;           // planes per S4 group
     static constexpr int G5 = 128 / W;             // planes per S5 chain
     static constexpr int NZ = G4 / G5;             // S5 chains per group
+    static constexpr int WPC = G5 * N1P / 32;      // D4 warps per chain (per half of h)
     static constexpr int K5 = G5 * N1P;            // S5 K (block-diagonal for W = 64)
     static constexpr int K5P = (K5 + 63) / 64 * 64;                      // K-major rows span 64 K
     static constexpr uint32_t YRB = 128u * kKg * 2u;                     // one Yr part, MN-major
@@ -105,6 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
     const int q0 = static_cast<int>(static_cast<long long>(blockIdx.x) * Q / gridDim.x);
     const int q1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * Q / gridDim.x);
     const int NG = (q1 - q0 + C::G4 - 1) / C::G4;  // S4 groups
+    // S5 chains of group t holding a live plane (fewer than NZ only in a partial last group)
+    auto nz_live = [&](int t) { return min(C::NZ, (q1 - q0 - t * C::G4 + C::G5 - 1) / C::G5); };
 
     // loaders: the spectra of one group, 8 consecutive ky per unit, in registers
     constexpr int kKB = C::R2P / 8;                                   // ky blocks per slot
@@ -143,9 +149,11 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
             tc::mbar_init(&bars.d5Empty[i], 1);
         }
         tc::mbar_init(&bars.d4Full, 1);
-        tc::mbar_init(&bars.d4Empty, 1);
-        tc::mbar_init(&bars.zFull, 1);
-        tc::mbar_init(&bars.zEmpty, 1);
+        tc::mbar_init(&bars.d4Empty, 2 * kE4Warps);
+        for (int j = 0; j < 4; ++j) {
+            tc::mbar_init(&bars.zFull[j], 2 * C::WPC);
+            tc::mbar_init(&bars.zEmpty[j], 1);
+        }
         tc::mbar_init(&bars.drain[0], 1);
         tc::mbar_init(&bars.drain[1], 1);
         tc::mbar_init(&bars.tab, 1);
@@ -155,6 +163,50 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = tmem_base;
+
+    // E4 of group t by one warp for h in [h_lo, h_lo + H/2): D4 lanes 32q.. hold rows (p, c),
+    // written as K row kz of the Z operand of the plane's S5 chain.
+    auto e4 = [&](int t, int h_lo) -> bool {
+        const int q = warp & 3;
+        const int l = q * 32 + lane, p = l / N1P, c = l % N1P;
+        const int chain = p / C::G5, kz = (p % C::G5) * N1P + c;
+        const bool live = chain < nz_live(t);  // warp-uniform
+        bool ok = tc::mbar_wait_bounded(&bars.d4Full, t & 1);
+        if (ok && live) ok = tc::mbar_wait_bounded(&bars.zEmpty[chain], (t & 1) ^ 1);
+        if (!__all_sync(0xffffffffu, ok)) return false;
+        tc::fence_after_sync();
+        if (live) {
+            const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+            uint8_t* z_hi = base + C::OFF_Z + static_cast<uint32_t>(chain) * 2u * C::ZB;
+            uint8_t* z_lo = z_hi + C::ZB;
+            const uint32_t krow = static_cast<uint32_t>(kz >> 3) * C::ZSBO + static_cast<uint32_t>(kz & 7) * 128u;
+#pragma unroll
+            for (int hh = 0; hh < H / 2; hh += 32) {
+                const int h0 = h_lo + hh;
+                float v[32];
+                tc::tmem_ld32_nowait(tmem + lane_addr + static_cast<uint32_t>(h0), v);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int c8 = 0; c8 < 4; ++c8) {
+                    uint4 h4, l4;
+                    tc::split8(v + 8 * c8, h4, l4);
+                    const int hc = h0 + 8 * c8;  // first h of this 16-byte chunk
+                    const uint32_t off = krow + static_cast<uint32_t>(hc >> 6) * 1024u +
+                                         (static_cast<uint32_t>(((hc & 63) >> 3) ^ (kz & 7)) << 4);
+                    *reinterpret_cast<uint4*>(z_hi + off) = h4;
+                    *reinterpret_cast<uint4*>(z_lo + off) = l4;
+                }
+            }
+        }
+        tc::fence_before_sync();
+        tc::fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tc::mbar_arrive(&bars.d4Empty);
+            if (live) tc::mbar_arrive(&bars.zFull[chain]);
+        }
+        return true;
+    };
 
     if (warp < kLoadWarps) {
         // ------------------------------------------------------------ loaders
@@ -197,52 +249,14 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&bars.yFull[yb]);
             if (t + 1 < NG) load_group(t + 1);
+            ok = e4(t, H / 2);
         }
         if (!ok && lane == 0) atomicExch(a.watchdog, 30);
     } else if (warp < kE5Warp0) {
-        // ------------------------------------------------------------ E4
-        const int q = warp & 3;
-        const int e4tid = tid - kE4Warp0 * 32;  // 0..127
-        const int l = q * 32 + lane;            // D4 lane: (p, c)
-        const int p = l / N1P, c = l % N1P;
-        const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
-        const int chain = p / C::G5, kz = (p % C::G5) * N1P + c;  // Z chain and its K row
+        // ------------------------------------------------------------ E4 (lower half of h)
         bool ok = true;
-        for (int t = 0; t < NG; ++t) {
-            ok = tc::mbar_wait_bounded(&bars.d4Full, t & 1) && tc::mbar_wait_bounded(&bars.zEmpty, (t & 1) ^ 1);
-            if (tc::named_any(kBarE4, kE4Warps * 32, !ok)) {
-                ok = false;
-                break;
-            }
-            tc::fence_after_sync();
-            uint8_t* z_hi = base + C::OFF_Z + static_cast<uint32_t>(chain) * 2u * C::ZB;
-            uint8_t* z_lo = z_hi + C::ZB;
-            const uint32_t krow = static_cast<uint32_t>(kz >> 3) * C::ZSBO + static_cast<uint32_t>(kz & 7) * 128u;
-#pragma unroll
-            for (int h0 = 0; h0 < H; h0 += 32) {
-                float v[32];
-                tc::tmem_ld32_nowait(tmem + lane_addr + static_cast<uint32_t>(h0), v);
-                tc::tmem_wait_ld();
-#pragma unroll
-                for (int c8 = 0; c8 < 4; ++c8) {
-                    uint4 h4, l4;
-                    tc::split8(v + 8 * c8, h4, l4);
-                    const int hc = h0 + 8 * c8;  // first h of this 16-byte chunk
-                    const uint32_t off = krow + static_cast<uint32_t>(hc >> 6) * 1024u +
-                                         (static_cast<uint32_t>(((hc & 63) >> 3) ^ (kz & 7)) << 4);
-                    *reinterpret_cast<uint4*>(z_hi + off) = h4;
-                    *reinterpret_cast<uint4*>(z_lo + off) = l4;
-                }
-            }
-            tc::fence_before_sync();
-            tc::fence_async_smem();
-            tc::named_sync(kBarE4, kE4Warps * 32);
-            if (e4tid == 0) {
-                tc::mbar_arrive(&bars.d4Empty);
-                tc::mbar_arrive(&bars.zFull);
-            }
-        }
-        if (!ok && e4tid == 0) atomicExch(a.watchdog, 31);
+        for (int t = 0; t < NG && ok; ++t) ok = e4(t, 0);
+        if (!ok && lane == 0) atomicExch(a.watchdog, 31);
     } else if (warp < kMmaWarp) {
         // ------------------------------------------------------------ E5
         const int q = warp & 3, sub = (warp - kE5Warp0) >> 2;  // sub-partition, half of h
@@ -254,7 +268,8 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
         bool ok = true;
         int n = 0;  // S5 chains consumed
         for (int t = 0; t < NG && ok; ++t) {
-            for (int j = 0; j < C::NZ; ++j, ++n) {
+            const int nzl = nz_live(t);
+            for (int j = 0; j < nzl; ++j, ++n) {
                 const int b = n & 1;
                 ok = tc::mbar_wait_bounded(&bars.d5Full[b], (n >> 1) & 1);
                 if (tc::named_any(kBarE5, kE5Warps * 32, !ok)) {
@@ -321,10 +336,11 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
             const uint64_t dE[2] = {tc::desc_sw128(sb + C::OFF_E), tc::desc_sw128(sb + C::OFF_E + C::EB)};
             int n = 0;
             for (int t = 0; t < NG && ok; ++t) {
-                for (int j = 0; j < C::NZ && ok; ++j, ++n) {
+                const int nzl = nz_live(t);
+                for (int j = 0; j < nzl && ok; ++j, ++n) {
                     const int b = n & 1;
-                    if (j == 0) ok = tc::mbar_wait_bounded(&bars.zFull, t & 1);
-                    if (ok) ok = tc::mbar_wait_bounded(&bars.d5Empty[b], ((n >> 1) & 1) ^ 1);
+                    ok = tc::mbar_wait_bounded(&bars.zFull[j], t & 1) &&
+                         tc::mbar_wait_bounded(&bars.d5Empty[b], ((n >> 1) & 1) ^ 1);
                     if (!ok) break;
                     tc::fence_after_sync();
                     const uint32_t zc = sb + C::OFF_Z + static_cast<uint32_t>(j) * 2u * C::ZB;
@@ -341,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
                         }
                     }
                     tc::mma_commit(&bars.d5Full[b]);
-                    if (j == C::NZ - 1) tc::mma_commit(&bars.zEmpty);
+                    tc::mma_commit(&bars.zEmpty[j]);
                 }
             }
         }

@@ -3,17 +3,20 @@
 //
 //   y_c[b][o][k] = sum_i x_c[b][i][k] * w_c[i][o][k]      c in {1, 2}, k over m1*m2 modes
 //
-// mix_tma_kernel (mode counts that are even, 16-byte aligned operands): one CTA owns one
-// corner, a tile of TM consecutive modes and a range of output channels.  One 3-D TMA
-// load brings x_c[:, :, tile] (every batch item and input channel) and one brings
-// w_c[:, o-range, tile] into shared memory - no per-thread global loads, every weight
-// byte read once per CTA - then each thread accumulates a 2 (output channels) x 4 (batch
-// items) block of complex outputs per mode.  mix_smem_kernel is the same contraction with
-// per-thread loads, for the shapes the TMA boxes cannot describe.  Both corners run in
-// one launch on the caller's stream (the reference launched them serially on the null
-// stream).
+// mix_ring_kernel (mode counts that are even, 16-byte aligned operands, at least 8 input
+// channels): one CTA owns one corner, a tile of 16 consecutive modes (128-byte rows), a
+// block of batch items and a block of output channels.  Input channels stream in chunks of
+// 8 through a ring of 3-D TMA loads (x_c[b-block, chunk, tile] and w_c[chunk, o-block,
+// tile]) consumed by KS groups of warps in turn (split K, for enough warps per SM at small
+// sizes); each thread keeps a BT x OT block of complex accumulators for one mode, and the
+// stores of a half-warp cover one 128-byte line of y.  mix_smem_kernel is the same contraction with
+// per-thread loads, for the shapes the TMA boxes cannot describe.  Both corners run in one
+// launch on the caller's stream (the reference launched them serially on the null stream).
 #include <algorithm>
+#include <cmath>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include <cuda.h>
 
@@ -96,89 +99,132 @@ __global__ void __launch_bounds__(kThreads) mix_smem_kernel(const MixArgs a) {
 }
 
 
-struct MixTmaArgs {
+constexpr int kRingTM = 16;        // modes per tile: every staged row is one 128-byte line
+constexpr int kRingIC = 8;         // input channels per ring chunk
+constexpr int kRingMaxStages = 4;
+
+struct MixRingArgs {
     float2* y[2];
-    int B, Cin, Cout, NM, OC, TM, BB, n_os;  // BB batch items per CTA; n_os output-channel splits
-    uint32_t x_bytes, w_bytes, w_off;  // box bytes, byte offset of the weight tile
+    int B, Cin, Cout, NM;
+    int NCH, NS, n_os;  // channel chunks, ring stages, output-channel blocks
+    uint32_t stage_bytes;
     int* watchdog;
 };
 
-// x_c viewed as [B][Cin][2*NM] floats, w_c as [Cin][Cout][2*NM]; boxes (2*TM, Cin, B) and
-// (2*TM, OC, Cin) land in shared memory in exactly the [B][Cin][TM] / [Cin][OC][TM] float2
-// order the accumulation loop reads (no swizzle).  Modes past NM read as zero.
-template <int TM>
-__global__ void __launch_bounds__(kThreads) mix_tma_kernel(const __grid_constant__ CUtensorMap tx0,
-                                                           const __grid_constant__ CUtensorMap tx1,
-                                                           const __grid_constant__ CUtensorMap tw0,
-                                                           const __grid_constant__ CUtensorMap tw1,
-                                                           const MixTmaArgs a) {
+// x_c viewed as [B][Cin][2*NM] floats, w_c as [Cin][Cout][2*NM].  Chunk c of the ring holds
+// x_c[b-block, 8c.., tile] as [BB][8][16] float2 and w_c[8c.., o-block, tile] as [8][OC][16]
+// float2 (TMA boxes (32, 8, BB) and (32, OC, 8), zero-filled past the tensor edges, so a
+// partial tile, batch block or channel chunk contributes nothing).  The CTA's KS groups of
+// warps take every KS-th chunk (the ring depth is a multiple of KS, so a group refills its
+// own slots); within a group, thread (g, mode k) keeps BT batch items x OT output channels,
+// and the two half-warps share their batch items, so an x read is one broadcast line.  The
+// groups' partial sums are added in group order at the end.
+template <int BT, int OT, int NBQ, int NOQ, int KS>
+__global__ void __launch_bounds__(16 * NBQ * NOQ * KS) mix_ring_kernel(const __grid_constant__ CUtensorMap tx0,
+                                                                       const __grid_constant__ CUtensorMap tx1,
+                                                                       const __grid_constant__ CUtensorMap tw0,
+                                                                       const __grid_constant__ CUtensorMap tw1,
+                                                                       const MixRingArgs a) {
+    constexpr int BB = BT * NBQ, OC = OT * NOQ, IC = kRingIC, GT = 16 * NBQ * NOQ;
+    constexpr uint32_t XB = static_cast<uint32_t>(BB) * IC * kRingTM * 8u;
     extern __shared__ uint8_t mix_raw[];
-    __shared__ uint64_t bar;
-    __shared__ int tiles_ok;
+    __shared__ uint64_t full[kRingMaxStages];
+    __shared__ int failed;
     uint8_t* base = tc::align1024(mix_raw);
     const int corner = blockIdx.y;
-    const int k0 = blockIdx.x * TM;
-    const int o_base = (blockIdx.z % a.n_os) * a.OC, b_base = (blockIdx.z / a.n_os) * a.BB;
+    const int k0 = blockIdx.x * kRingTM;
+    const int o_base = (blockIdx.z % a.n_os) * OC, b_base = (blockIdx.z / a.n_os) * BB;
+    const CUtensorMap* mx = corner ? &tx1 : &tx0;
+    const CUtensorMap* mw = corner ? &tw1 : &tw0;
+    const int NS = a.NS, NCH = a.NCH;
+    auto issue = [&](int c) {
+        uint8_t* st = base + static_cast<uint32_t>(c % NS) * a.stage_bytes;
+        uint64_t* bar = &full[c % NS];
+        tc::mbar_arrive_expect_tx(bar, a.stage_bytes);
+        tc::tma_load_3d(st, mx, 2 * k0, c * IC, b_base, bar);
+        tc::tma_load_3d(st + XB, mw, 2 * k0, o_base, c * IC, bar);
+    };
     if (threadIdx.x == 0) {
-        tc::mbar_init(&bar, 1);
+        for (int i = 0; i < kRingMaxStages; ++i) tc::mbar_init(&full[i], 1);
         tc::fence_async_smem();
-        tc::mbar_arrive_expect_tx(&bar, a.x_bytes + a.w_bytes);
-        tc::tma_load_3d(base, corner ? &tx1 : &tx0, 2 * k0, 0, b_base, &bar);
-        tc::tma_load_3d(base + a.w_off, corner ? &tw1 : &tw0, 2 * k0, o_base, 0, &bar);
-        // one thread waits for the tiles while the others park at the barrier
-        tiles_ok = tc::mbar_wait_bounded(&bar, 0) ? 1 : 0;
-        if (!tiles_ok) atomicExch(a.watchdog, 40);
+        for (int c = 0; c < min(NS, NCH); ++c) issue(c);
+        failed = 0;
     }
     __syncthreads();
-    if (!tiles_ok) return;
-    const float2* Xs = reinterpret_cast<const float2*>(base);            // [BB][Cin][TM]
-    const float2* Ws = reinterpret_cast<const float2*>(base + a.w_off);  // [Cin][OCs][TM]
-    const int BBs = a.BB, B = min(a.BB, a.B - b_base), Cin = a.Cin, OCs = a.OC, OC = min(a.OC, a.Cout - o_base);
-    const int tm = min(TM, a.NM - k0);
-    float2* __restrict__ Y = a.y[corner];
-    const int nog = (OC + kOT - 1) / kOT;
-    const int nbg = (B + kBT - 1) / kBT;
-    const int ntiles = tm * nog * nbg;
-    const int wstride = OCs * TM;  // float2 between consecutive input channels of a weight column
-    for (int t = threadIdx.x; t < ntiles; t += kThreads) {
-        const int kk = t % tm;
-        const int rest = t / tm;
-        const int og = rest % nog, bg = rest / nog;
-        const int o0 = og * kOT, b0 = bg * kBT;
-        // operand columns; rows past the staged tile are clamped (their products are never stored)
-        const float2* wp[kOT];
-        const float2* xp[kBT];
+
+    const int kg = threadIdx.x / GT, gt = threadIdx.x % GT;
+    const int k = gt & (kRingTM - 1), g = gt >> 4;
+    const int oq = g % NOQ, bq = g / NOQ;
+    float2 acc[BT][OT];
 #pragma unroll
-        for (int p = 0; p < kOT; ++p) wp[p] = Ws + min(o0 + p, OCs - 1) * TM + kk;
+    for (int q = 0; q < BT; ++q)
 #pragma unroll
-        for (int q = 0; q < kBT; ++q) xp[q] = Xs + static_cast<size_t>(min(b0 + q, BBs - 1)) * Cin * TM + kk;
-        float2 acc[kOT][kBT];
+        for (int p = 0; p < OT; ++p) acc[q][p] = make_float2(0.f, 0.f);
+    for (int c = kg; c < NCH; c += KS) {
+        const int slot = c % NS;
+        const bool ok = tc::mbar_wait_bounded(&full[slot], (c / NS) & 1);
+        if (tc::named_any(1 + kg, GT, !ok)) {
+            if (gt == 0) failed = 1;
+            break;
+        }
+        const float2* xp = reinterpret_cast<const float2*>(base + static_cast<uint32_t>(slot) * a.stage_bytes) +
+                           bq * BT * IC * kRingTM + k;
+        const float2* wp = reinterpret_cast<const float2*>(base + static_cast<uint32_t>(slot) * a.stage_bytes + XB) +
+                           oq * OT * kRingTM + k;
 #pragma unroll
-        for (int p = 0; p < kOT; ++p)
+        for (int i = 0; i < IC; ++i) {
+            float2 xv[BT], wv[OT];
 #pragma unroll
-            for (int q = 0; q < kBT; ++q) acc[p][q] = make_float2(0.f, 0.f);
-#pragma unroll 4
-        for (int i = 0; i < Cin; ++i) {
-            float2 wv[kOT], xv[kBT];
+            for (int q = 0; q < BT; ++q) xv[q] = xp[(q * IC + i) * kRingTM];
 #pragma unroll
-            for (int p = 0; p < kOT; ++p) wv[p] = wp[p][i * wstride];
+            for (int p = 0; p < OT; ++p) wv[p] = wp[(i * OC + p) * kRingTM];
 #pragma unroll
-            for (int q = 0; q < kBT; ++q) xv[q] = xp[q][i * TM];
+            for (int q = 0; q < BT; ++q)
 #pragma unroll
-            for (int p = 0; p < kOT; ++p)
-#pragma unroll
-                for (int q = 0; q < kBT; ++q) {
-                    acc[p][q].x = fmaf(xv[q].x, wv[p].x, fmaf(-xv[q].y, wv[p].y, acc[p][q].x));
-                    acc[p][q].y = fmaf(xv[q].x, wv[p].y, fmaf(xv[q].y, wv[p].x, acc[p][q].y));
+                for (int p = 0; p < OT; ++p) {
+                    acc[q][p].x = fmaf(xv[q].x, wv[p].x, fmaf(-xv[q].y, wv[p].y, acc[q][p].x));
+                    acc[q][p].y = fmaf(xv[q].x, wv[p].y, fmaf(xv[q].y, wv[p].x, acc[q][p].y));
                 }
         }
-#pragma unroll
-        for (int p = 0; p < kOT; ++p)
-#pragma unroll
-            for (int q = 0; q < kBT; ++q)
-                if (o0 + p < OC && b0 + q < B)
-                    Y[(static_cast<size_t>(b_base + b0 + q) * a.Cout + o_base + o0 + p) * a.NM + k0 + kk] = acc[p][q];
+        tc::named_sync(1 + kg, GT);  // the group is done with the slot before it is refilled
+        if (gt == 0 && c + NS < NCH) issue(c + NS);
     }
+    __syncthreads();  // every chunk has been consumed: no copy is in flight
+    if (failed) {
+        if (threadIdx.x == 0) atomicExch(a.watchdog, 40);
+        return;
+    }
+    if (KS > 1) {
+        // partial sums of groups 1.. through shared memory, [group][element][thread]
+        float2* red = reinterpret_cast<float2*>(base);
+        if (kg > 0) {
+#pragma unroll
+            for (int q = 0; q < BT; ++q)
+#pragma unroll
+                for (int p = 0; p < OT; ++p) red[((kg - 1) * BT * OT + q * OT + p) * GT + gt] = acc[q][p];
+        }
+        __syncthreads();
+        if (kg > 0) return;
+        for (int j = 1; j < KS; ++j)
+#pragma unroll
+            for (int q = 0; q < BT; ++q)
+#pragma unroll
+                for (int p = 0; p < OT; ++p) {
+                    const float2 v = red[((j - 1) * BT * OT + q * OT + p) * GT + gt];
+                    acc[q][p].x += v.x;
+                    acc[q][p].y += v.y;
+                }
+    }
+    const int kk = k0 + k;
+    if (kk >= a.NM) return;
+    float2* __restrict__ Y = corner ? a.y[1] : a.y[0];
+#pragma unroll
+    for (int q = 0; q < BT; ++q)
+#pragma unroll
+        for (int p = 0; p < OT; ++p) {
+            const int b = b_base + bq * BT + q, o = o_base + oq * OT + p;
+            if (b < a.B && o < a.Cout) Y[(static_cast<size_t>(b) * a.Cout + o) * a.NM + kk] = acc[q][p];
+        }
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -213,62 +259,134 @@ bool encode3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint64_
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// The TMA-staged launch; returns cudaErrorNotSupported when the shape or alignment does not
-// fit its boxes (the caller then uses mix_smem_kernel).
-cudaError_t launch_mix_tma(const float2* x1, const float2* x2, const float2* w1, const float2* w2, float2* y1,
-                           float2* y2, int ncorner, int B, int Cin, int Cout, int NM, cudaStream_t stream) {
+struct RingCfg {
+    int BT, OT, NBQ, NOQ, KS;
+};
+
+const RingCfg kRingCands[] = {{5, 2, 4, 4, 2}, {5, 2, 4, 2, 4}, {4, 4, 4, 4, 2}, {4, 4, 4, 2, 4},
+                              {4, 2, 4, 4, 2}, {2, 2, 4, 4, 2}, {1, 2, 2, 4, 2}};
+constexpr int kNumRingCands = static_cast<int>(sizeof(kRingCands) / sizeof(kRingCands[0]));
+
+const void* ring_kernel(int ci) {
+    switch (ci) {
+        case 0: return reinterpret_cast<const void*>(mix_ring_kernel<5, 2, 4, 4, 2>);
+        case 1: return reinterpret_cast<const void*>(mix_ring_kernel<5, 2, 4, 2, 4>);
+        case 2: return reinterpret_cast<const void*>(mix_ring_kernel<4, 4, 4, 4, 2>);
+        case 3: return reinterpret_cast<const void*>(mix_ring_kernel<4, 4, 4, 2, 4>);
+        case 4: return reinterpret_cast<const void*>(mix_ring_kernel<4, 2, 4, 4, 2>);
+        case 5: return reinterpret_cast<const void*>(mix_ring_kernel<2, 2, 4, 4, 2>);
+        default: return reinterpret_cast<const void*>(mix_ring_kernel<1, 2, 2, 4, 2>);
+    }
+}
+
+struct RingChoice {
+    int ci, ns;
+    size_t smem;
+};
+
+// The ring shape with the least modelled time: FMA work (padding included) at a rate that
+// saturates at 16 resident warps per SM, or the staging traffic from L2 at 64 B per SM cycle,
+// whichever is larger, plus a load latency per CTA wave.  ci < 0 when no shape fits.
+cudaError_t choose_ring(int ncorner, int B, int Cin, int Cout, int NM, RingChoice* out) {
+    const int NMT = (NM + kRingTM - 1) / kRingTM;
+    const int sms = num_sms();
+    const int nch = (Cin + kRingIC - 1) / kRingIC;
+    const double x_total = static_cast<double>(ncorner) * B * Cin * NM * 8.0;
+    const double w_total = static_cast<double>(ncorner) * Cin * Cout * NM * 8.0;
+    *out = RingChoice{-1, 0, 0};
+    double best_t = 0;
+    for (int ci = 0; ci < kNumRingCands; ++ci) {
+        const RingCfg& c = kRingCands[ci];
+        const int BB = c.BT * c.NBQ, OC = c.OT * c.NOQ, threads = 16 * c.NBQ * c.NOQ * c.KS;
+        if (BB > B || OC > Cout) continue;  // TMA boxes stay inside the tensors
+        const long long stage = static_cast<long long>(BB + OC) * kRingIC * kRingTM * 8;
+        // ring depth: a multiple of KS, at most 4, every chunk in flight if they fit; a group
+        // that takes more than one chunk needs two slots, or each refill waits for its load
+        const int ns = std::min(kRingMaxStages, (nch + c.KS - 1) / c.KS * c.KS);
+        if (ns < std::min(nch, 2 * c.KS)) continue;
+        const long long red = static_cast<long long>(c.KS - 1) * c.BT * c.OT * (threads / c.KS) * 8;
+        const size_t smem = static_cast<size_t>(std::max(ns * stage, red) + 1024);
+        if (smem > 200 * 1024) continue;
+        int per_sm = 1;
+        cudaError_t err = prepare_kernel(ring_kernel(ci), smem, threads, &per_sm);
+        if (err != cudaSuccess) return err;
+        if (per_sm < 1) continue;
+        const long long nbs = (B + BB - 1) / BB, nos = (Cout + OC - 1) / OC;
+        const long long ctas = static_cast<long long>(ncorner) * NMT * nbs * nos;
+        const double resident = std::min<double>(static_cast<double>(ctas) / sms, static_cast<double>(per_sm));
+        const double warps = resident * threads / 32.0;
+        const double cmacs = static_cast<double>(ncorner) * NMT * kRingTM * nbs * BB * nos * OC * Cin;
+        const double fma = 4.0 * cmacs / (sms * 128.0 * std::min(1.0, warps / 16.0));
+        const double l2 = (x_total * nos + w_total * nbs) / (sms * 64.0);
+        const double waves = std::ceil(static_cast<double>(ctas) / (static_cast<double>(sms) * per_sm));
+        const double t = std::max(fma, l2) + 2000.0 * waves;
+        if (out->ci < 0 || t < best_t) {
+            *out = RingChoice{ci, ns, smem};
+            best_t = t;
+        }
+    }
+    return cudaSuccess;
+}
+
+// The TMA ring launch; returns cudaErrorNotSupported when the shape or alignment does not fit
+// its boxes (the caller then uses mix_smem_kernel).
+cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1, const float2* w2, float2* y1,
+                            float2* y2, int ncorner, int B, int Cin, int Cout, int NM, cudaStream_t stream) {
     const uintptr_t al = reinterpret_cast<uintptr_t>(x1) | reinterpret_cast<uintptr_t>(w1) |
                          (ncorner == 2 ? (reinterpret_cast<uintptr_t>(x2) | reinterpret_cast<uintptr_t>(w2)) : 0);
-    if (NM % 2 != 0 || (al & 15) != 0 || B > 256 || Cin > 256) return cudaErrorNotSupported;
-    // Mode tile: 4 when there are enough tiles to fill the GPU twice over, else 2; output
-    // channels split across CTAs until the GPU is filled and the weight tile stays small.
-    const long long want = 2LL * num_sms();
-    const int TM = (static_cast<long long>(ncorner) * (NM / 4) >= want) ? 4 : 2;
-    const long long tiles = static_cast<long long>(ncorner) * ((NM + TM - 1) / TM);
-    int os = 1;
-    const int bs = 1;
-    while (os < Cout && (tiles * os < want || static_cast<long long>(Cin) * ((Cout + os - 1) / os) * TM * 8 > 64 * 1024))
-        os *= 2;
-    const int OC = (Cout + os - 1) / os, BB = (B + bs - 1) / bs;
-    if (OC > 256 || BB > 256) return cudaErrorNotSupported;
-    MixTmaArgs a;
+    if (NM % 2 != 0 || (al & 15) != 0 || Cin < kRingIC) return cudaErrorNotSupported;
+    // Tile shapes: the one with the least modelled time, chosen once per shape and device.
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static std::mutex m;
+    static std::map<std::tuple<int, int, int, int, int, int>, RingChoice> chosen;
+    RingChoice ch{-1, 0, 0};
+    const int nch = (Cin + kRingIC - 1) / kRingIC;
+    {
+        std::lock_guard<std::mutex> lock(m);
+        const auto key = std::make_tuple(dev, ncorner, B, Cin, Cout, NM);
+        auto it = chosen.find(key);
+        if (it != chosen.end()) {
+            ch = it->second;
+        } else {
+            e = choose_ring(ncorner, B, Cin, Cout, NM, &ch);
+            if (e != cudaSuccess) return e;
+            chosen.emplace(key, ch);
+        }
+    }
+    if (ch.ci < 0) return cudaErrorNotSupported;
+    const int best = ch.ci, best_ns = ch.ns;
+    const size_t best_smem = ch.smem;
+    const RingCfg& cfg = kRingCands[best];
+    const int BB = cfg.BT * cfg.NBQ, OC = cfg.OT * cfg.NOQ;
+    MixRingArgs a;
     a.y[0] = y1;
     a.y[1] = y2;
     a.B = B;
     a.Cin = Cin;
     a.Cout = Cout;
     a.NM = NM;
-    a.OC = OC;
-    a.TM = TM;
-    a.BB = BB;
+    a.NCH = nch;
+    a.NS = best_ns;
     a.n_os = (Cout + OC - 1) / OC;
+    a.stage_bytes = static_cast<uint32_t>(BB + OC) * kRingIC * kRingTM * 8u;
     const int n_bs = (B + BB - 1) / BB;
-    a.x_bytes = static_cast<uint32_t>(BB) * Cin * TM * 8u;
-    a.w_bytes = static_cast<uint32_t>(Cin) * OC * TM * 8u;
-    a.w_off = (a.x_bytes + 127u) / 128u * 128u;
-    const size_t smem = a.w_off + a.w_bytes + 1024;
-    if (smem > 200 * 1024) return cudaErrorNotSupported;
-    cudaError_t e = device_watchdog(&a.watchdog);
+    const int threads = 16 * cfg.NBQ * cfg.NOQ * cfg.KS;
+    e = device_watchdog(&a.watchdog);
     if (e != cudaSuccess) return e;
     CUtensorMap tx[2], tw[2];
-    const int nc = ncorner;
     const float2* xs[2] = {x1, x2};
     const float2* ws[2] = {w1, w2};
     for (int c = 0; c < 2; ++c) {
-        const int src = c < nc ? c : 0;  // an unused second corner repeats the first map
-        if (!encode3d(&tx[c], xs[src], 2ull * NM, Cin, B, 2u * TM, Cin, BB) ||
-            !encode3d(&tw[c], ws[src], 2ull * NM, Cout, Cin, 2u * TM, OC, Cin))
+        const int src = c < ncorner ? c : 0;  // an unused second corner repeats the first map
+        if (!encode3d(&tx[c], xs[src], 2ull * NM, Cin, B, 2u * kRingTM, kRingIC, BB) ||
+            !encode3d(&tw[c], ws[src], 2ull * NM, Cout, Cin, 2u * kRingTM, OC, kRingIC))
             return cudaErrorNotSupported;
     }
-    int per_sm = 1;
-    const dim3 grid((NM + TM - 1) / TM, ncorner, a.n_os * n_bs);
-    auto run = [&](auto kernel) -> cudaError_t {
-        cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), smem, kThreads, &per_sm);
-        if (err != cudaSuccess) return err;
-        kernel<<<grid, kThreads, smem, stream>>>(tx[0], tx[1], tw[0], tw[1], a);
-        return cudaGetLastError();
-    };
-    return TM == 4 ? run(mix_tma_kernel<4>) : run(mix_tma_kernel<2>);
+    const dim3 grid(static_cast<unsigned>((NM + kRingTM - 1) / kRingTM), ncorner, a.n_os * n_bs);
+    void* args[] = {&tx[0], &tx[1], &tw[0], &tw[1], &a};
+    return cudaLaunchKernel(ring_kernel(best), grid, dim3(threads), args, best_smem, stream);
 }
 
 }  // namespace
@@ -276,7 +394,7 @@ cudaError_t launch_mix_tma(const float2* x1, const float2* x2, const float2* w1,
 cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, const float2* w2,
                        float2* y1, float2* y2, int ncorner, int B, int Cin, int Cout, int NM,
                        cudaStream_t stream) {
-    const cudaError_t te = launch_mix_tma(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream);
+    const cudaError_t te = launch_mix_ring(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream);
     if (te != cudaErrorNotSupported) return te;
     MixArgs a;
     a.x[0] = x1;

@@ -85,7 +85,9 @@ def test_linearity_full_size(cuda_device):
     y1 = run_device(x, w1, w2, c["m1"], c["m2"], cuda_device)
     y2 = run_device(x2, w1, w2, c["m1"], c["m2"], cuda_device)
     y12 = run_device(a * x + b * x2, w1, w2, c["m1"], c["m2"], cuda_device)
-    assert_close((a * y1 + b * y2).cpu().numpy(), y12.cpu().numpy(), 1e-5)
+    # each forward carries about 1e-5 (of the output scale) of bf16x3 / fp32 rounding, and
+    # a*y1 + b*y2 - y12 adds |a| + |b| + 1 = 3.25 of them
+    assert_close((a * y1 + b * y2).cpu().numpy(), y12.cpu().numpy(), 3e-5)
 
 
 def test_deterministic_and_fully_written(cuda_device):

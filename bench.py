@@ -144,6 +144,21 @@ class ClockSampler:
 
 # ------------------------------------------------------------------------- our arm
 
+def capture_graphs(device, fns) -> list:
+    """One CUDA graph per callable; each is called with the capture stream's handle."""
+    graphs = []
+    cap = torch.cuda.Stream(device)
+    cap.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cap):
+        for fn in fns:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=cap):
+                fn(cap.cuda_stream)
+            graphs.append(g)
+    torch.cuda.current_stream(device).wait_stream(cap)
+    return graphs
+
+
 def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: int, *, with_e2e: bool,
                  with_breakdown: bool, sampler_gpu: int | None):
     import scx_data
@@ -166,10 +181,10 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
     stream = torch.cuda.current_stream(device)
     sh = stream.cuda_stream
 
-    def step(i):
+    def launch(i, stream_handle):
         s = i % nsets
         rc = lib.scx_spectral_conv2d_fwd(xs[s].data_ptr(), w1.data_ptr(), w2.data_ptr(), ys[s].data_ptr(), B, Cin,
-                                         Cout, H, W, m1, m2, ws.data_ptr(), ws_bytes, sh)
+                                         Cout, H, W, m1, m2, ws.data_ptr(), ws_bytes, stream_handle)
         if rc != 0:
             raise RuntimeError(f"scx_spectral_conv2d_fwd failed: {rc}")
 
@@ -177,8 +192,20 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
         if world > 1:
             torch.distributed.barrier()
 
-    for i in range(warmup):
-        step(i)
+    # CUDA graphs: one per input buffer set (one forward, three kernels) and one for a whole
+    # rotation over the sets; steps run as rotations plus single steps for the remainder
+    launch(0, sh)  # first use of the shape builds the twiddle tables outside any capture
+    torch.cuda.synchronize(device)
+    graphs = capture_graphs(device, [lambda h, s=s: launch(s, h) for s in range(nsets)] +
+                            [lambda h: [launch(s, h) for s in range(nsets)]])
+
+    def run_steps(n):
+        for _ in range(n // nsets):
+            graphs[nsets].replay()
+        for s in range(n % nsets):
+            graphs[s].replay()
+
+    run_steps(warmup)
     torch.cuda.synchronize(device)
     barrier()
     torch.cuda.synchronize(device)
@@ -189,27 +216,26 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
     if sampler:
         sampler.__enter__()
     ev0.record(stream)
-    for i in range(steps):
-        step(i)
+    run_steps(steps)
     ev1.record(stream)
     torch.cuda.synchronize(device)
     t_ms = ev0.elapsed_time(ev1)
     if sampler:
         # keep the same load running for >= 1 s so that the 100 ms sampler sees it
         t_end = time.perf_counter() + 1.2
-        i = 0
         while time.perf_counter() < t_end:
-            for _ in range(20):
-                step(i)
-                i += 1
+            run_steps(4 * nsets)
             torch.cuda.synchronize(device)
         sampler.__exit__()
         clocks = sampler.summary()
     barrier()
     t_ms_max = scx_dist.max_over_ranks(t_ms, device)
     ms_per_step = t_ms_max / steps
+    # 256-point grids run as a quadrant fold, four tensor-core forwards, the mixing, four
+    # inverses and an unfold; the per-kernel split below covers the three-kernel shapes
+    folded = H > 128 or W > 128
     res = {"cfg": c, "ms_per_step": ms_per_step, "samples_per_s": world * B / (ms_per_step / 1e3),
-           "launches_per_step": 3, "clocks": clocks}
+           "launches_per_step": 11 if folded else 3, "clocks": clocks, "cuda_graph": True}
 
     nbytes = spectral_bytes(c)
     peak, peak_kind = hbm_peak()
@@ -218,33 +244,48 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
         "unit": "GB/s", "peak_kind": peak_kind, "bytes": nbytes["fused_path"]}
     res["roofline_fused_path"]["frac"] = res["roofline_fused_path"]["achieved"] / peak
 
-    if with_breakdown:
-        # per-kernel CUDA-event durations of the three launches of one forward
+    if with_breakdown and not folded:
+        # per-kernel durations: each kernel replayed alone from a CUDA graph of nsets launches
+        # (the inputs rotate as in the step), CUDA events around the replays
         ci = B * Cin * m1 * m2 * 2
         co = B * Cout * m1 * m2 * 2
         X1 = ws.view(torch.float32)[:ci]
         X2 = ws.view(torch.float32)[ci:2 * ci]
         Y1 = ws.view(torch.float32)[2 * ci:2 * ci + co]
         Y2 = ws.view(torch.float32)[2 * ci + co:2 * ci + 2 * co]
+
+        def k_fwd(i, h):
+            return lib.scx_rfft2_corners(xs[i % nsets].data_ptr(), X1.data_ptr(), X2.data_ptr(), B, Cin, H, W, m1,
+                                         m2, h)
+
+        def k_mix(i, h):
+            return lib.scx_spectral_mul_dual(X1.data_ptr(), X2.data_ptr(), w1.data_ptr(), w2.data_ptr(),
+                                             Y1.data_ptr(), Y2.data_ptr(), B, Cin, Cout, m1, m2, h)
+
+        def k_inv(i, h):
+            return lib.scx_irfft2_corners(Y1.data_ptr(), Y2.data_ptr(), ys[i % nsets].data_ptr(), B, Cout, H, W,
+                                          m1, m2, h)
+
+        kern = {}
         reps = max(10, steps)
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(reps)]
-        for r in range(reps):
-            s = r % nsets
-            e = evs[r]
-            e[0].record(stream)
-            lib.scx_rfft2_corners(xs[s].data_ptr(), X1.data_ptr(), X2.data_ptr(), B, Cin, H, W, m1, m2, sh)
-            e[1].record(stream)
-            lib.scx_spectral_mul_dual(X1.data_ptr(), X2.data_ptr(), w1.data_ptr(), w2.data_ptr(), Y1.data_ptr(),
-                                      Y2.data_ptr(), B, Cin, Cout, m1, m2, sh)
-            e[2].record(stream)
-            lib.scx_irfft2_corners(Y1.data_ptr(), Y2.data_ptr(), ys[s].data_ptr(), B, Cout, H, W, m1, m2, sh)
-            e[3].record(stream)
-        torch.cuda.synchronize(device)
-        kern = {"dft_fwd": 0.0, "mix": 0.0, "dft_inv": 0.0}
-        for e in evs:
-            kern["dft_fwd"] += e[0].elapsed_time(e[1]) / reps
-            kern["mix"] += e[1].elapsed_time(e[2]) / reps
-            kern["dft_inv"] += e[2].elapsed_time(e[3]) / reps
+        for kname, fn in (("dft_fwd", k_fwd), ("mix", k_mix), ("dft_inv", k_inv)):
+            for i in range(nsets):  # warm, and check the status outside the capture
+                rc = fn(i, sh)
+                if rc != 0:
+                    raise RuntimeError(f"{kname} failed: {rc}")
+            torch.cuda.synchronize(device)
+            g = capture_graphs(device, [lambda h: [fn(i, h) for i in range(nsets)]])[0]
+            g.replay()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(device)
+            kern[kname] = e0.elapsed_time(e1) / (reps * nsets)
+            del g
+
         total = sum(kern.values())
         res["kernels"] = {k: {"ms": v, "share": v / total, "bytes": nbytes[k],
                               "gbs": nbytes[k] / (v / 1e3) / 1e9} for k, v in kern.items()}
@@ -391,9 +432,11 @@ def ours(args) -> None:
                              with_breakdown=True, sampler_gpu=None)
             extras[wname] = {"ms_per_step": r["ms_per_step"], "samples_per_s": r["samples_per_s"],
                              "roofline_fused_path_frac": r["roofline_fused_path"]["frac"],
-                             "dominant_kernel": r["roofline"]["kernel"],
-                             "dominant_kernel_frac": r["roofline"]["frac"],
-                             "kernels_ms": {k: v["ms"] for k, v in r["kernels"].items()}}
+                             "launches_per_step": r["launches_per_step"], "cuda_graph": True}
+            if "roofline" in r:
+                extras[wname].update(dominant_kernel=r["roofline"]["kernel"],
+                                     dominant_kernel_frac=r["roofline"]["frac"],
+                                     kernels_ms={k: v["ms"] for k, v in r["kernels"].items()})
         extras["fno_ns_b20_w32_64x64_m12_l4"] = run_fno(max(10, args.steps // 2), warmup, device, world, rank)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -409,7 +452,8 @@ def ours(args) -> None:
             "config": {"workload": args.workload, "batch_per_gpu": c["B"], "global_batch": c["B"] * world,
                        "channels_in": c["Cin"], "channels_out": c["Cout"], "height": c["H"], "width": c["W"],
                        "modes1": c["m1"], "modes2": c["m2"], "parallelism": f"batch-shard x{world}",
-                       "l2": "inputs rotate over buffer sets totalling >= 3x L2 between steps"},
+                       "l2": "inputs rotate over buffer sets totalling >= 3x L2 between steps",
+                       "launch": "CUDA graphs of whole rotations over the buffer sets (three kernels per forward)"},
             "roofline": res.get("roofline"), "roofline_fused_path": res["roofline_fused_path"],
             "kernels": res.get("kernels"), "e2e": res.get("e2e"), "cpu_baseline": cpu,
             "clocks": res["clocks"], "gpu_launches": res["launches_per_step"] * args.steps,

@@ -28,7 +28,8 @@
 //
 // Warp roles (persistent, one CTA per SM, planes split into contiguous balanced ranges):
 //   warp 19      lane 0 initialises the barriers, starts the table and the first ring loads
-//                before the setup barrier, then streams 32-row chunks of x into a shared-memory
+//                before the setup barrier (the x loads after griddepcontrol.wait: the kernel is
+//                launched as a programmatic dependent of the previous one), then streams 32-row chunks of x into a shared-memory
 //                ring with 1-D bulk copies (about 100 KB in flight per SM)
 //   warps 0..7   converters: ring -> bf16 hi/lo in registers -> the TMEM A operand, stored
 //                only while no A-in-TMEM MMA is in flight (stores issued while such MMAs ran
@@ -142,6 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
     };
     const int k_first = min(NK, C::NS);  // chunks issued before the setup barrier
 
+    if (tid == 0) tc::grid_dep_launch();  // the next kernel's CTAs may start their prologue
     if (warp == 0) {
         tc::tmem_alloc(&tmem_base, C::TMEM_COLS);
         tc::tmem_relinquish();
@@ -162,10 +164,12 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         tc::mbar_init(&bars.tab, 1);
         for (int i = 0; i < 3; ++i) tc::mbar_init(&bars.drain[i], 1);
         tc::fence_async_smem();
-        // the ring starts empty: the first NS chunks need no slot wait
-        for (int k = 0; k < k_first; ++k) issue_chunk(k);
         tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
         tc::bulk_g2s(base + C::OFF_FB, a.tab, a.tab_bytes, &bars.tab);
+        // x may be written by the previous kernel in the stream; the ring starts empty, so the
+        // first NS chunks need no slot wait
+        tc::grid_dep_wait();
+        for (int k = 0; k < k_first; ++k) issue_chunk(k);
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -481,8 +485,7 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
     cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), C::SMEM, kThreads, &per_sm);
     if (err != cudaSuccess) return err;
     const int grid = std::max(1, std::min(a.P, num_sms()));
-    kernel<<<grid, kThreads, C::SMEM, stream>>>(a);
-    return cudaGetLastError();
+    return launch_chained(kernel, dim3(grid), dim3(kThreads), C::SMEM, stream, a);
 }
 
 template <int H, int W>

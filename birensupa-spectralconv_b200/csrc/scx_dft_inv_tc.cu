@@ -21,7 +21,8 @@
 // Every product is bf16x3 (hi*hi + hi*lo + lo*hi) chained along K into one fp32
 // accumulator.  Warp roles (persistent, one CTA per SM, contiguous balanced plane ranges):
 //   warps 0..3   loaders: corner spectra -> Yr operand (MN-major, double-buffered); the first
-//                group's loads are issued before the setup barrier.  They also run E4 for the
+//                group's loads are issued before the setup barrier, after griddepcontrol.wait
+//                (the kernel is launched as a programmatic dependent of the previous one).  They also run E4 for the
 //                upper half of h.
 //   warps 4..7   E4 for the lower half of h; each warp hands its S5 chain's Z over alone, so
 //                the next group's E4 for a chain waits only for that chain's S5
@@ -135,7 +136,11 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
             }
         }
     };
-    if (warp < kLoadWarps && NG > 0) load_group(0);  // in flight during the setup below
+    if (tid == 0) tc::grid_dep_launch();  // the next kernel's CTAs may start their prologue
+    if (warp < kLoadWarps && NG > 0) {
+        tc::grid_dep_wait();  // the spectra come from the previous kernel in the stream
+        load_group(0);        // in flight during the setup below
+    }
 
     if (warp == 0) {
         tc::tmem_alloc(&tmem_base, C::TMEM_COLS);
@@ -463,8 +468,7 @@ cudaError_t run_inv(const InvArgs& a, cudaStream_t stream) {
     cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), C::SMEM, kThreads, &per_sm);
     if (err != cudaSuccess) return err;
     const int grid = std::max(1, std::min(a.Q, num_sms()));
-    kernel<<<grid, kThreads, C::SMEM, stream>>>(a);
-    return cudaGetLastError();
+    return launch_chained(kernel, dim3(grid), dim3(kThreads), C::SMEM, stream, a);
 }
 
 template <int H, int W>

@@ -13,6 +13,8 @@
 // assignment in the reference overwrites the first.
 #pragma once
 
+#include <utility>
+
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -41,6 +43,29 @@ int num_sms();
 // (once per kernel/device/size: later launches, e.g. inside stream capture, make no call)
 // and returns how many blocks of `threads` threads fit on one SM.
 cudaError_t prepare_kernel(const void* kernel, size_t bytes, int threads, int* blocks_per_sm);
+
+// Launches `kernel` with programmatic stream serialization: its CTAs may start (and run their
+// prologue) while the previous kernel in the stream finishes; the kernel must execute
+// griddepcontrol.wait in every CTA before it reads what earlier work wrote.
+template <typename... Params, typename... Args>
+cudaError_t launch_chained(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// The same for a kernel known by address, with its arguments as an array of pointers.
+cudaError_t launch_chained_raw(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                               void** args);
 
 // ---- kernel launchers (no argument validation here; the C-ABI layer validates) ----
 

@@ -145,8 +145,10 @@ __global__ void __launch_bounds__(16 * NBQ * NOQ * KS) mix_ring_kernel(const __g
         tc::tma_load_3d(st + XB, mw, 2 * k0, o_base, c * IC, bar);
     };
     if (threadIdx.x == 0) {
+        tc::grid_dep_launch();  // the next kernel's CTAs may start their prologue
         for (int i = 0; i < kRingMaxStages; ++i) tc::mbar_init(&full[i], 1);
         tc::fence_async_smem();
+        tc::grid_dep_wait();  // x comes from the previous kernel in the stream
         for (int c = 0; c < min(NS, NCH); ++c) issue(c);
         failed = 0;
     }
@@ -386,7 +388,7 @@ cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1
     }
     const dim3 grid(static_cast<unsigned>((NM + kRingTM - 1) / kRingTM), ncorner, a.n_os * n_bs);
     void* args[] = {&tx[0], &tx[1], &tw[0], &tw[1], &a};
-    return cudaLaunchKernel(ring_kernel(best), grid, dim3(threads), args, best_smem, stream);
+    return launch_chained_raw(ring_kernel(best), grid, dim3(threads), best_smem, stream, args);
 }
 
 }  // namespace

@@ -48,6 +48,21 @@ int num_sms() {
     return n;
 }
 
+cudaError_t launch_chained_raw(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                               void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, kernel, args);
+}
+
 cudaError_t prepare_kernel(const void* kernel, size_t bytes, int threads, int* blocks_per_sm) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);

@@ -4,9 +4,8 @@
 //   fno_lift_kernel            1x1 conv (T+2 -> hidden) with the grid channels generated
 //                              in-kernel (fno_ns/model.py:168-181,193-195) or read from a
 //                              channels-last input
-//   fno_skip_kernel            per pixel: z = spectral + W h + b for every output channel,
-//                              plus per-warp (mean, M2) partial statistics of each plane
-//   fno_norm_gelu_kernel       instance statistics combined exactly (Chan's formula), then
+//   fno_skip_kernel            per pixel: z = spectral + W h + b for every output channel
+//   fno_norm_gelu_kernel       one CTA per plane: two-pass instance statistics, then
 //                              normalisation and GELU (fno_ns/model.py:96-99,133-134)
 //   fno_project_kernel         per pixel: hidden -> proj_hidden (GELU) -> out_channels, the
 //                              proj_hidden-wide intermediate never leaves registers
@@ -77,14 +76,15 @@ __global__ void __launch_bounds__(kThreads) fno_lift_kernel(const float* __restr
         if (c < hidden) hb[static_cast<size_t>(c) * HW] = acc[c];
 }
 
-// Fourier-layer epilogue, part A (one thread per pixel):
-//   z[b][o][p] = s[b][o][p] + bias[o] + sum_i Wskip[o][i] h[b][i][p]    (written over s)
-// With instance_norm it also writes, per warp of 32 pixels and channel, the partial
-// statistics (mean, M2 = sum (z - mean)^2) to part[b][o][warp]; without it, it writes
-// GELU(z) to h_next directly.  grid = (ceil(HW / 256), B)
-template <int HMAX>
+// Fourier-layer epilogue, part A:
+//   z[b][o][p] = s[b][o][p] + bias[o] + sum_i Wskip[o][i] h[b][i][p]
+// written over s when instance_norm is on (part B normalises it), else GELU(z) written to
+// h_next.  Each thread takes PX pixels kThreads apart (one shared-memory read of a weight row
+// feeds PX pixels) and four output channels per pass (independent FMA chains; each channel's
+// sum keeps its order over i).  grid = (ceil(HW / (kThreads * PX)), B)
+template <int HMAX, int PX>
 __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ s, const float* __restrict__ h,
-                                                            float* __restrict__ h_next, float2* __restrict__ part,
+                                                            float* __restrict__ h_next,
                                                             const float* __restrict__ w,
                                                             const float* __restrict__ bias, int HW, int hidden,
                                                             int instance_norm) {
@@ -95,95 +95,134 @@ __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ 
     }
     __syncthreads();
     const int b = blockIdx.y;
-    const int p = blockIdx.x * kThreads + threadIdx.x;
-    const bool valid = p < HW;
-    const int pp = valid ? p : 0;
-    float hv[HMAX];
-    const float* hb = h + static_cast<size_t>(b) * hidden * HW + pp;
+    const int p0 = blockIdx.x * kThreads * PX + threadIdx.x;
+    if (p0 >= HW) return;
+    int pix[PX];
+    bool live[PX];
 #pragma unroll
-    for (int i = 0; i < HMAX; ++i) hv[i] = i < hidden ? __ldg(hb + static_cast<size_t>(i) * HW) : 0.f;
-    float* sb = s + static_cast<size_t>(b) * hidden * HW + pp;
-    const int lane = threadIdx.x & 31;
-    const int nwarps_plane = (HW + 31) / 32;
-    const int gwarp = p / 32;  // warp index within the plane
-    for (int o = 0; o < hidden; ++o) {
-        const float4* wr = reinterpret_cast<const float4*>(ws + o * HMAX);
-        float z = __ldg(bias + o) + (valid ? sb[static_cast<size_t>(o) * HW] : 0.f);
+    for (int x = 0; x < PX; ++x) {
+        live[x] = p0 + x * kThreads < HW;
+        pix[x] = live[x] ? p0 + x * kThreads : p0;  // a pixel past the plane repeats the first one
+    }
+    const size_t plane0 = static_cast<size_t>(b) * hidden * HW;
+    float hv[PX][HMAX];
+#pragma unroll
+    for (int x = 0; x < PX; ++x)
+#pragma unroll
+        for (int i = 0; i < HMAX; ++i)
+            hv[x][i] = i < hidden ? __ldg(h + plane0 + static_cast<size_t>(i) * HW + pix[x]) : 0.f;
+    for (int o0 = 0; o0 < hidden; o0 += 4) {
+        float z[4][PX];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int o = min(o0 + t, hidden - 1);
+            const float bo = __ldg(bias + o);
+#pragma unroll
+            for (int x = 0; x < PX; ++x) z[t][x] = bo + s[plane0 + static_cast<size_t>(o) * HW + pix[x]];
+        }
 #pragma unroll
         for (int i4 = 0; i4 < HMAX / 4; ++i4) {
-            const float4 wv = wr[i4];
-            z = fmaf(wv.x, hv[4 * i4 + 0], z);
-            z = fmaf(wv.y, hv[4 * i4 + 1], z);
-            z = fmaf(wv.z, hv[4 * i4 + 2], z);
-            z = fmaf(wv.w, hv[4 * i4 + 3], z);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const float4 wv = reinterpret_cast<const float4*>(ws + min(o0 + t, hidden - 1) * HMAX)[i4];
+#pragma unroll
+                for (int x = 0; x < PX; ++x) {
+                    z[t][x] = fmaf(wv.x, hv[x][4 * i4 + 0], z[t][x]);
+                    z[t][x] = fmaf(wv.y, hv[x][4 * i4 + 1], z[t][x]);
+                    z[t][x] = fmaf(wv.z, hv[x][4 * i4 + 2], z[t][x]);
+                    z[t][x] = fmaf(wv.w, hv[x][4 * i4 + 3], z[t][x]);
+                }
+            }
         }
-        if (!instance_norm) {
-            if (valid) h_next[(static_cast<size_t>(b) * hidden + o) * HW + p] = gelu_erf(z);
-            continue;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            if (o0 + t >= hidden) break;
+            const size_t row = plane0 + static_cast<size_t>(o0 + t) * HW;
+#pragma unroll
+            for (int x = 0; x < PX; ++x) {
+                if (!live[x]) continue;
+                if (instance_norm)
+                    s[row + pix[x]] = z[t][x];
+                else
+                    h_next[row + pix[x]] = gelu_erf(z[t][x]);
+            }
         }
-        if (valid) sb[static_cast<size_t>(o) * HW] = z;
-        // warp partials over the valid pixels of this warp (a warp wholly past the plane
-        // has none; the condition is uniform across the warp)
-        const int wstart = gwarp * 32;
-        if (wstart >= HW) continue;
-        const int n = min(32, HW - wstart);
-        float sum = valid ? z : 0.f;
-        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        const float mean = sum / static_cast<float>(n);
-        const float d = valid ? z - mean : 0.f;
-        float m2 = d * d;
-        for (int off = 16; off > 0; off >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, off);
-        if (lane == 0) part[(static_cast<size_t>(b) * hidden + o) * nwarps_plane + gwarp] = make_float2(mean, m2);
     }
 }
 
-// Fourier-layer epilogue, part B: combines the warp partials of each (b, o) plane with
-// Chan's parallel-variance formula (mean = sum n_w mean_w / N, M2 = sum [M2_w + n_w
-// (mean_w - mean)^2]) and writes h_next = GELU((z - mean) / sqrt(M2 / N + eps)).
-// grid = (ceil(HW / 256), B); each block recombines the statistics of its batch item.
-template <int HMAX>
-__global__ void __launch_bounds__(kThreads) fno_norm_gelu_kernel(const float* __restrict__ z,
-                                                                 float* __restrict__ h_next,
-                                                                 const float2* __restrict__ part, int HW,
-                                                                 int hidden) {
-    __shared__ float mean_s[HMAX], rstd_s[HMAX];
-    const int b = blockIdx.y;
-    const int nw = (HW + 31) / 32;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int o = warp; o < hidden; o += kThreads / 32) {
-        const float2* pp = part + (static_cast<size_t>(b) * hidden + o) * nw;
-        float sum = 0.f;
-        for (int k = lane; k < nw; k += 32) {
-            const int n = min(32, HW - k * 32);
-            sum += pp[k].x * static_cast<float>(n);
-        }
-        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        const float mean = sum / static_cast<float>(HW);
-        float m2 = 0.f;
-        for (int k = lane; k < nw; k += 32) {
-            const int n = min(32, HW - k * 32);
-            const float d = pp[k].x - mean;
-            m2 += pp[k].y + static_cast<float>(n) * d * d;
-        }
-        for (int off = 16; off > 0; off >>= 1) m2 += __shfl_xor_sync(0xffffffffu, m2, off);
-        if (lane == 0) {
-            mean_s[o] = mean;
-            rstd_s[o] = 1.0f / sqrtf(m2 / static_cast<float>(HW) + 1e-5f);
-        }
-    }
+// Sum over the CTA in a fixed order (per-warp butterflies, then warp 0 adds the warp sums in
+// warp order); every thread gets the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();  // red is free (an earlier call's readers are done)
+    if (lane == 0) red[warp] = v;
     __syncthreads();
-    const int p = blockIdx.x * kThreads + threadIdx.x;
-    if (p >= HW) return;
-    const size_t base = static_cast<size_t>(b) * hidden * HW + p;
-    for (int o = 0; o < hidden; ++o) {
-        const size_t i = base + static_cast<size_t>(o) * HW;
-        h_next[i] = gelu_erf((z[i] - mean_s[o]) * rstd_s[o]);
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < kThreads / 32; ++k) t += red[k];
+    return t;
+}
+
+// Fourier-layer epilogue, part B, one CTA per (b, o) plane: instance statistics in two exact
+// passes (mean, then the mean of (z - mean)^2, biased like torch's InstanceNorm2d) and
+// h_next = GELU((z - mean) / sqrt(var + eps)) (fno_ns/model.py:96-99,133-134).  A plane of at
+// most 16 values per thread (4096 pixels) is read once into registers; larger planes are read
+// again for each pass.  grid = B * hidden
+constexpr int kNormRegs = 16;
+
+__global__ void __launch_bounds__(kThreads) fno_norm_gelu_kernel(const float* __restrict__ z,
+                                                                 float* __restrict__ h_next, int HW) {
+    __shared__ float red[kThreads / 32];
+    const size_t plane = blockIdx.x;
+    const float* zp = z + plane * HW;
+    float* hp = h_next + plane * HW;
+    const float inv_n = 1.0f / static_cast<float>(HW);
+    if (HW <= kNormRegs * kThreads) {
+        float v[kNormRegs];
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k) {
+            const int i = threadIdx.x + k * kThreads;
+            v[k] = i < HW ? __ldg(zp + i) : 0.f;
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k) sum += v[k];
+        const float mean = block_sum(sum, red) * inv_n;
+        float m2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k) {
+            const int i = threadIdx.x + k * kThreads;
+            const float d = i < HW ? v[k] - mean : 0.f;
+            m2 = fmaf(d, d, m2);
+        }
+        const float rstd = 1.0f / sqrtf(block_sum(m2, red) * inv_n + 1e-5f);
+#pragma unroll
+        for (int k = 0; k < kNormRegs; ++k) {
+            const int i = threadIdx.x + k * kThreads;
+            if (i < HW) hp[i] = gelu_erf((v[k] - mean) * rstd);
+        }
+        return;
     }
+    float sum = 0.f;
+    for (int i = threadIdx.x; i < HW; i += kThreads) sum += __ldg(zp + i);
+    const float mean = block_sum(sum, red) * inv_n;
+    float m2 = 0.f;
+    for (int i = threadIdx.x; i < HW; i += kThreads) {
+        const float d = __ldg(zp + i) - mean;
+        m2 = fmaf(d, d, m2);
+    }
+    const float rstd = 1.0f / sqrtf(block_sum(m2, red) * inv_n + 1e-5f);
+    for (int i = threadIdx.x; i < HW; i += kThreads) hp[i] = gelu_erf((__ldg(zp + i) - mean) * rstd);
 }
 
 // y[b][oc][p] = b2[oc] + sum_j W2[oc][j] GELU(b1[j] + sum_c W1[j][c] h[b][c][p])
-// grid = (ceil(HW / 256), B)
-template <int HMAX>
+// Each thread takes PX pixels (kThreads apart, so loads and stores stay coalesced): one
+// shared-memory read of a weight row feeds PX pixels.  Four hidden units per pass give four
+// independent FMA chains; each unit's sum keeps its order over c and the output sums take the
+// units in order j = 0, 1, ...  grid = (ceil(HW / (kThreads * PX)), B)
+template <int HMAX, int PX>
 __global__ void __launch_bounds__(kThreads) fno_project_kernel(const float* __restrict__ h, float* __restrict__ y,
                                                                const float* __restrict__ w1,
                                                                const float* __restrict__ b1,
@@ -202,39 +241,66 @@ __global__ void __launch_bounds__(kThreads) fno_project_kernel(const float* __re
     for (int i = threadIdx.x; i < oc_n * ph; i += kThreads) w2s[i] = w2[i];
     __syncthreads();
     const int b = blockIdx.y;
-    const int p = blockIdx.x * kThreads + threadIdx.x;
-    if (p >= HW) return;
+    const int p0 = blockIdx.x * kThreads * PX + threadIdx.x;
+    if (p0 >= HW) return;
     constexpr int kMaxOut = 4;
-    float hv[HMAX];
-    const float* hb = h + static_cast<size_t>(b) * hidden * HW + p;
+    float hv[PX][HMAX];
 #pragma unroll
-    for (int c = 0; c < HMAX; ++c) hv[c] = c < hidden ? __ldg(hb + static_cast<size_t>(c) * HW) : 0.f;
-    float out[kMaxOut];
+    for (int x = 0; x < PX; ++x) {
+        const int p = min(p0 + x * kThreads, HW - 1);  // a pixel past the plane repeats the last one
+        const float* hb = h + static_cast<size_t>(b) * hidden * HW + p;
 #pragma unroll
-    for (int o = 0; o < kMaxOut; ++o) out[o] = 0.f;
-    for (int j = 0; j < ph; ++j) {
-        const float4* wr = reinterpret_cast<const float4*>(w1s + j * HMAX);
-        float acc = b1s[j];
+        for (int c = 0; c < HMAX; ++c) hv[x][c] = c < hidden ? __ldg(hb + static_cast<size_t>(c) * HW) : 0.f;
+    }
+    float out[PX][kMaxOut];
+#pragma unroll
+    for (int x = 0; x < PX; ++x)
+#pragma unroll
+        for (int o = 0; o < kMaxOut; ++o) out[x][o] = 0.f;
+    for (int j0 = 0; j0 < ph; j0 += 4) {
+        float acc[4][PX];
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+            for (int x = 0; x < PX; ++x) acc[t][x] = b1s[min(j0 + t, ph - 1)];
 #pragma unroll
         for (int c4 = 0; c4 < HMAX / 4; ++c4) {
-            const float4 wv = wr[c4];
-            acc = fmaf(wv.x, hv[4 * c4 + 0], acc);
-            acc = fmaf(wv.y, hv[4 * c4 + 1], acc);
-            acc = fmaf(wv.z, hv[4 * c4 + 2], acc);
-            acc = fmaf(wv.w, hv[4 * c4 + 3], acc);
-        }
-        const float g = gelu_erf(acc);
 #pragma unroll
-        for (int o = 0; o < kMaxOut; ++o)
-            if (o < oc_n) out[o] = fmaf(w2s[o * ph + j], g, out[o]);
+            for (int t = 0; t < 4; ++t) {
+                const float4 wv = reinterpret_cast<const float4*>(w1s + min(j0 + t, ph - 1) * HMAX)[c4];
+#pragma unroll
+                for (int x = 0; x < PX; ++x) {
+                    acc[t][x] = fmaf(wv.x, hv[x][4 * c4 + 0], acc[t][x]);
+                    acc[t][x] = fmaf(wv.y, hv[x][4 * c4 + 1], acc[t][x]);
+                    acc[t][x] = fmaf(wv.z, hv[x][4 * c4 + 2], acc[t][x]);
+                    acc[t][x] = fmaf(wv.w, hv[x][4 * c4 + 3], acc[t][x]);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            if (j0 + t >= ph) break;
+#pragma unroll
+            for (int x = 0; x < PX; ++x) {
+                const float g = gelu_erf(acc[t][x]);
+#pragma unroll
+                for (int o = 0; o < kMaxOut; ++o)
+                    if (o < oc_n) out[x][o] = fmaf(w2s[o * ph + j0 + t], g, out[x][o]);
+            }
+        }
     }
 #pragma unroll
-    for (int o = 0; o < kMaxOut; ++o)
-        if (o < oc_n) y[(static_cast<size_t>(b) * oc_n + o) * HW + p] = out[o] + b2[o];
+    for (int x = 0; x < PX; ++x) {
+        const int p = p0 + x * kThreads;
+        if (p >= HW) break;
+#pragma unroll
+        for (int o = 0; o < kMaxOut; ++o)
+            if (o < oc_n) y[(static_cast<size_t>(b) * oc_n + o) * HW + p] = out[x][o] + b2[o];
+    }
 }
 
 struct FnoLayout {
-    size_t act_bytes, spec_in, spec_out, part_bytes, total;
+    size_t act_bytes, spec_in, spec_out, total;
 };
 
 bool fno_valid(const scx_fno2d_config* c) {
@@ -259,8 +325,7 @@ FnoLayout fno_layout(const scx_fno2d_config* c) {
     const size_t corner = static_cast<size_t>(c->batch_size) * c->hidden * c->modes1 * c->modes2 * 8;
     l.spec_in = a256(corner);
     l.spec_out = l.spec_in;
-    l.part_bytes = a256(static_cast<size_t>(c->batch_size) * c->hidden * ((hw + 31) / 32) * sizeof(float2));
-    l.total = 3 * l.act_bytes + 2 * l.spec_in + 2 * l.spec_out + l.part_bytes;
+    l.total = 3 * l.act_bytes + 2 * l.spec_in + 2 * l.spec_out;
     return l;
 }
 
@@ -278,32 +343,35 @@ cudaError_t run_pixel_kernels_lift(const scx_fno2d_config* cfg, const scx_fno2d_
 }
 
 template <int HMAX>
-cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const float* h, float* h_next, float2* part,
-                               const float* w, const float* bias, cudaStream_t s) {
+cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const float* h, float* h_next, const float* w, const float* bias, cudaStream_t s) {
     const int HW = cfg->height * cfg->width;
-    const dim3 grid((HW + kThreads - 1) / kThreads, cfg->batch_size);
-    fno_skip_kernel<HMAX><<<grid, kThreads, 0, s>>>(spec, h, h_next, part, w, bias, HW, cfg->hidden,
-                                                    cfg->instance_norm);
+    constexpr int PX = HMAX <= 32 ? 2 : 1;  // pixels per thread within the register budget
+    const dim3 grid((HW + kThreads * PX - 1) / (kThreads * PX), cfg->batch_size);
+    fno_skip_kernel<HMAX, PX><<<grid, kThreads, 0, s>>>(spec, h, h_next, w, bias, HW, cfg->hidden,
+                                                        cfg->instance_norm);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || !cfg->instance_norm) return e;
-    fno_norm_gelu_kernel<HMAX><<<grid, kThreads, 0, s>>>(spec, h_next, part, HW, cfg->hidden);
+    fno_norm_gelu_kernel<<<static_cast<unsigned>(cfg->batch_size * cfg->hidden), kThreads, 0, s>>>(spec, h_next,
+                                                                                             HW);
     return cudaGetLastError();
 }
 
 template <int HMAX>
 cudaError_t run_project(const scx_fno2d_config* cfg, const scx_fno2d_params* prm, const float* h, float* y,
                         cudaStream_t s) {
+    // one pixel per thread: with two, the 128-unit loop runs on too few warps to hide its latency
+    constexpr int PX = 1;
     const int HW = cfg->height * cfg->width;
-    const dim3 grid((HW + kThreads - 1) / kThreads, cfg->batch_size);
+    const dim3 grid((HW + kThreads * PX - 1) / (kThreads * PX), cfg->batch_size);
     const size_t smem = static_cast<size_t>(cfg->proj_hidden * HMAX + cfg->proj_hidden +
                                             cfg->out_channels * cfg->proj_hidden) * 4;
     int per_sm = 1;
-    cudaError_t e = scx::prepare_kernel(reinterpret_cast<const void*>(fno_project_kernel<HMAX>), smem, kThreads,
+    cudaError_t e = scx::prepare_kernel(reinterpret_cast<const void*>(fno_project_kernel<HMAX, PX>), smem, kThreads,
                                         &per_sm);
     if (e != cudaSuccess) return e;
-    fno_project_kernel<HMAX><<<grid, kThreads, smem, s>>>(h, y, prm->proj1_w, prm->proj1_b, prm->proj2_w,
-                                                          prm->proj2_b, HW, cfg->hidden, cfg->proj_hidden,
-                                                          cfg->out_channels);
+    fno_project_kernel<HMAX, PX><<<grid, kThreads, smem, s>>>(h, y, prm->proj1_w, prm->proj1_b, prm->proj2_w,
+                                                              prm->proj2_b, HW, cfg->hidden, cfg->proj_hidden,
+                                                              cfg->out_channels);
     return cudaGetLastError();
 }
 
@@ -339,7 +407,6 @@ extern "C" int scx_fno2d_fwd(const scx_fno2d_config* cfg, const scx_fno2d_params
     float2* X2 = reinterpret_cast<float2*>(sp + L.spec_in);
     float2* Y1 = reinterpret_cast<float2*>(sp + 2 * L.spec_in);
     float2* Y2 = reinterpret_cast<float2*>(sp + 2 * L.spec_in + L.spec_out);
-    float2* part = reinterpret_cast<float2*>(sp + 2 * L.spec_in + 2 * L.spec_out);
     const int hmax = hmax_for(C);
 
     e = hmax == 16 ? run_pixel_kernels_lift<16>(cfg, prm, x, act[0], s)
@@ -359,12 +426,11 @@ extern "C" int scx_fno2d_fwd(const scx_fno2d_config* cfg, const scx_fno2d_params
         if (e != cudaSuccess) return e;
         e = scx::dft_inv(Y1, Y2, NM, m2, act[spec], B * C, H, W, m1, m2, *tw, s);
         if (e != cudaSuccess) return e;
-        e = hmax == 16 ? run_layer_epilogue<16>(cfg, act[spec], act[cur], act[nxt], part, prm->skip_w[l],
-                                                prm->skip_b[l], s)
-                       : (hmax == 32 ? run_layer_epilogue<32>(cfg, act[spec], act[cur], act[nxt], part,
-                                                              prm->skip_w[l], prm->skip_b[l], s)
-                                     : run_layer_epilogue<64>(cfg, act[spec], act[cur], act[nxt], part,
-                                                              prm->skip_w[l], prm->skip_b[l], s));
+        e = hmax == 16 ? run_layer_epilogue<16>(cfg, act[spec], act[cur], act[nxt], prm->skip_w[l], prm->skip_b[l], s)
+                       : (hmax == 32 ? run_layer_epilogue<32>(cfg, act[spec], act[cur], act[nxt], prm->skip_w[l],
+                                                              prm->skip_b[l], s)
+                                     : run_layer_epilogue<64>(cfg, act[spec], act[cur], act[nxt], prm->skip_w[l],
+                                                              prm->skip_b[l], s));
         if (e != cudaSuccess) return e;
         cur = nxt;
     }

@@ -9,7 +9,8 @@
 //                              normalisation and GELU (fno_ns/model.py:96-99,133-134)
 //   fno_project_kernel         per pixel: hidden -> proj_hidden (GELU) -> out_channels, the
 //                              proj_hidden-wide intermediate never leaves registers
-//                              (fno_ns/model.py:162-166)
+//                              (fno_ns/model.py:162-166); the shapes scx_fno_proj_tc.cu
+//                              supports run its tensor-core version instead
 #include <algorithm>
 #include <cmath>
 
@@ -359,9 +360,14 @@ cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const f
 template <int HMAX>
 cudaError_t run_project(const scx_fno2d_config* cfg, const scx_fno2d_params* prm, const float* h, float* y,
                         cudaStream_t s) {
-    // one pixel per thread: with two, the 128-unit loop runs on too few warps to hide its latency
-    constexpr int PX = 1;
     const int HW = cfg->height * cfg->width;
+    if (scx::fno_project_tc_supported(cfg->hidden, cfg->proj_hidden, cfg->out_channels, HW) &&
+        ((reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(prm->proj1_w)) & 15) == 0)
+        return scx::launch_fno_project_tc(h, y, prm->proj1_w, prm->proj1_b, prm->proj2_w, prm->proj2_b,
+                                          cfg->batch_size, HW, cfg->hidden, cfg->proj_hidden, cfg->out_channels, s);
+    // FFMA fallback, one pixel per thread: with two, the 128-unit loop runs on too few warps to
+    // hide its latency
+    constexpr int PX = 1;
     const dim3 grid((HW + kThreads * PX - 1) / (kThreads * PX), cfg->batch_size);
     const size_t smem = static_cast<size_t>(cfg->proj_hidden * HMAX + cfg->proj_hidden +
                                             cfg->out_channels * cfg->proj_hidden) * 4;

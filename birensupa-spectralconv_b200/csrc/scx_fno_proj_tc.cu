@@ -2,15 +2,17 @@
 //
 //   y[b][oc][p] = b2[oc] + sum_j W2[oc][j] GELU(b1[j] + sum_c W1[j][c] h[b][c][p])
 //
-// One CTA (4 warps) per tile of 128 pixels of one batch item.  The first layer is a GEMM
+// One CTA (8 warps) per tile of 128 pixels of one batch item.  The first layer is a GEMM
 // D[pixel][j] = sum_c h[c][pixel] W1[j][c] (M = 128 pixels, N = proj_hidden, K = hidden) in
-// bf16x3 (hi*hi + hi*lo + lo*hi, fp32 TMEM accumulator):
-//   A = the h tile, MN-major in shared memory (pixels are contiguous for a fixed channel in
-//       h's [B][C][H*W] layout), split into bf16 hi/lo by the CTA's threads;
+// 3xTF32 (hi*hi + hi*lo + lo*hi with hi = the top 19 bits and lo = the exact remainder, fp32
+// TMEM accumulator; about 1e-6 relative per product, where bf16x3's 2e-5 was too coarse for
+// 32-term sums feeding the output):
+//   A = the h tile, K-major in shared memory (transposed from h's [B][C][H*W] layout while it
+//       is split by the CTA's threads);
 //   B = W1, K-major in shared memory, split the same way.
-// Lane l of warp w then holds pixel 32w + l: it reads its row of D from TMEM 32 columns at a
-// time and finishes bias, GELU and the second layer in registers, taking the hidden units in
-// order j = 0, 1, ... like fno_project_kernel.  The wait for the MMAs is bounded (about a
+// Lane l of warps w and w + 4 then holds pixel 32w + l: each reads half of its row of D from
+// TMEM, 16 columns at a time, and finishes bias, GELU and the second layer for its half of the
+// hidden units in order; the two halves' sums are added through shared memory.  The wait for the MMAs is bounded (about a
 // second); a CTA that gives up stores a code in the device watchdog word and writes nothing.
 #include "scx_internal.h"
 #include "scx_tc.cuh"
@@ -18,11 +20,71 @@
 namespace scx {
 namespace {
 
-constexpr int kProjThreads = 128;  // 4 warps: one TMEM sub-partition each
+constexpr int kProjThreads = 256;  // 8 warps: two per TMEM sub-partition
 constexpr int kTile = 128;         // pixels per CTA (MMA M)
 constexpr int kMaxOut = 4;
 
 __device__ __forceinline__ float gelu(float z) { return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f)); }
+
+// W [N][K] (row-major, K = channels) -> tf32 hi/lo (fp32 containers), K-major SW128: 4
+// consecutive k of row n per 16-byte unit.
+__device__ __forceinline__ void stage_weights(const float* __restrict__ w, int N, int K, uint8_t* w_hi,
+                                              uint8_t* w_lo) {
+    for (int u = threadIdx.x; u < N * (K / 4); u += blockDim.x) {
+        const int n = u / (K / 4), k0 = (u % (K / 4)) * 4;
+        const float4 v = __ldg(reinterpret_cast<const float4*>(w + static_cast<size_t>(n) * K + k0));
+        float4 hi, lo;
+        tc::split_tf32(v.x, hi.x, lo.x);
+        tc::split_tf32(v.y, hi.y, lo.y);
+        tc::split_tf32(v.z, hi.z, lo.z);
+        tc::split_tf32(v.w, hi.w, lo.w);
+        const uint32_t off = tc::kmajor_offset32(N, n, k0);
+        *reinterpret_cast<float4*>(w_hi + off) = hi;
+        *reinterpret_cast<float4*>(w_lo + off) = lo;
+    }
+}
+
+// The [C][kTile] pixel tile at hb (channel stride HW) -> tf32 hi/lo, K-major SW128 (row =
+// pixel, K = channel): each unit reads 4 channels of one pixel (consecutive lanes take
+// consecutive pixels, so every load instruction reads 128 contiguous bytes) and writes one
+// 16-byte unit.
+__device__ __forceinline__ void stage_tile(const float* __restrict__ hb, int C, int HW, uint8_t* a_hi,
+                                           uint8_t* a_lo) {
+    for (int u = threadIdx.x; u < kTile * (C / 4); u += blockDim.x) {
+        const int m = u % kTile, c0 = (u / kTile) * 4;
+        const float* src = hb + static_cast<size_t>(c0) * HW + m;
+        float4 hi, lo;
+        tc::split_tf32(__ldg(src), hi.x, lo.x);
+        tc::split_tf32(__ldg(src + HW), hi.y, lo.y);
+        tc::split_tf32(__ldg(src + 2 * static_cast<size_t>(HW)), hi.z, lo.z);
+        tc::split_tf32(__ldg(src + 3 * static_cast<size_t>(HW)), hi.w, lo.w);
+        const uint32_t off = tc::kmajor_offset32(kTile, m, c0);
+        *reinterpret_cast<float4*>(a_hi + off) = hi;
+        *reinterpret_cast<float4*>(a_lo + off) = lo;
+    }
+}
+
+// D[pixel][n] = sum_c tile[c][pixel] W[n][c] in 3xTF32 ((A_hi, W_hi), (A_hi, W_lo), (A_lo, W_hi)
+// chained along K, 8 channels per instruction), issued by the calling thread, completion on
+// `done`.
+__device__ __forceinline__ void issue_gemm(uint32_t tmem, const uint8_t* w_hi, const uint8_t* w_lo,
+                                           const uint8_t* a_hi, const uint8_t* a_lo, int N, int K, uint64_t* done) {
+    const uint64_t dW[2] = {tc::desc_sw128(tc::smem_u32(w_hi)), tc::desc_sw128(tc::smem_u32(w_lo))};
+    const uint64_t dA[2] = {tc::desc_sw128(tc::smem_u32(a_hi)), tc::desc_sw128(tc::smem_u32(a_lo))};
+    const uint32_t id = tc::idesc_tf32(kTile, N);
+    for (int part = 0; part < 3; ++part) {
+        const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
+        for (int ks = 0; ks < K / 8; ++ks) {
+            // K blocks of 32 channels: rows * 128 bytes apart; 32 bytes per K step within one
+            const uint32_t ao = (static_cast<uint32_t>(ks >> 2) * kTile * 128u + (ks & 3) * 32u) >> 4;
+            const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * static_cast<uint32_t>(N) * 128u + (ks & 3) * 32u) >> 4;
+            tc::mma_tf32(tmem, dA[ap] + ao, dW[bp] + bo, id, (part | ks) ? 1u : 0u);
+        }
+    }
+    tc::mma_commit(done);
+}
+
+uint32_t tmem_cols_for(int n) { return n <= 32 ? 32u : (n <= 64 ? 64u : (n <= 128 ? 128u : 256u)); }
 
 struct ProjArgs {
     const float* h;
@@ -36,8 +98,7 @@ struct ProjArgs {
     int* watchdog;
 };
 
-// Shared memory: W1 hi | W1 lo (K-major SW128, ph rows of 128 bytes each) | h tile hi | lo
-// (MN-major SW128: C/8 K-groups of 2 x 1 KB MN atoms) | b1 | w2.
+// Shared memory: W1 hi | W1 lo | h tile hi | h tile lo (all K-major SW128, fp32) | b1 | w2.
 __global__ void __launch_bounds__(kProjThreads) fno_project_tc_kernel(const ProjArgs a) {
     extern __shared__ uint8_t proj_raw[];
     __shared__ uint64_t done;
@@ -45,51 +106,26 @@ __global__ void __launch_bounds__(kProjThreads) fno_project_tc_kernel(const Proj
     uint8_t* base = tc::align1024(proj_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int C = a.C, ph = a.ph;
-    const uint32_t WB = static_cast<uint32_t>(ph) * 128u;       // one W1 part
-    const uint32_t AB = static_cast<uint32_t>(C / 8) * 2048u;   // one h part
+    const uint32_t WB = static_cast<uint32_t>(ph) * C * 4u;     // one W1 part
+    const uint32_t AB = static_cast<uint32_t>(kTile) * C * 4u;  // one h part
     uint8_t* w_hi = base;
     uint8_t* w_lo = base + WB;
     uint8_t* a_hi = base + 2 * WB;
     uint8_t* a_lo = a_hi + AB;
     float* b1s = reinterpret_cast<float*>(a_lo + AB);
     float* w2s = b1s + ph;
+    float* part = w2s + a.oc * ph;  // [kMaxOut][kTile]: the second half's partial outputs
 
     if (warp == 0) {
         tc::tmem_alloc(&tmem_base, a.tmem_cols);
         tc::tmem_relinquish();
     }
     if (tid == 0) tc::mbar_init(&done, 1);
-
-    // W1 -> bf16 hi/lo, K-major: 8 consecutive channels of row j per 16-byte unit
-    for (int u = tid; u < ph * (C / 8); u += kProjThreads) {
-        const int j = u / (C / 8), c0 = (u % (C / 8)) * 8;
-        const float4* src = reinterpret_cast<const float4*>(a.w1 + static_cast<size_t>(j) * C + c0);
-        const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
-        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        uint4 hi, lo;
-        tc::split8(v, hi, lo);
-        const uint32_t off = tc::kmajor_offset(ph, j, c0);
-        *reinterpret_cast<uint4*>(w_hi + off) = hi;
-        *reinterpret_cast<uint4*>(w_lo + off) = lo;
-    }
-    // h tile -> bf16 hi/lo, MN-major: 8 consecutive pixels of channel c per 16-byte unit
+    stage_weights(a.w1, ph, C, w_hi, w_lo);
     const int tiles_per_plane = a.HW / kTile;
     const int b = blockIdx.x / tiles_per_plane;
     const int p0 = (blockIdx.x % tiles_per_plane) * kTile;
-    const float* hb = a.h + static_cast<size_t>(b) * C * a.HW + p0;
-    for (int u = tid; u < C * (kTile / 8); u += kProjThreads) {
-        const int c = u / (kTile / 8), m0 = (u % (kTile / 8)) * 8;
-        const float4* src = reinterpret_cast<const float4*>(hb + static_cast<size_t>(c) * a.HW + m0);
-        const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
-        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        uint4 hi, lo;
-        tc::split8(v, hi, lo);
-        const uint32_t off = static_cast<uint32_t>(c >> 3) * 2048u + static_cast<uint32_t>(m0 >> 6) * 1024u +
-                             static_cast<uint32_t>(c & 7) * 128u +
-                             (static_cast<uint32_t>(((m0 & 63) >> 3) ^ (c & 7)) << 4);
-        *reinterpret_cast<uint4*>(a_hi + off) = hi;
-        *reinterpret_cast<uint4*>(a_lo + off) = lo;
-    }
+    stage_tile(a.h + static_cast<size_t>(b) * C * a.HW + p0, C, a.HW, a_hi, a_lo);
     for (int i = tid; i < ph; i += kProjThreads) b1s[i] = __ldg(a.b1 + i);
     for (int i = tid; i < a.oc * ph; i += kProjThreads) w2s[i] = __ldg(a.w2 + i);
     tc::fence_async_smem();
@@ -97,49 +133,45 @@ __global__ void __launch_bounds__(kProjThreads) fno_project_tc_kernel(const Proj
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = tmem_base;
-
-    if (tid == 0) {
-        const uint32_t sb = tc::smem_u32(base);
-        const uint64_t dW[2] = {tc::desc_sw128(sb), tc::desc_sw128(sb + WB)};
-        const uint64_t dA[2] = {tc::desc_mn_sw128(sb + 2 * WB, 1024u, 2048u),
-                                tc::desc_mn_sw128(sb + 2 * WB + AB, 1024u, 2048u)};
-        const uint32_t id = tc::idesc_bf16(kTile, ph) | tc::kIdescAMajorMN;
-        // (h_hi, W_hi), (h_hi, W_lo), (h_lo, W_hi), chained along K
-        for (int part = 0; part < 3; ++part) {
-            const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
-            for (int ks = 0; ks < C / 16; ++ks) {
-                const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4, bo = (static_cast<uint32_t>(ks) * 32u) >> 4;
-                tc::mma_bf16(tmem, dA[ap] + ao, dW[bp] + bo, id, (part | ks) ? 1u : 0u);
-            }
-        }
-        tc::mma_commit(&done);
-    }
+    if (tid == 0) issue_gemm(tmem, w_hi, w_lo, a_hi, a_lo, ph, C, &done);
     const bool ok = tc::mbar_wait_bounded(&done, 0);
     tc::fence_after_sync();
-    if (ok) {
-        float out[kMaxOut];
+    // warps w and w + 4 read the same TMEM lanes (pixels 32 (w % 4) ..): the first takes the
+    // hidden units [0, ph/2), the second [ph/2, ph); the outputs are the first half's sums plus
+    // the second's
+    const int sub = warp & 3, half = warp >> 2, m = sub * 32 + lane;
+    float out[kMaxOut];
 #pragma unroll
-        for (int o = 0; o < kMaxOut; ++o) out[o] = 0.f;
-        const uint32_t row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-        for (int j0 = 0; j0 < ph; j0 += 32) {
-            float v[32];
-            tc::tmem_ld32_nowait(row + static_cast<uint32_t>(j0), v);
+    for (int o = 0; o < kMaxOut; ++o) out[o] = 0.f;
+    if (ok) {
+        const uint32_t row = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+        const int jh = ph / 2;
+        for (int j0 = half * jh; j0 < (half + 1) * jh; j0 += 16) {
+            float v[16];
+            tc::tmem_ld16_nowait(row + static_cast<uint32_t>(j0), v);
             tc::tmem_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 32; ++k) {
+            for (int k = 0; k < 16; ++k) {
                 const float g = gelu(v[k] + b1s[j0 + k]);
 #pragma unroll
                 for (int o = 0; o < kMaxOut; ++o)
                     if (o < a.oc) out[o] = fmaf(w2s[o * ph + j0 + k], g, out[o]);
             }
         }
-        const int p = p0 + warp * 32 + lane;
+        if (half == 1) {
+#pragma unroll
+            for (int o = 0; o < kMaxOut; ++o) part[o * kTile + m] = out[o];
+        }
+    }
+    __syncthreads();
+    if (ok && half == 0) {
+        const int p = p0 + m;
 #pragma unroll
         for (int o = 0; o < kMaxOut; ++o)
-            if (o < a.oc) a.y[(static_cast<size_t>(b) * a.oc + o) * a.HW + p] = out[o] + __ldg(a.b2 + o);
-    } else if (lane == 0) {
-        atomicExch(a.watchdog, 50);
+            if (o < a.oc)
+                a.y[(static_cast<size_t>(b) * a.oc + o) * a.HW + p] = (out[o] + part[o * kTile + m]) + __ldg(a.b2 + o);
     }
+    if (!ok && tid == 0) atomicExch(a.watchdog, 50);
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) {
@@ -149,14 +181,15 @@ __global__ void __launch_bounds__(kProjThreads) fno_project_tc_kernel(const Proj
 }
 
 size_t proj_smem(int C, int ph, int oc) {
-    return 2u * static_cast<size_t>(ph) * 128u + 2u * static_cast<size_t>(C / 8) * 2048u +
-           static_cast<size_t>(ph + oc * ph) * 4u + 1024u;
+    return 2u * static_cast<size_t>(ph) * C * 4u + 2u * static_cast<size_t>(kTile) * C * 4u +
+           static_cast<size_t>(ph + oc * ph + kMaxOut * kTile) * 4u + 1024u;
 }
 
 }  // namespace
 
 bool fno_project_tc_supported(int hidden, int ph, int oc, int HW) {
-    return hidden % 16 == 0 && hidden >= 16 && hidden <= 64 && ph % 32 == 0 && ph >= 32 && ph <= 256 && oc >= 1 &&
+    // K-major rows are 32 channels (128 bytes) wide, so hidden is 32 or 64
+    return (hidden == 32 || hidden == 64) && ph % 32 == 0 && ph >= 32 && ph <= 256 && oc >= 1 &&
            oc <= kMaxOut && HW % kTile == 0 && proj_smem(hidden, ph, oc) <= 200u * 1024u;
 }
 
@@ -176,7 +209,7 @@ cudaError_t launch_fno_project_tc(const float* h, float* y, const float* w1, con
     a.C = hidden;
     a.ph = ph;
     a.oc = oc;
-    a.tmem_cols = ph <= 32 ? 32u : (ph <= 64 ? 64u : (ph <= 128 ? 128u : 256u));
+    a.tmem_cols = tmem_cols_for(ph);
     cudaError_t e = device_watchdog(&a.watchdog);
     if (e != cudaSuccess) return e;
     const size_t smem = proj_smem(hidden, ph, oc);
@@ -189,3 +222,4 @@ cudaError_t launch_fno_project_tc(const float* h, float* y, const float* w1, con
 }
 
 }  // namespace scx
+

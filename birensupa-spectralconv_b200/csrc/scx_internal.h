@@ -138,8 +138,8 @@ cudaError_t dft_inv(const float2* in1, const float2* in2, long long in_plane_str
 cudaError_t device_watchdog(int** out);
 
 // FNO projection y = b2 + W2 GELU(b1 + W1 h) on the tensor core (scx_fno_proj_tc.cu): h is
-// [B][hidden][HW], y [B][oc][HW].  Supported: hidden a multiple of 16 up to 64, proj_hidden a
-// multiple of 32 up to 256, oc <= 4, HW a multiple of 128, 16-byte aligned h and W1.
+// [B][hidden][HW], y [B][oc][HW].  Supported: hidden 32 or 64, proj_hidden a multiple of 32 up
+// to 256, oc <= 4, HW a multiple of 128, 16-byte aligned h and W1.
 bool fno_project_tc_supported(int hidden, int ph, int oc, int HW);
 cudaError_t launch_fno_project_tc(const float* h, float* y, const float* w1, const float* b1, const float* w2,
                                   const float* b2, int B, int HW, int hidden, int ph, int oc, cudaStream_t stream);

@@ -1,6 +1,8 @@
 // FNO-2d forward (fno_ns/model.py:137-259) as one C-ABI call.
 //
-// Kernels besides the spectral convolution (scx_dft_*.cu, scx_mix.cu):
+// Kernels besides the spectral convolution (scx_dft_*.cu, scx_mix.cu), all launched as
+// programmatic dependents of the previous kernel (each CTA waits with griddepcontrol.wait
+// before its first read of activations; weights are staged before that):
 //   fno_lift_kernel            1x1 conv (T+2 -> hidden) with the grid channels generated
 //                              in-kernel (fno_ns/model.py:168-181,193-195) or read from a
 //                              channels-last input
@@ -16,6 +18,7 @@
 
 #include "scx.h"
 #include "scx_internal.h"
+#include "scx_tc.cuh"
 
 namespace {
 
@@ -38,6 +41,7 @@ __global__ void __launch_bounds__(kThreads) fno_lift_kernel(const float* __restr
                                                             const float* __restrict__ w,
                                                             const float* __restrict__ bias, int H, int W, int T,
                                                             int hidden, int layout) {
+    scx::tc::grid_dep_launch();  // launched as a programmatic dependent: the next kernel may start
     extern __shared__ float lift_smem[];
     const int cin = T + 2;
     float* ws = lift_smem;  // [cin][HMAX] (transposed: one input channel's weights contiguous)
@@ -46,6 +50,7 @@ __global__ void __launch_bounds__(kThreads) fno_lift_kernel(const float* __restr
         ws[i] = c < hidden ? w[c * cin + k] : 0.f;
     }
     __syncthreads();
+    scx::tc::grid_dep_wait();  // inputs may come from the previous kernel in the stream
     const int HW = H * W;
     const int b = blockIdx.y;
     const int p = blockIdx.x * kThreads + threadIdx.x;
@@ -89,12 +94,14 @@ __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ 
                                                             const float* __restrict__ w,
                                                             const float* __restrict__ bias, int HW, int hidden,
                                                             int instance_norm) {
+    scx::tc::grid_dep_launch();
     __shared__ __align__(16) float ws[HMAX * HMAX];  // [o][i], zero padded
     for (int i = threadIdx.x; i < HMAX * HMAX; i += kThreads) {
         const int o = i / HMAX, k = i - o * HMAX;
         ws[i] = (o < hidden && k < hidden) ? w[o * hidden + k] : 0.f;
     }
     __syncthreads();
+    scx::tc::grid_dep_wait();  // s and h come from earlier kernels in the stream
     const int b = blockIdx.y;
     const int p0 = blockIdx.x * kThreads * PX + threadIdx.x;
     if (p0 >= HW) return;
@@ -176,6 +183,8 @@ constexpr int kNormRegs = 16;
 __global__ void __launch_bounds__(kThreads) fno_norm_gelu_kernel(const float* __restrict__ z,
                                                                  float* __restrict__ h_next, int HW) {
     __shared__ float red[kThreads / 32];
+    scx::tc::grid_dep_launch();
+    scx::tc::grid_dep_wait();  // z comes from the skip kernel
     const size_t plane = blockIdx.x;
     const float* zp = z + plane * HW;
     float* hp = h_next + plane * HW;
@@ -230,6 +239,7 @@ __global__ void __launch_bounds__(kThreads) fno_project_kernel(const float* __re
                                                                const float* __restrict__ w2,
                                                                const float* __restrict__ b2, int HW, int hidden,
                                                                int ph, int oc_n) {
+    scx::tc::grid_dep_launch();
     extern __shared__ __align__(16) float proj_smem[];
     float* w1s = proj_smem;          // [ph][HMAX] zero padded
     float* b1s = w1s + ph * HMAX;    // [ph]
@@ -241,6 +251,7 @@ __global__ void __launch_bounds__(kThreads) fno_project_kernel(const float* __re
     for (int i = threadIdx.x; i < ph; i += kThreads) b1s[i] = b1[i];
     for (int i = threadIdx.x; i < oc_n * ph; i += kThreads) w2s[i] = w2[i];
     __syncthreads();
+    scx::tc::grid_dep_wait();  // h comes from the last layer's kernels
     const int b = blockIdx.y;
     const int p0 = blockIdx.x * kThreads * PX + threadIdx.x;
     if (p0 >= HW) return;
@@ -338,9 +349,8 @@ cudaError_t run_pixel_kernels_lift(const scx_fno2d_config* cfg, const scx_fno2d_
     const int HW = cfg->height * cfg->width;
     const dim3 grid((HW + kThreads - 1) / kThreads, cfg->batch_size);
     const size_t smem = static_cast<size_t>(cfg->in_frames + 2) * HMAX * 4;
-    fno_lift_kernel<HMAX><<<grid, kThreads, smem, s>>>(x, h0, prm->lift_w, prm->lift_b, cfg->height, cfg->width,
-                                                       cfg->in_frames, cfg->hidden, cfg->input_layout);
-    return cudaGetLastError();
+    return scx::launch_chained(fno_lift_kernel<HMAX>, grid, dim3(kThreads), smem, s, x, h0, prm->lift_w, prm->lift_b,
+                               cfg->height, cfg->width, cfg->in_frames, cfg->hidden, cfg->input_layout);
 }
 
 template <int HMAX>
@@ -348,13 +358,11 @@ cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const f
     const int HW = cfg->height * cfg->width;
     constexpr int PX = HMAX <= 32 ? 2 : 1;  // pixels per thread within the register budget
     const dim3 grid((HW + kThreads * PX - 1) / (kThreads * PX), cfg->batch_size);
-    fno_skip_kernel<HMAX, PX><<<grid, kThreads, 0, s>>>(spec, h, h_next, w, bias, HW, cfg->hidden,
-                                                        cfg->instance_norm);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = scx::launch_chained(fno_skip_kernel<HMAX, PX>, grid, dim3(kThreads), 0, s, spec, h, h_next, w,
+                                        bias, HW, cfg->hidden, cfg->instance_norm);
     if (e != cudaSuccess || !cfg->instance_norm) return e;
-    fno_norm_gelu_kernel<<<static_cast<unsigned>(cfg->batch_size * cfg->hidden), kThreads, 0, s>>>(spec, h_next,
-                                                                                             HW);
-    return cudaGetLastError();
+    return scx::launch_chained(fno_norm_gelu_kernel, dim3(static_cast<unsigned>(cfg->batch_size * cfg->hidden)),
+                               dim3(kThreads), 0, s, spec, h_next, HW);
 }
 
 template <int HMAX>
@@ -375,10 +383,9 @@ cudaError_t run_project(const scx_fno2d_config* cfg, const scx_fno2d_params* prm
     cudaError_t e = scx::prepare_kernel(reinterpret_cast<const void*>(fno_project_kernel<HMAX, PX>), smem, kThreads,
                                         &per_sm);
     if (e != cudaSuccess) return e;
-    fno_project_kernel<HMAX, PX><<<grid, kThreads, smem, s>>>(h, y, prm->proj1_w, prm->proj1_b, prm->proj2_w,
-                                                              prm->proj2_b, HW, cfg->hidden, cfg->proj_hidden,
-                                                              cfg->out_channels);
-    return cudaGetLastError();
+    return scx::launch_chained(fno_project_kernel<HMAX, PX>, grid, dim3(kThreads), smem, s, h, y, prm->proj1_w,
+                               prm->proj1_b, prm->proj2_w, prm->proj2_b, HW, cfg->hidden, cfg->proj_hidden,
+                               cfg->out_channels);
 }
 
 }  // namespace

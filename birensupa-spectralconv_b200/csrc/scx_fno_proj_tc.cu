@@ -120,14 +120,18 @@ __global__ void __launch_bounds__(kProjThreads) fno_project_tc_kernel(const Proj
         tc::tmem_alloc(&tmem_base, a.tmem_cols);
         tc::tmem_relinquish();
     }
-    if (tid == 0) tc::mbar_init(&done, 1);
+    if (tid == 0) {
+        tc::grid_dep_launch();  // launched as a programmatic dependent: the next kernel may start
+        tc::mbar_init(&done, 1);
+    }
     stage_weights(a.w1, ph, C, w_hi, w_lo);
+    for (int i = tid; i < ph; i += kProjThreads) b1s[i] = __ldg(a.b1 + i);
+    for (int i = tid; i < a.oc * ph; i += kProjThreads) w2s[i] = __ldg(a.w2 + i);
+    tc::grid_dep_wait();  // h comes from the last layer's kernels
     const int tiles_per_plane = a.HW / kTile;
     const int b = blockIdx.x / tiles_per_plane;
     const int p0 = (blockIdx.x % tiles_per_plane) * kTile;
     stage_tile(a.h + static_cast<size_t>(b) * C * a.HW + p0, C, a.HW, a_hi, a_lo);
-    for (int i = tid; i < ph; i += kProjThreads) b1s[i] = __ldg(a.b1 + i);
-    for (int i = tid; i < a.oc * ph; i += kProjThreads) w2s[i] = __ldg(a.w2 + i);
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
@@ -217,8 +221,7 @@ cudaError_t launch_fno_project_tc(const float* h, float* y, const float* w1, con
     e = prepare_kernel(reinterpret_cast<const void*>(fno_project_tc_kernel), smem, kProjThreads, &per_sm);
     if (e != cudaSuccess) return e;
     const unsigned grid = static_cast<unsigned>(static_cast<long long>(B) * (HW / kTile));
-    fno_project_tc_kernel<<<grid, kProjThreads, smem, stream>>>(a);
-    return cudaGetLastError();
+    return launch_chained(fno_project_tc_kernel, dim3(grid), dim3(kProjThreads), smem, stream, a);
 }
 
 }  // namespace scx

@@ -462,7 +462,7 @@ def ours(args) -> None:
             "clocks": res["clocks"], "gpu_launches": res["launches_per_step"] * args.steps,
             "workloads": extras,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -511,10 +511,25 @@ def reference(args) -> None:
                                    "einsum recipe (reference_pytorch.py) restated, on the host CPU"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+# The JSON result line goes to the process's original stdout; file descriptor 1 itself is
+# pointed at stderr, so that banners printed by native libraries (NCCL's version line, for
+# one) cannot land in front of it.
+_RESULT_OUT = None
+
+
+def emit(line: dict) -> None:
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    print(json.dumps(line), file=out, flush=True)
 
 
 def main() -> None:
+    global _RESULT_OUT
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse_args()
     if args.impl == "reference":
         reference(args)

@@ -87,7 +87,10 @@ __global__ void __launch_bounds__(kThreads) fno_lift_kernel(const float* __restr
 // written over s when instance_norm is on (part B normalises it), else GELU(z) written to
 // h_next.  Each thread takes PX pixels kThreads apart (one shared-memory read of a weight row
 // feeds PX pixels) and four output channels per pass (independent FMA chains; each channel's
-// sum keeps its order over i).  grid = (ceil(HW / (kThreads * PX)), B)
+// sum keeps its order over i); the output channels are split into groups of kSkipGroup over
+// grid.z, for enough warps per SM.  grid = (ceil(HW / (kThreads * PX)), B, ceil(hidden / kSkipGroup))
+constexpr int kSkipGroup = 8;
+
 template <int HMAX, int PX>
 __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ s, const float* __restrict__ h,
                                                             float* __restrict__ h_next,
@@ -119,7 +122,8 @@ __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ 
 #pragma unroll
         for (int i = 0; i < HMAX; ++i)
             hv[x][i] = i < hidden ? __ldg(h + plane0 + static_cast<size_t>(i) * HW + pix[x]) : 0.f;
-    for (int o0 = 0; o0 < hidden; o0 += 4) {
+    const int o_end = min(hidden, static_cast<int>(blockIdx.z + 1) * kSkipGroup);
+    for (int o0 = blockIdx.z * kSkipGroup; o0 < o_end; o0 += 4) {
         float z[4][PX];
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
@@ -144,7 +148,7 @@ __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ 
         }
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-            if (o0 + t >= hidden) break;
+            if (o0 + t >= o_end) break;
             const size_t row = plane0 + static_cast<size_t>(o0 + t) * HW;
 #pragma unroll
             for (int x = 0; x < PX; ++x) {
@@ -357,7 +361,8 @@ template <int HMAX>
 cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const float* h, float* h_next, const float* w, const float* bias, cudaStream_t s) {
     const int HW = cfg->height * cfg->width;
     constexpr int PX = HMAX <= 32 ? 2 : 1;  // pixels per thread within the register budget
-    const dim3 grid((HW + kThreads * PX - 1) / (kThreads * PX), cfg->batch_size);
+    const dim3 grid((HW + kThreads * PX - 1) / (kThreads * PX), cfg->batch_size,
+                    (cfg->hidden + kSkipGroup - 1) / kSkipGroup);
     cudaError_t e = scx::launch_chained(fno_skip_kernel<HMAX, PX>, grid, dim3(kThreads), 0, s, spec, h, h_next, w,
                                         bias, HW, cfg->hidden, cfg->instance_norm);
     if (e != cudaSuccess || !cfg->instance_norm) return e;

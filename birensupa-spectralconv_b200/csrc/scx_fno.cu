@@ -162,6 +162,76 @@ __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ 
     }
 }
 
+// The same skip GEMM with four consecutive pixels per thread (float4 loads and stores), for
+// planes whose pixel count is a multiple of 4 and hidden a multiple of 16: input channels in
+// blocks of 16, each float4 of weights feeding 16 FMAs.  Each output keeps the order bias + s,
+// then i = 0, 1, ..., so the results equal fno_skip_kernel's bit for bit.
+// grid = (ceil(HW / (4 * kThreads)), B, ceil(hidden / kSkipGroup))
+template <int HMAX>
+__global__ void __launch_bounds__(kThreads) fno_skip_quad_kernel(float* __restrict__ s, const float* __restrict__ h,
+                                                                 float* __restrict__ h_next,
+                                                                 const float* __restrict__ w,
+                                                                 const float* __restrict__ bias, int HW, int hidden,
+                                                                 int instance_norm) {
+    scx::tc::grid_dep_launch();
+    __shared__ __align__(16) float ws[HMAX * HMAX];  // [o][i], zero padded
+    for (int i = threadIdx.x; i < HMAX * HMAX; i += kThreads) {
+        const int o = i / HMAX, k = i - o * HMAX;
+        ws[i] = (o < hidden && k < hidden) ? w[o * hidden + k] : 0.f;
+    }
+    __syncthreads();
+    scx::tc::grid_dep_wait();  // s and h come from earlier kernels in the stream
+    const int HW4 = HW / 4;
+    const int q = blockIdx.x * kThreads + threadIdx.x;  // pixel quad
+    if (q >= HW4) return;
+    const int b = blockIdx.y;
+    const int o_begin = blockIdx.z * kSkipGroup, o_end = min(hidden, o_begin + kSkipGroup);
+    const size_t plane0 = static_cast<size_t>(b) * hidden * HW;
+    const float4* h4 = reinterpret_cast<const float4*>(h + plane0) + q;
+    float4* s4 = reinterpret_cast<float4*>(s + plane0) + q;
+    float4 z[kSkipGroup];
+#pragma unroll
+    for (int t = 0; t < kSkipGroup; ++t) {
+        const int o = min(o_begin + t, hidden - 1);
+        const float bo = __ldg(bias + o);
+        const float4 sv = s4[static_cast<size_t>(o) * HW4];
+        z[t] = make_float4(bo + sv.x, bo + sv.y, bo + sv.z, bo + sv.w);
+    }
+    for (int i0 = 0; i0 < hidden; i0 += 16) {
+        float4 hv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) hv[i] = __ldg(h4 + static_cast<size_t>(i0 + i) * HW4);
+#pragma unroll
+        for (int t = 0; t < kSkipGroup; ++t) {
+            const float4* wr = reinterpret_cast<const float4*>(ws + min(o_begin + t, hidden - 1) * HMAX + i0);
+#pragma unroll
+            for (int i4 = 0; i4 < 4; ++i4) {
+                const float4 wv = wr[i4];
+                const float wk[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 hk = hv[4 * i4 + k];
+                    z[t].x = fmaf(wk[k], hk.x, z[t].x);
+                    z[t].y = fmaf(wk[k], hk.y, z[t].y);
+                    z[t].z = fmaf(wk[k], hk.z, z[t].z);
+                    z[t].w = fmaf(wk[k], hk.w, z[t].w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kSkipGroup; ++t) {
+        const int o = o_begin + t;
+        if (o >= o_end) break;
+        if (instance_norm) {
+            s4[static_cast<size_t>(o) * HW4] = z[t];
+        } else {
+            reinterpret_cast<float4*>(h_next + plane0)[static_cast<size_t>(o) * HW4 + q] =
+                make_float4(gelu_erf(z[t].x), gelu_erf(z[t].y), gelu_erf(z[t].z), gelu_erf(z[t].w));
+        }
+    }
+}
+
 // Sum over the CTA in a fixed order (per-warp butterflies, then warp 0 adds the warp sums in
 // warp order); every thread gets the result.
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -360,11 +430,20 @@ cudaError_t run_pixel_kernels_lift(const scx_fno2d_config* cfg, const scx_fno2d_
 template <int HMAX>
 cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const float* h, float* h_next, const float* w, const float* bias, cudaStream_t s) {
     const int HW = cfg->height * cfg->width;
-    constexpr int PX = HMAX <= 32 ? 2 : 1;  // pixels per thread within the register budget
-    const dim3 grid((HW + kThreads * PX - 1) / (kThreads * PX), cfg->batch_size,
-                    (cfg->hidden + kSkipGroup - 1) / kSkipGroup);
-    cudaError_t e = scx::launch_chained(fno_skip_kernel<HMAX, PX>, grid, dim3(kThreads), 0, s, spec, h, h_next, w,
-                                        bias, HW, cfg->hidden, cfg->instance_norm);
+    cudaError_t e;
+    if (HW % 4 == 0 && cfg->hidden % 16 == 0 &&
+        ((reinterpret_cast<uintptr_t>(spec) | reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(h_next)) &
+         15) == 0) {
+        const dim3 grid((HW / 4 + kThreads - 1) / kThreads, cfg->batch_size, (cfg->hidden + kSkipGroup - 1) / kSkipGroup);
+        e = scx::launch_chained(fno_skip_quad_kernel<HMAX>, grid, dim3(kThreads), 0, s, spec, h, h_next, w, bias, HW,
+                                cfg->hidden, cfg->instance_norm);
+    } else {
+        constexpr int PX = HMAX <= 32 ? 2 : 1;  // pixels per thread within the register budget
+        const dim3 grid((HW + kThreads * PX - 1) / (kThreads * PX), cfg->batch_size,
+                        (cfg->hidden + kSkipGroup - 1) / kSkipGroup);
+        e = scx::launch_chained(fno_skip_kernel<HMAX, PX>, grid, dim3(kThreads), 0, s, spec, h, h_next, w, bias, HW,
+                                cfg->hidden, cfg->instance_norm);
+    }
     if (e != cudaSuccess || !cfg->instance_norm) return e;
     return scx::launch_chained(fno_norm_gelu_kernel, dim3(static_cast<unsigned>(cfg->batch_size * cfg->hidden)),
                                dim3(kThreads), 0, s, spec, h_next, HW);

@@ -263,6 +263,41 @@ __global__ void __launch_bounds__(kThreads) fno_norm_gelu_kernel(const float* __
     const float* zp = z + plane * HW;
     float* hp = h_next + plane * HW;
     const float inv_n = 1.0f / static_cast<float>(HW);
+    if ((HW & 3) == 0 && HW <= kNormRegs * kThreads) {
+        // the same with 16-byte accesses: element 4 (tid + k kThreads) + e of the plane
+        const float4* z4 = reinterpret_cast<const float4*>(zp);
+        float4* h4 = reinterpret_cast<float4*>(hp);
+        const int HW4 = HW / 4;
+        float4 v[kNormRegs / 4];
+#pragma unroll
+        for (int k = 0; k < kNormRegs / 4; ++k) {
+            const int i = threadIdx.x + k * kThreads;
+            v[k] = i < HW4 ? __ldg(z4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float sum = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormRegs / 4; ++k) sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+        const float mean = block_sum(sum, red) * inv_n;
+        float m2 = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormRegs / 4; ++k) {
+            if (threadIdx.x + k * kThreads >= HW4) continue;
+            const float dx = v[k].x - mean, dy = v[k].y - mean, dz = v[k].z - mean, dw = v[k].w - mean;
+            m2 = fmaf(dx, dx, m2);
+            m2 = fmaf(dy, dy, m2);
+            m2 = fmaf(dz, dz, m2);
+            m2 = fmaf(dw, dw, m2);
+        }
+        const float rstd = 1.0f / sqrtf(block_sum(m2, red) * inv_n + 1e-5f);
+#pragma unroll
+        for (int k = 0; k < kNormRegs / 4; ++k) {
+            const int i = threadIdx.x + k * kThreads;
+            if (i < HW4)
+                h4[i] = make_float4(gelu_erf((v[k].x - mean) * rstd), gelu_erf((v[k].y - mean) * rstd),
+                                    gelu_erf((v[k].z - mean) * rstd), gelu_erf((v[k].w - mean) * rstd));
+        }
+        return;
+    }
     if (HW <= kNormRegs * kThreads) {
         float v[kNormRegs];
 #pragma unroll

@@ -380,7 +380,9 @@ def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
     ms = t_ms / steps
     del graph
     return {"ms_per_step": ms, "samples_per_s": world * B / (ms / 1e3), "batch_per_gpu": B,
-            "launches_per_step": 2 + 5 * fw["layers"], "cuda_graph": True,
+            # lift, then per layer forward DFT, mixing, inverse DFT and the fused skip +
+            # instance norm + GELU (one cluster launch at 64x64), then the projection
+            "launches_per_step": 2 + 4 * fw["layers"], "cuda_graph": True,
             "gather": "nccl all_gather_into_tensor to rank 0 inside the step" if world > 1 else None,
             "l2": "256 MiB flush between steps (not timed)"}
 

@@ -6,13 +6,20 @@
 //   fno_lift_kernel            1x1 conv (T+2 -> hidden) with the grid channels generated
 //                              in-kernel (fno_ns/model.py:168-181,193-195) or read from a
 //                              channels-last input
-//   fno_skip_kernel            per pixel: z = spectral + W h + b for every output channel
-//   fno_norm_gelu_kernel       one CTA per plane: two-pass instance statistics, then
-//                              normalisation and GELU (fno_ns/model.py:96-99,133-134)
+//   fno_skip_norm_kernel       with instance norm, planes of up to 8192 pixels (a multiple
+//                              of 4): skip GEMM, two-pass instance statistics over a
+//                              thread-block cluster per plane group, normalisation and GELU
+//                              (fno_ns/model.py:96-99,133-134) in one launch
+//   fno_skip_kernel            otherwise, per pixel: z = spectral + W h + b for every output
+//                              channel (fno_skip_quad_kernel: four pixels per thread)
+//   fno_norm_gelu_kernel       then one CTA per plane: two-pass instance statistics,
+//                              normalisation and GELU
 //   fno_project_kernel         per pixel: hidden -> proj_hidden (GELU) -> out_channels, the
 //                              proj_hidden-wide intermediate never leaves registers
 //                              (fno_ns/model.py:162-166); the shapes scx_fno_proj_tc.cu
 //                              supports run its tensor-core version instead
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <cmath>
 
@@ -90,6 +97,9 @@ __global__ void __launch_bounds__(kThreads) fno_lift_kernel(const float* __restr
 // sum keeps its order over i); the output channels are split into groups of kSkipGroup over
 // grid.z, for enough warps per SM.  grid = (ceil(HW / (kThreads * PX)), B, ceil(hidden / kSkipGroup))
 constexpr int kSkipGroup = 8;
+// Input channels per batch of loads in the four-pixel kernels: eight float4 registers, which
+// keeps them at three 256-thread CTAs per SM (one wave for B20 at 64x64)
+constexpr int kSkipBatch = 8;
 
 template <int HMAX, int PX>
 __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ s, const float* __restrict__ h,
@@ -164,11 +174,11 @@ __global__ void __launch_bounds__(kThreads) fno_skip_kernel(float* __restrict__ 
 
 // The same skip GEMM with four consecutive pixels per thread (float4 loads and stores), for
 // planes whose pixel count is a multiple of 4 and hidden a multiple of 16: input channels in
-// blocks of 16, each float4 of weights feeding 16 FMAs.  Each output keeps the order bias + s,
+// batches of kSkipBatch loads, each float4 of weights feeding 16 FMAs.  Each output keeps the order bias + s,
 // then i = 0, 1, ..., so the results equal fno_skip_kernel's bit for bit.
 // grid = (ceil(HW / (4 * kThreads)), B, ceil(hidden / kSkipGroup))
 template <int HMAX>
-__global__ void __launch_bounds__(kThreads) fno_skip_quad_kernel(float* __restrict__ s, const float* __restrict__ h,
+__global__ void __launch_bounds__(kThreads, 3) fno_skip_quad_kernel(float* __restrict__ s, const float* __restrict__ h,
                                                                  float* __restrict__ h_next,
                                                                  const float* __restrict__ w,
                                                                  const float* __restrict__ bias, int HW, int hidden,
@@ -197,15 +207,15 @@ __global__ void __launch_bounds__(kThreads) fno_skip_quad_kernel(float* __restri
         const float4 sv = s4[static_cast<size_t>(o) * HW4];
         z[t] = make_float4(bo + sv.x, bo + sv.y, bo + sv.z, bo + sv.w);
     }
-    for (int i0 = 0; i0 < hidden; i0 += 16) {
-        float4 hv[16];
+    for (int i0 = 0; i0 < hidden; i0 += kSkipBatch) {
+        float4 hv[kSkipBatch];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) hv[i] = __ldg(h4 + static_cast<size_t>(i0 + i) * HW4);
+        for (int i = 0; i < kSkipBatch; ++i) hv[i] = __ldg(h4 + static_cast<size_t>(i0 + i) * HW4);
 #pragma unroll
         for (int t = 0; t < kSkipGroup; ++t) {
             const float4* wr = reinterpret_cast<const float4*>(ws + min(o_begin + t, hidden - 1) * HMAX + i0);
 #pragma unroll
-            for (int i4 = 0; i4 < 4; ++i4) {
+            for (int i4 = 0; i4 < kSkipBatch / 4; ++i4) {
                 const float4 wv = wr[i4];
                 const float wk[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
@@ -335,6 +345,148 @@ __global__ void __launch_bounds__(kThreads) fno_norm_gelu_kernel(const float* __
     const float rstd = 1.0f / sqrtf(block_sum(m2, red) * inv_n + 1e-5f);
     for (int i = threadIdx.x; i < HW; i += kThreads) hp[i] = gelu_erf((__ldg(zp + i) - mean) * rstd);
 }
+
+// Per-channel sums of v[t] over this CTA in a fixed order (warp butterflies, then warp sums
+// in warp order), written to out[t] by thread t.  The caller synchronises before reading out.
+__device__ __forceinline__ void cta_channel_sums(float (&v)[kSkipGroup], float (*red)[kSkipGroup], float* out) {
+#pragma unroll
+    for (int t = 0; t < kSkipGroup; ++t)
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v[t] += __shfl_xor_sync(0xffffffffu, v[t], off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane < kSkipGroup) {
+        float mine = v[0];
+#pragma unroll
+        for (int t = 1; t < kSkipGroup; ++t) mine = lane == t ? v[t] : mine;
+        red[warp][lane] = mine;
+    }
+    __syncthreads();
+    if (threadIdx.x < kSkipGroup) {
+        float tot = 0.f;
+#pragma unroll
+        for (int k = 0; k < kThreads / 32; ++k) tot += red[k][threadIdx.x];
+        out[threadIdx.x] = tot;
+    }
+}
+
+// Fourier-layer epilogue with instance norm in one kernel: the skip GEMM of
+// fno_skip_quad_kernel (same z, bit for bit), then the instance statistics of each (b, o)
+// plane, then h_next = GELU((z - mean) / sqrt(var + eps)) (fno_ns/model.py:96-99,133-134).
+// A thread-block cluster of gridDim.x CTAs (at most 8) covers one plane group: each CTA
+// reduces its pixels per output channel, and the partial sums are read from the cluster's
+// CTAs through distributed shared memory in rank order, so every CTA gets the same mean and
+// variance (two exact passes, biased like torch's InstanceNorm2d).  z stays in registers:
+// no z write, no second read, one launch per layer fewer.
+// grid = (ceil(HW / (4 * kThreads)), B, ceil(hidden / kSkipGroup)), cluster = (gridDim.x, 1, 1)
+template <int HMAX>
+__global__ void __launch_bounds__(kThreads, 3) fno_skip_norm_kernel(const float* __restrict__ s,
+                                                                 const float* __restrict__ h,
+                                                                 float* __restrict__ h_next,
+                                                                 const float* __restrict__ w,
+                                                                 const float* __restrict__ bias, int HW, int hidden) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    scx::tc::grid_dep_launch();
+    __shared__ __align__(16) float ws[HMAX * HMAX];  // [o][i], zero padded
+    __shared__ float red[kThreads / 32][kSkipGroup];
+    __shared__ float part[2][kSkipGroup];  // this CTA's channel sums: z, then (z - mean)^2
+    __shared__ float stat[2][kSkipGroup];  // mean, 1 / sqrt(var + eps)
+    for (int i = threadIdx.x; i < HMAX * HMAX; i += kThreads) {
+        const int o = i / HMAX, k = i - o * HMAX;
+        ws[i] = (o < hidden && k < hidden) ? w[o * hidden + k] : 0.f;
+    }
+    __syncthreads();
+    scx::tc::grid_dep_wait();  // s and h come from earlier kernels in the stream
+    const int HW4 = HW / 4;
+    const int q = blockIdx.x * kThreads + threadIdx.x;  // pixel quad
+    const bool live = q < HW4;  // a thread past the plane computes on quad 0 and contributes nothing
+    const int qq = live ? q : 0;
+    const int b = blockIdx.y;
+    const int o_begin = blockIdx.z * kSkipGroup, o_end = min(hidden, o_begin + kSkipGroup);
+    const size_t plane0 = static_cast<size_t>(b) * hidden * HW;
+    const float4* h4 = reinterpret_cast<const float4*>(h + plane0) + qq;
+    const float4* s4 = reinterpret_cast<const float4*>(s + plane0) + qq;
+    float4 z[kSkipGroup];
+#pragma unroll
+    for (int t = 0; t < kSkipGroup; ++t) {
+        const int o = min(o_begin + t, hidden - 1);
+        const float bo = __ldg(bias + o);
+        const float4 sv = __ldg(s4 + static_cast<size_t>(o) * HW4);
+        z[t] = make_float4(bo + sv.x, bo + sv.y, bo + sv.z, bo + sv.w);
+    }
+    for (int i0 = 0; i0 < hidden; i0 += kSkipBatch) {
+        float4 hv[kSkipBatch];
+#pragma unroll
+        for (int i = 0; i < kSkipBatch; ++i) hv[i] = __ldg(h4 + static_cast<size_t>(i0 + i) * HW4);
+#pragma unroll
+        for (int t = 0; t < kSkipGroup; ++t) {
+            const float4* wr = reinterpret_cast<const float4*>(ws + min(o_begin + t, hidden - 1) * HMAX + i0);
+#pragma unroll
+            for (int i4 = 0; i4 < kSkipBatch / 4; ++i4) {
+                const float4 wv = wr[i4];
+                const float wk[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float4 hk = hv[4 * i4 + k];
+                    z[t].x = fmaf(wk[k], hk.x, z[t].x);
+                    z[t].y = fmaf(wk[k], hk.y, z[t].y);
+                    z[t].z = fmaf(wk[k], hk.z, z[t].z);
+                    z[t].w = fmaf(wk[k], hk.w, z[t].w);
+                }
+            }
+        }
+    }
+    const float inv_n = 1.0f / static_cast<float>(HW);
+    const unsigned ranks = cluster.num_blocks();
+    // pass 1: mean
+    float v[kSkipGroup];
+#pragma unroll
+    for (int t = 0; t < kSkipGroup; ++t) v[t] = live ? (z[t].x + z[t].y) + (z[t].z + z[t].w) : 0.f;
+    cta_channel_sums(v, red, part[0]);
+    cluster.sync();  // every CTA's part[0] is written and visible cluster-wide
+    if (threadIdx.x < kSkipGroup) {
+        float tot = 0.f;
+        for (unsigned r = 0; r < ranks; ++r) tot += cluster.map_shared_rank(&part[0][0], r)[threadIdx.x];
+        stat[0][threadIdx.x] = tot * inv_n;
+    }
+    __syncthreads();
+    // pass 2: biased variance about the mean
+#pragma unroll
+    for (int t = 0; t < kSkipGroup; ++t) {
+        const float mean = stat[0][t];
+        const float dx = z[t].x - mean, dy = z[t].y - mean, dz = z[t].z - mean, dw = z[t].w - mean;
+        float m2 = 0.f;
+        m2 = fmaf(dx, dx, m2);
+        m2 = fmaf(dy, dy, m2);
+        m2 = fmaf(dz, dz, m2);
+        m2 = fmaf(dw, dw, m2);
+        v[t] = live ? m2 : 0.f;
+    }
+    cta_channel_sums(v, red, part[1]);
+    cluster.sync();  // every CTA's part[1] is written and visible cluster-wide
+    if (threadIdx.x < kSkipGroup) {
+        float tot = 0.f;
+        for (unsigned r = 0; r < ranks; ++r) tot += cluster.map_shared_rank(&part[1][0], r)[threadIdx.x];
+        stat[1][threadIdx.x] = 1.0f / sqrtf(tot * inv_n + 1e-5f);
+    }
+    // no CTA leaves (and releases its shared memory) while another may still read its part[];
+    // also publishes stat[1] within the CTA
+    cluster.sync();
+    if (!live) return;
+    float4* out4 = reinterpret_cast<float4*>(h_next + plane0) + q;
+#pragma unroll
+    for (int t = 0; t < kSkipGroup; ++t) {
+        const int o = o_begin + t;
+        if (o >= o_end) break;
+        const float mean = stat[0][t], rstd = stat[1][t];
+        out4[static_cast<size_t>(o) * HW4] =
+            make_float4(gelu_erf((z[t].x - mean) * rstd), gelu_erf((z[t].y - mean) * rstd),
+                        gelu_erf((z[t].z - mean) * rstd), gelu_erf((z[t].w - mean) * rstd));
+    }
+}
+
+// Largest cluster the fused skip+norm kernel is launched with (portable cluster size).
+constexpr int kMaxNormCluster = 8;
 
 // y[b][oc][p] = b2[oc] + sum_j W2[oc][j] GELU(b1[j] + sum_c W1[j][c] h[b][c][p])
 // Each thread takes PX pixels (kThreads apart, so loads and stores stay coalesced): one
@@ -466,9 +618,30 @@ template <int HMAX>
 cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const float* h, float* h_next, const float* w, const float* bias, cudaStream_t s) {
     const int HW = cfg->height * cfg->width;
     cudaError_t e;
-    if (HW % 4 == 0 && cfg->hidden % 16 == 0 &&
-        ((reinterpret_cast<uintptr_t>(spec) | reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(h_next)) &
-         15) == 0) {
+    const bool quads = HW % 4 == 0 && cfg->hidden % 16 == 0 &&
+                       ((reinterpret_cast<uintptr_t>(spec) | reinterpret_cast<uintptr_t>(h) |
+                         reinterpret_cast<uintptr_t>(h_next)) & 15) == 0;
+    const int cluster = (HW / 4 + kThreads - 1) / kThreads;  // CTAs per plane in the quad layout
+    if (quads && cfg->instance_norm && cluster <= kMaxNormCluster) {
+        // skip GEMM, statistics and GELU in one launch: a cluster of CTAs per plane group
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(cluster, cfg->batch_size, (cfg->hidden + kSkipGroup - 1) / kSkipGroup);
+        lc.blockDim = dim3(kThreads);
+        lc.dynamicSmemBytes = 0;
+        lc.stream = s;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = cluster;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 2;
+        return cudaLaunchKernelEx(&lc, fno_skip_norm_kernel<HMAX>, static_cast<const float*>(spec), h, h_next, w,
+                                  bias, HW, cfg->hidden);
+    }
+    if (quads) {
         const dim3 grid((HW / 4 + kThreads - 1) / kThreads, cfg->batch_size, (cfg->hidden + kSkipGroup - 1) / kSkipGroup);
         e = scx::launch_chained(fno_skip_quad_kernel<HMAX>, grid, dim3(kThreads), 0, s, spec, h, h_next, w, bias, HW,
                                 cfg->hidden, cfg->instance_norm);

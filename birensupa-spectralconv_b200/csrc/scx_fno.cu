@@ -31,7 +31,7 @@ namespace {
 
 constexpr int kThreads = 256;
 
-__device__ __forceinline__ float gelu_erf(float z) { return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu_erf(float z) { return scx::tc::gelu_as(z); }
 
 // torch.linspace(0, 1, n)[i] in fp32: start + i*step on the first half, end - (n-1-i)*step on
 // the second half, step = 1/(n-1).

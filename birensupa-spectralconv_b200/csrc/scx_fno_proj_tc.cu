@@ -24,7 +24,7 @@ constexpr int kProjThreads = 256;  // 8 warps: two per TMEM sub-partition
 constexpr int kTile = 128;         // pixels per CTA (MMA M)
 constexpr int kMaxOut = 4;
 
-__device__ __forceinline__ float gelu(float z) { return 0.5f * z * (1.0f + erff(z * 0.70710678118654752f)); }
+__device__ __forceinline__ float gelu(float z) { return tc::gelu_as(z); }
 
 // W [N][K] (row-major, K = channels) -> tf32 hi/lo (fp32 containers), K-major SW128: 4
 // consecutive k of row n per 16-byte unit.
@@ -82,6 +82,32 @@ __device__ __forceinline__ void issue_gemm(uint32_t tmem, const uint8_t* w_hi, c
         }
     }
     tc::mma_commit(done);
+}
+
+// Bias, GELU and the second layer over hidden units [j_begin, j_end) (multiples of 16) of this
+// thread's TMEM lane: out[o] += W2[o][j] GELU(D[j] + b1[j]) in order j = j_begin, ...
+template <int OC>
+__device__ __forceinline__ void finish_units(uint32_t row, int j_begin, int j_end, const float* b1s,
+                                             const float* w2s, int ph, float (&out)[kMaxOut]) {
+    for (int j0 = j_begin; j0 < j_end; j0 += 16) {
+        float v[16];
+        tc::tmem_ld16_nowait(row + static_cast<uint32_t>(j0), v);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+            const float4 bb = *reinterpret_cast<const float4*>(b1s + j0 + 4 * k4);
+            const float g0 = gelu(v[4 * k4 + 0] + bb.x), g1 = gelu(v[4 * k4 + 1] + bb.y);
+            const float g2 = gelu(v[4 * k4 + 2] + bb.z), g3 = gelu(v[4 * k4 + 3] + bb.w);
+#pragma unroll
+            for (int o = 0; o < OC; ++o) {
+                const float4 ww = *reinterpret_cast<const float4*>(w2s + o * ph + j0 + 4 * k4);
+                out[o] = fmaf(ww.x, g0, out[o]);
+                out[o] = fmaf(ww.y, g1, out[o]);
+                out[o] = fmaf(ww.z, g2, out[o]);
+                out[o] = fmaf(ww.w, g3, out[o]);
+            }
+        }
+    }
 }
 
 uint32_t tmem_cols_for(int n) { return n <= 32 ? 32u : (n <= 64 ? 64u : (n <= 128 ? 128u : 256u)); }
@@ -150,17 +176,11 @@ __global__ void __launch_bounds__(kProjThreads) fno_project_tc_kernel(const Proj
     if (ok) {
         const uint32_t row = tmem + (static_cast<uint32_t>(sub * 32) << 16);
         const int jh = ph / 2;
-        for (int j0 = half * jh; j0 < (half + 1) * jh; j0 += 16) {
-            float v[16];
-            tc::tmem_ld16_nowait(row + static_cast<uint32_t>(j0), v);
-            tc::tmem_wait_ld();
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-                const float g = gelu(v[k] + b1s[j0 + k]);
-#pragma unroll
-                for (int o = 0; o < kMaxOut; ++o)
-                    if (o < a.oc) out[o] = fmaf(w2s[o * ph + j0 + k], g, out[o]);
-            }
+        switch (a.oc) {
+            case 1: finish_units<1>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
+            case 2: finish_units<2>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
+            case 3: finish_units<3>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
+            default: finish_units<4>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
         }
         if (half == 1) {
 #pragma unroll

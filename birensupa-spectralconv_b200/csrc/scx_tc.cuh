@@ -424,8 +424,8 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, int c0,
 // Mathematical Functions (1964): erfc(x) = t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) e^(-x^2),
 // t = 1 / (1 + p x), with |error| <= 1.5e-7; with the fast reciprocal and exponential the
 // GELU's absolute error stays below 1e-6 |z|.  Phi(z) = 1 - erfc(|z| / sqrt 2) / 2 for z >= 0
-// and erfc(|z| / sqrt 2) / 2 below.  Library erff branches on |x|, so lanes holding small and
-// large values run both paths; this form runs one path of about 17 instructions.
+// and erfc(|z| / sqrt 2) / 2 below.  No data-dependent branch: every lane runs the same
+// 17 or so instructions.
 __device__ __forceinline__ float gelu_as(float z) {
     const float x = fabsf(z) * 0.70710678118654752f;
     const float t = __fdividef(1.0f, fmaf(0.3275911f, x, 1.0f));

@@ -224,6 +224,49 @@ def spectral_conv2d_fwd(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, mod
     return out
 
 
+def spectral_conv2d_fwd_host(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, modes1: int, modes2: int,
+                             device: torch.device, out: torch.Tensor | None = None, chunks: int = 0) -> torch.Tensor:
+    """Fused SpectralConv2d forward from a host tensor to a host tensor through
+    scx_spectral_conv2d_fwd_host: the batch is streamed through the device in chunks whose
+    uploads, forwards and downloads overlap.  x [B,Cin,H,W] contiguous float32 on the CPU
+    (page-locked for the overlap); w1/w2 as for spectral_conv2d_fwd, on ``device``.  Returns
+    a page-locked [B,Cout,H,W] host tensor (or fills ``out``) once the result is there."""
+    _check(x.dim() == 4, "x must be [B,C,H,W]")
+    _check(not x.is_cuda and x.dtype == torch.float32 and x.is_contiguous(),
+           "x must be a contiguous float32 host tensor")
+    if w1.is_complex():
+        w1 = torch.view_as_real(w1.resolve_conj().contiguous())
+    if w2.is_complex():
+        w2 = torch.view_as_real(w2.resolve_conj().contiguous())
+    _check_freq_tensor(w1, "weights1")
+    _check_freq_tensor(w2, "weights2")
+    _check(w1.shape == w2.shape, "weights1/weights2 shape mismatch")
+    _check(w1.device == device and w2.device == device, "weights must be on the device")
+    B, Cin, H, W = (int(s) for s in x.shape)
+    _check(w1.size(0) == Cin, "weights C_in mismatch")
+    _check(w1.size(2) == modes1 and w1.size(3) == modes2, "weights modes mismatch")
+    Cout = int(w1.size(1))
+    _check(1 <= modes1 <= H and 1 <= modes2 <= W // 2 + 1, "modes out of range for the grid")
+    if out is None:
+        out = torch.empty(B, Cout, H, W, dtype=torch.float32, pin_memory=True)
+    else:
+        _check(out.shape == (B, Cout, H, W) and out.is_contiguous() and out.dtype == torch.float32
+               and not out.is_cuda, "out must be a contiguous float32 [B,Cout,H,W] host tensor")
+    lib = _scx.lib
+    need = lib.scx_spectral_conv2d_workspace_size(B, Cin, Cout, H, W, int(modes1), int(modes2))
+    _check(need > 0, "invalid SpectralConv2d sizes")
+    ws = workspace(need, device)
+    x_dev = torch.empty(B, Cin, H, W, dtype=torch.float32, device=device)
+    y_dev = torch.empty(B, Cout, H, W, dtype=torch.float32, device=device)
+    with _scx.device_guard(device):
+        _scx.check(lib.scx_spectral_conv2d_fwd_host(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), out.data_ptr(), B,
+                                                    Cin, Cout, H, W, int(modes1), int(modes2), x_dev.data_ptr(),
+                                                    y_dev.data_ptr(), ws.data_ptr(), ws.numel(), int(chunks),
+                                                    _scx.stream_of(device)),
+                   "spectral_conv2d_fwd_host")
+    return out
+
+
 def prepare(height: int, width: int, modes1: int, modes2: int) -> None:
     """Builds the twiddle tables of one shape on the current device (outside capture)."""
     _scx.check(_scx.lib.scx_prepare(int(height), int(width), int(modes1), int(modes2)), "prepare")

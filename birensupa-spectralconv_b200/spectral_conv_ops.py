@@ -180,58 +180,18 @@ def _to_device_input(x: torch.Tensor, device: torch.device) -> torch.Tensor:
     return x.detach().to(device=device, dtype=torch.float32).contiguous()
 
 
-_COPY_STREAMS: dict = {}
-_HOST_CHUNKS = 5  # batch chunks of a host-in / host-out call
-
-
-def _copy_streams(device: torch.device) -> tuple:
-    key = device.index
-    if key not in _COPY_STREAMS:
-        _COPY_STREAMS[key] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
-    return _COPY_STREAMS[key]
-
-
-def _host_forward_pipelined(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, modes1: int, modes2: int,
-                            device: torch.device) -> torch.Tensor:
-    """Host input -> host result with the batch split into chunks: the upload of chunk i + 1,
-    the forward of chunk i (on the caller's stream) and the download of chunk i - 1 overlap,
-    so both PCIe directions are busy at once.  Batch items are independent, and every chunk
-    goes through the same three kernels, so each sample's result is what one call gives."""
-    B = int(x.shape[0])
-    n = min(B, _HOST_CHUNKS)
-    bounds = [(B * i // n, B * (i + 1) // n) for i in range(n)]
-    up, down = _copy_streams(device)
-    compute = torch.cuda.current_stream(device)
-    x_dev = torch.empty(x.shape, dtype=torch.float32, device=device)
-    Cout = int(w1.shape[1])
-    y_dev = torch.empty((B, Cout) + tuple(x.shape[2:]), dtype=torch.float32, device=device)
-    host = torch.empty(y_dev.shape, dtype=torch.float32, pin_memory=True)
-    up.wait_stream(compute)  # x_dev and y_dev are free once earlier work on the caller's stream is
-    down.wait_stream(compute)
-    for lo, hi in bounds:
-        with torch.cuda.stream(up):
-            x_dev[lo:hi].copy_(x[lo:hi], non_blocking=True)
-        compute.wait_stream(up)
-        spectral_conv_ext.spectral_conv2d_fwd(x_dev[lo:hi], w1, w2, modes1, modes2, out=y_dev[lo:hi])
-        down.wait_stream(compute)
-        with torch.cuda.stream(down):
-            host[lo:hi].copy_(y_dev[lo:hi], non_blocking=True)
-    down.synchronize()
-    return host
-
-
 def spectral_conv2d_fused(x: torch.Tensor, weights1: torch.Tensor, weights2: torch.Tensor, modes1: int,
                           modes2: int, *, to_cpu: bool = True, synchronize: bool | None = None) -> torch.Tensor:
     """Device-resident forward (spectral_conv/spectral_conv_ops.py:363-417): one truncated
     DFT kernel, one dual-corner mixing kernel, one inverse DFT kernel.  ``to_cpu=False``
     keeps the output on the device.  A page-locked float32 host input with a host result is
-    streamed through in batch chunks (``_host_forward_pipelined``)."""
+    streamed through in batch chunks by one native call (scx_spectral_conv2d_fwd_host)."""
     device = _device_for(x)
     w1 = _weights_to_device_cached(weights1, device)
     w2 = _weights_to_device_cached(weights2, device)
     if (to_cpu and not x.is_cuda and x.dim() == 4 and x.dtype == torch.float32 and x.is_contiguous()
             and x.is_pinned() and x.shape[0] > 1):
-        return _host_forward_pipelined(x, w1, w2, int(modes1), int(modes2), device)
+        return spectral_conv_ext.spectral_conv2d_fwd_host(x, w1, w2, int(modes1), int(modes2), device)
     x_dev = _to_device_input(x, device)
     y = spectral_conv_ext.spectral_conv2d_fwd(x_dev, w1, w2, int(modes1), int(modes2))
     if to_cpu:

@@ -109,6 +109,24 @@ int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* 
                             int height, int width, int modes1, int modes2, void* workspace,
                             size_t workspace_bytes, scx_stream_t stream);
 
+/* The same forward from host memory to host memory: the host-facing call of
+ * spectral_conv2d_supa with a CPU tensor (spectral_conv/spectral_conv_ops.py:480-505, which
+ * copies the batch up, runs the forward and copies it down in turn).  x_host
+ * [B][Cin][H][W] and y_host [B][Cout][H][W] are host memory, page-locked for the copies to
+ * overlap (cudaHostAlloc / cudaHostRegister; pageable memory gives the same result, slower);
+ * weights1/weights2 as for scx_spectral_conv2d_fwd.  x_dev and y_dev are caller-owned device
+ * buffers of B*Cin*H*W and B*Cout*H*W floats, workspace as for scx_spectral_conv2d_fwd with
+ * the whole batch.  The batch is split into `chunks` pieces (0: the library's default, 6;
+ * the first and last half-size): the upload of piece i+1, the forward of piece i on `stream`
+ * and the download of piece i-1 overlap on two library-owned copy streams.  Returns when
+ * y_host holds the result (not graph-capturable); later work on `stream` is ordered after
+ * it.  Calls on one device are serialised. */
+int scx_spectral_conv2d_fwd_host(const float* x_host, const float* weights1, const float* weights2,
+                                 float* y_host, int batch_size, int channels_in, int channels_out,
+                                 int height, int width, int modes1, int modes2, float* x_dev,
+                                 float* y_dev, void* workspace, size_t workspace_bytes, int chunks,
+                                 scx_stream_t stream);
+
 /* ---------------------------------------------------------------------------------
  * FNO-2d forward (fno_ns/model.py:137-259): lift -> n_layers x Fourier layer ->
  * projection, one call.  Replaces FNO2d.forward_supa_chain (fno_ns/model.py:219-259) with

@@ -90,10 +90,10 @@ def test_linearity_full_size(cuda_device):
     assert_close((a * y1 + b * y2).cpu().numpy(), y12.cpu().numpy(), 3e-5)
 
 
-@pytest.mark.parametrize("batch", [20, 7])  # five chunks; ragged chunks (1, 1, 2, 1, 2)
+@pytest.mark.parametrize("batch", [20, 7])  # six chunks (2, 4, 4, 4, 4, 2); ragged (1, 1, 2, 1, 1, 1)
 def test_pinned_host_call_matches_device_call(batch, cuda_device):
-    """A page-locked host input with a host result runs in pipelined batch chunks; every
-    sample equals the device-resident call's result."""
+    """A page-locked host input with a host result runs in pipelined batch chunks
+    (scx_spectral_conv2d_fwd_host); every sample equals the device-resident call's result."""
     import spectral_conv_ops
 
     x, w1, w2, c = scx_data.make_spectral_case("spectral_b20_c32_64x64_m12", batch=batch)
@@ -107,6 +107,47 @@ def test_pinned_host_call_matches_device_call(batch, cuda_device):
     # warp groups for B = 20, two for chunks of 4), which reorders its 32-term fp32 sums: about
     # 3e-6 of max|y| measured
     assert_close(y_dev.cpu().numpy(), y_host.numpy(), 1e-5)
+
+
+@pytest.mark.parametrize("batch,chunks,pinned", [
+    (20, 0, True), (20, 1, True), (20, 3, False), (5, 32, True), (1, 0, True), (13, 7, False)])
+def test_host_entry_chunking(batch, chunks, pinned, cuda_device):
+    """scx_spectral_conv2d_fwd_host for any chunk count (clamped to the batch), page-locked or
+    pageable host memory: the result matches the device call sample by sample, and a second
+    call into the same output gives the same bits."""
+    import spectral_conv_ext
+
+    x, w1, w2, c = scx_data.make_spectral_case("spectral_b20_c32_64x64_m12", batch=batch)
+    w1d = torch.view_as_real(w1.to(cuda_device))
+    w2d = torch.view_as_real(w2.to(cuda_device))
+    y_dev = spectral_conv_ext.spectral_conv2d_fwd(x.to(cuda_device), w1d, w2d, c["m1"], c["m2"])
+    xh = x.pin_memory() if pinned else x.contiguous()
+    y_host = spectral_conv_ext.spectral_conv2d_fwd_host(xh, w1d, w2d, c["m1"], c["m2"], cuda_device,
+                                                        chunks=chunks)
+    assert y_host.device.type == "cpu" and y_host.shape == y_dev.shape
+    # chunks may take another mixing tile shape than the whole batch (see above)
+    assert_close(y_dev.cpu().numpy(), y_host.numpy(), 1e-5)
+    again = torch.full_like(y_host, float("nan"))
+    spectral_conv_ext.spectral_conv2d_fwd_host(xh, w1d, w2d, c["m1"], c["m2"], cuda_device, out=again,
+                                               chunks=chunks)
+    assert torch.equal(again, y_host)
+
+
+def test_host_entry_rejects_bad_arguments(cuda_device):
+    import _scx
+
+    x, w1, w2, c = scx_data.make_spectral_case("spectral_b20_c32_64x64_m12", batch=2)
+    lib = _scx.lib
+    buf = torch.empty(1 << 20, dtype=torch.uint8, device=cuda_device)
+    p = buf.data_ptr()
+    with _scx.device_guard(cuda_device):
+        # null host pointer, negative chunk count, too small a workspace
+        assert lib.scx_spectral_conv2d_fwd_host(0, p, p, x.data_ptr(), 2, 32, 32, 64, 64, 12, 12, p, p, p, 1 << 20,
+                                                0, None) != 0
+        assert lib.scx_spectral_conv2d_fwd_host(x.data_ptr(), p, p, x.data_ptr(), 2, 32, 32, 64, 64, 12, 12, p, p,
+                                                p, 1 << 20, -1, None) != 0
+        assert lib.scx_spectral_conv2d_fwd_host(x.data_ptr(), p, p, x.data_ptr(), 2, 32, 32, 64, 64, 12, 12, p, p,
+                                                p, 16, 0, None) != 0
 
 
 def test_deterministic_and_fully_written(cuda_device):

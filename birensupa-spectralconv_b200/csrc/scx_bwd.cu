@@ -1,0 +1,187 @@
+// SpectralConv2d backward: the gradients torch's autograd gives for the reference forward
+// (spectral_conv/reference_pytorch.py:30-47: rfft2, two corner einsums, zero-padded irfft2),
+// from the forward's corner spectra.  The reference itself differentiates only the mixing
+// (SpectralMulFunction, spectral_conv/spectral_conv_ops.py:260-286); this extends it to the
+// whole layer on the device.
+//
+// With y = sum over retained (kx, ky) of (c_ky / HW) Re(Y e^{+i theta}) (c_ky = 1 for ky = 0
+// and, W even, ky = W/2, else 2; the inverse kernels' row weights), Y_c = mix(X_c, W_c) per
+// mode and X = sum x e^{-i theta}, torch's conventions (gradient = dL/dRe + i dL/dIm) give
+//   G       = fwd(grad_y)                          (the forward DFT kernel, unscaled)
+//   grad_Y  = (c_ky / HW) G
+//   grad_X  = grad_Y W^H per mode,   grad_W = X^H grad_Y per mode
+//   grad_x  = sum Re(grad_X e^{+i theta}) = inv(G W^H)
+// The last line holds because c_ky / HW depends only on the mode, so it commutes with the
+// channel mixing and cancels the inverse kernel's own row weights.  Corner-1 rows that corner
+// 2 overwrites in the forward (2 m1 > H) do not reach y, so their G rows are zeroed first;
+// the inverse drops those rows of grad_X, which are then zero anyway.
+//
+// Kernels: the forward DFT, two dual-corner mixings and the inverse DFT of the forward path,
+// plus three small elementwise passes (conjugate transposes of W and X per mode, the per-ky
+// scale of grad_W, the overlap-row mask).
+#include <algorithm>
+
+#include "scx.h"
+#include "scx_internal.h"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+inline size_t a256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+// out_c[d1][d0][m] = conj(in_c[d0][d1][m]) for both corners c = blockIdx.y (complex, NM modes
+// contiguous); threads walk the output in order.
+__global__ void __launch_bounds__(kThreads) conj_transpose_kernel(const float2* __restrict__ in1,
+                                                                  const float2* __restrict__ in2,
+                                                                  float2* __restrict__ out1, float2* __restrict__ out2,
+                                                                  int D0, int D1, int NM) {
+    const float2* in = blockIdx.y == 0 ? in1 : in2;
+    float2* out = blockIdx.y == 0 ? out1 : out2;
+    const long long total = static_cast<long long>(D0) * D1 * NM;
+    for (long long t = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * kThreads) {
+        const int m = static_cast<int>(t % NM);
+        const long long r = t / NM;
+        const int d0 = static_cast<int>(r % D0), d1 = static_cast<int>(r / D0);
+        const float2 v = __ldg(in + (static_cast<long long>(d0) * D1 + d1) * NM + m);
+        out[t] = make_float2(v.x, -v.y);
+    }
+}
+
+// a_c[r][ky] *= c_ky / (H W) over rows r < rows (rows = Cin * Cout * m1) of both corners.
+__global__ void __launch_bounds__(kThreads) scale_ky_kernel(float2* __restrict__ a1, float2* __restrict__ a2,
+                                                            long long rows, int m2, int W, float inv_hw) {
+    float2* a = blockIdx.y == 0 ? a1 : a2;
+    const long long total = rows * m2;
+    for (long long t = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * kThreads) {
+        const int ky = static_cast<int>(t % m2);
+        const bool single = ky == 0 || ((W % 2 == 0) && ky == W / 2);
+        const float f = single ? inv_hw : 2.0f * inv_hw;
+        const float2 v = a[t];
+        a[t] = make_float2(v.x * f, v.y * f);
+    }
+}
+
+// g1[p][s][ky] = 0 for corner-1 slots s in [r0, m1) (spectrum rows that corner 2 overwrites).
+__global__ void __launch_bounds__(kThreads) zero_rows_kernel(float2* __restrict__ g1, long long planes, int m1,
+                                                             int m2, int r0) {
+    const int nrow = m1 - r0;
+    const long long total = planes * nrow * m2;
+    for (long long t = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * kThreads) {
+        const int ky = static_cast<int>(t % m2);
+        const long long r = t / m2;
+        const int s = r0 + static_cast<int>(r % nrow);
+        const long long p = r / nrow;
+        g1[(p * m1 + s) * m2 + ky] = make_float2(0.f, 0.f);
+    }
+}
+
+unsigned blocks_for(long long n) {
+    return static_cast<unsigned>(std::min<long long>((n + kThreads - 1) / kThreads, 148LL * 16));
+}
+
+struct BwdLayout {
+    size_t g, z, wh, xh, scratch, total;
+};
+
+BwdLayout bwd_layout(int B, int Cin, int Cout, int H, int W, int m1, int m2) {
+    const size_t NM = static_cast<size_t>(m1) * m2;
+    BwdLayout L;
+    L.g = a256(static_cast<size_t>(B) * Cout * NM * sizeof(float2));    // G per corner
+    L.z = a256(static_cast<size_t>(B) * Cin * NM * sizeof(float2));     // G W^H per corner
+    L.wh = a256(static_cast<size_t>(Cout) * Cin * NM * sizeof(float2)); // W^H per corner
+    L.xh = a256(static_cast<size_t>(Cin) * B * NM * sizeof(float2));    // X^H per corner
+    L.scratch = scx::tc_split_supported(H, W, m1, m2)
+                    ? a256(scx::split_scratch_bytes(static_cast<long long>(B) * std::max(Cin, Cout), H, W))
+                    : 0;
+    L.total = 2 * (L.g + L.z + L.wh + L.xh) + L.scratch;
+    return L;
+}
+
+}  // namespace
+
+extern "C" size_t scx_spectral_conv2d_bwd_workspace_size(int batch_size, int channels_in, int channels_out,
+                                                         int height, int width, int modes1, int modes2) {
+    // the forward's shape rules
+    if (scx_spectral_conv2d_workspace_size(batch_size, channels_in, channels_out, height, width, modes1, modes2) == 0)
+        return 0;
+    return bwd_layout(batch_size, channels_in, channels_out, height, width, modes1, modes2).total;
+}
+
+extern "C" int scx_spectral_conv2d_bwd(const float* grad_y, const float* x_corners, const float* weights1,
+                                       const float* weights2, float* grad_x, float* grad_w1, float* grad_w2,
+                                       int batch_size, int channels_in, int channels_out, int height, int width,
+                                       int modes1, int modes2, void* workspace, size_t workspace_bytes,
+                                       scx_stream_t stream) {
+    if (!grad_y || !weights1 || !weights2 || !workspace) return cudaErrorInvalidValue;
+    if ((grad_w1 == nullptr) != (grad_w2 == nullptr)) return cudaErrorInvalidValue;
+    if (grad_w1 && !x_corners) return cudaErrorInvalidValue;
+    const size_t need = scx_spectral_conv2d_bwd_workspace_size(batch_size, channels_in, channels_out, height, width,
+                                                               modes1, modes2);
+    if (need == 0 || workspace_bytes < need) return cudaErrorInvalidValue;
+    auto misaligned = [](const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) != 0; };
+    if (misaligned(grad_y, 4) || misaligned(weights1, 8) || misaligned(weights2, 8) || misaligned(workspace, 256) ||
+        (grad_x && misaligned(grad_x, 4)) || (x_corners && misaligned(x_corners, 8)) ||
+        (grad_w1 && (misaligned(grad_w1, 8) || misaligned(grad_w2, 8))))
+        return cudaErrorInvalidValue;
+    const int B = batch_size, Cin = channels_in, Cout = channels_out, H = height, W = width, m1 = modes1,
+              m2 = modes2;
+    const int NM = m1 * m2;
+    const scx::Twiddles* tw = nullptr;
+    cudaError_t e = scx::get_twiddles(H, W, m1, m2, &tw);
+    if (e != cudaSuccess) return e;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const BwdLayout L = bwd_layout(B, Cin, Cout, H, W, m1, m2);
+    unsigned char* base = static_cast<unsigned char*>(workspace);
+    float2* G1 = reinterpret_cast<float2*>(base);
+    float2* G2 = reinterpret_cast<float2*>(base + L.g);
+    float2* Z1 = reinterpret_cast<float2*>(base + 2 * L.g);
+    float2* Z2 = reinterpret_cast<float2*>(base + 2 * L.g + L.z);
+    float2* WH1 = reinterpret_cast<float2*>(base + 2 * (L.g + L.z));
+    float2* WH2 = reinterpret_cast<float2*>(base + 2 * (L.g + L.z) + L.wh);
+    float2* XH1 = reinterpret_cast<float2*>(base + 2 * (L.g + L.z + L.wh));
+    float2* XH2 = reinterpret_cast<float2*>(base + 2 * (L.g + L.z + L.wh) + L.xh);
+    float* scratch = L.scratch ? reinterpret_cast<float*>(base + 2 * (L.g + L.z + L.wh + L.xh)) : nullptr;
+
+    // G = fwd(grad_y), both corners, [B][Cout][m1][m2]
+    e = scx::dft_fwd(grad_y, G1, G2, NM, m2, B * Cout, H, W, m1, m2, *tw, s, scratch, L.scratch);
+    if (e != cudaSuccess) return e;
+    if (2 * m1 > H) {
+        const long long n = static_cast<long long>(B) * Cout * (2 * m1 - H) * m2;
+        zero_rows_kernel<<<blocks_for(n), kThreads, 0, s>>>(G1, static_cast<long long>(B) * Cout, m1, m2, H - m1);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
+    if (grad_x) {
+        // grad_x = inv(G W^H): W^H [Cout][Cin] per mode
+        const long long n = static_cast<long long>(Cin) * Cout * NM;
+        conj_transpose_kernel<<<dim3(blocks_for(n), 2), kThreads, 0, s>>>(
+            reinterpret_cast<const float2*>(weights1), reinterpret_cast<const float2*>(weights2), WH1, WH2, Cin,
+            Cout, NM);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = scx::launch_mix(G1, G2, WH1, WH2, Z1, Z2, 2, B, Cout, Cin, NM, s);
+        if (e == cudaSuccess) e = scx::dft_inv(Z1, Z2, NM, m2, grad_x, B * Cin, H, W, m1, m2, *tw, s, scratch, L.scratch);
+        if (e != cudaSuccess) return e;
+    }
+    if (grad_w1) {
+        // grad_W = (c_ky / HW) X^H G: X^H [Cin][B] per mode
+        const float2* X1 = reinterpret_cast<const float2*>(x_corners);
+        const float2* X2 = X1 + static_cast<size_t>(B) * Cin * NM;
+        const long long n = static_cast<long long>(B) * Cin * NM;
+        conj_transpose_kernel<<<dim3(blocks_for(n), 2), kThreads, 0, s>>>(X1, X2, XH1, XH2, B, Cin, NM);
+        e = cudaGetLastError();
+        if (e == cudaSuccess)
+            e = scx::launch_mix(XH1, XH2, G1, G2, reinterpret_cast<float2*>(grad_w1), reinterpret_cast<float2*>(grad_w2),
+                                2, Cin, B, Cout, NM, s);
+        if (e != cudaSuccess) return e;
+        const long long rows = static_cast<long long>(Cin) * Cout * m1;
+        scale_ky_kernel<<<dim3(blocks_for(rows * m2), 2), kThreads, 0, s>>>(
+            reinterpret_cast<float2*>(grad_w1), reinterpret_cast<float2*>(grad_w2), rows, m2, W,
+            static_cast<float>(1.0 / (static_cast<double>(H) * W)));
+        e = cudaGetLastError();
+    }
+    return e;
+}

@@ -267,6 +267,74 @@ def spectral_conv2d_fwd_host(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor
     return out
 
 
+def spectral_conv2d_fwd_saved(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, modes1: int,
+                              modes2: int) -> tuple:
+    """spectral_conv2d_fwd that also keeps the input corner spectra for the backward:
+    returns (y, x_corners), x_corners [2,B,Cin,m1,m2,2] float32 (corner 1, corner 2) - the
+    head of a workspace of its own, where the forward leaves them."""
+    _check(x.dim() == 4 and x.is_cuda and x.dtype == torch.float32 and x.is_contiguous(),
+           "x must be contiguous float32 CUDA [B,C,H,W]")
+    w1 = torch.view_as_real(w1.resolve_conj().contiguous()) if w1.is_complex() else w1
+    w2 = torch.view_as_real(w2.resolve_conj().contiguous()) if w2.is_complex() else w2
+    _check_freq_tensor(w1, "weights1")
+    _check_freq_tensor(w2, "weights2")
+    _check(w1.shape == w2.shape and w1.device == x.device and w2.device == x.device,
+           "weights must match and be on x.device")
+    B, Cin, H, W = (int(s) for s in x.shape)
+    _check(w1.size(0) == Cin and w1.size(2) == modes1 and w1.size(3) == modes2, "weights shape mismatch")
+    _check(1 <= modes1 <= H and 1 <= modes2 <= W // 2 + 1, "modes out of range for the grid")
+    Cout = int(w1.size(1))
+    lib = _scx.lib
+    need = lib.scx_spectral_conv2d_workspace_size(B, Cin, Cout, H, W, int(modes1), int(modes2))
+    _check(need > 0, "invalid SpectralConv2d sizes")
+    ws = torch.empty(need, dtype=torch.uint8, device=x.device)
+    y = torch.empty(B, Cout, H, W, device=x.device, dtype=torch.float32)
+    with _scx.device_guard(x.device):
+        _scx.check(lib.scx_spectral_conv2d_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), y.data_ptr(), B, Cin,
+                                               Cout, H, W, int(modes1), int(modes2), ws.data_ptr(), ws.numel(),
+                                               _scx.stream_of(x.device)),
+                   "spectral_conv2d_fwd")
+    n = 2 * B * Cin * modes1 * modes2 * 2
+    x_corners = ws[: n * 4].view(torch.float32).view(2, B, Cin, modes1, modes2, 2)
+    return y, x_corners
+
+
+def spectral_conv2d_bwd(grad_y: torch.Tensor, x_corners: torch.Tensor | None, w1: torch.Tensor, w2: torch.Tensor,
+                        modes1: int, modes2: int, need_x: bool = True, need_w: bool = True) -> tuple:
+    """SpectralConv2d backward through scx_spectral_conv2d_bwd: (grad_x or None, grad_w1 or
+    None, grad_w2 or None), weight gradients as interleaved [Cin,Cout,m1,m2,2] float32.
+    x_corners is the second result of spectral_conv2d_fwd_saved (needed for weight grads)."""
+    _check(grad_y.dim() == 4 and grad_y.is_cuda and grad_y.dtype == torch.float32,
+           "grad_y must be float32 CUDA [B,Cout,H,W]")
+    grad_y = grad_y.contiguous()
+    w1 = torch.view_as_real(w1.resolve_conj().contiguous()) if w1.is_complex() else w1.contiguous()
+    w2 = torch.view_as_real(w2.resolve_conj().contiguous()) if w2.is_complex() else w2.contiguous()
+    _check_freq_tensor(w1, "weights1")
+    _check(w1.shape == w2.shape, "weights1/weights2 shape mismatch")
+    B, Cout, H, W = (int(s) for s in grad_y.shape)
+    Cin = int(w1.size(0))
+    _check(int(w1.size(1)) == Cout and w1.size(2) == modes1 and w1.size(3) == modes2, "weights shape mismatch")
+    dev = grad_y.device
+    grad_x = torch.empty(B, Cin, H, W, device=dev, dtype=torch.float32) if need_x else None
+    gw1 = torch.empty_like(w1) if need_w else None
+    gw2 = torch.empty_like(w2) if need_w else None
+    if need_w:
+        _check(x_corners is not None and x_corners.is_contiguous()
+               and tuple(x_corners.shape) == (2, B, Cin, modes1, modes2, 2), "x_corners shape mismatch")
+    lib = _scx.lib
+    need = lib.scx_spectral_conv2d_bwd_workspace_size(B, Cin, Cout, H, W, int(modes1), int(modes2))
+    _check(need > 0, "invalid SpectralConv2d sizes")
+    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+    with _scx.device_guard(dev):
+        _scx.check(lib.scx_spectral_conv2d_bwd(grad_y.data_ptr(), ptr(x_corners) if need_w else None,
+                                               w1.data_ptr(), w2.data_ptr(), ptr(grad_x), ptr(gw1), ptr(gw2), B, Cin,
+                                               Cout, H, W, int(modes1), int(modes2), ws.data_ptr(), ws.numel(),
+                                               _scx.stream_of(dev)),
+                   "spectral_conv2d_bwd")
+    return grad_x, gw1, gw2
+
+
 def prepare(height: int, width: int, modes1: int, modes2: int) -> None:
     """Builds the twiddle tables of one shape on the current device (outside capture)."""
     _scx.check(_scx.lib.scx_prepare(int(height), int(width), int(modes1), int(modes2)), "prepare")

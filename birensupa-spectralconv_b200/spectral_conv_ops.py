@@ -265,6 +265,51 @@ class SpectralConv2dSupa(nn.Module):
                                     use_sufft=use_sufft, to_cpu=to_cpu)
 
 
+class SpectralConv2dFunction(torch.autograd.Function):
+    """Differentiable SpectralConv2d on the device: the fused forward keeps the input corner
+    spectra, and the backward (scx_spectral_conv2d_bwd) returns the gradients torch autograd
+    gives for spectral_conv/reference_pytorch.py:30-47.  The reference differentiates only
+    the mixing (SpectralMulFunction, spectral_conv/spectral_conv_ops.py:260-286)."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, weights1: torch.Tensor, weights2: torch.Tensor, modes1: int,
+                modes2: int) -> torch.Tensor:
+        device = x.device
+        w1 = _weights_to_device_cached(weights1, device)
+        w2 = _weights_to_device_cached(weights2, device)
+        y, x_corners = spectral_conv_ext.spectral_conv2d_fwd_saved(
+            x.detach().to(torch.float32).contiguous(), w1, w2, int(modes1), int(modes2))
+        ctx.x_corners = x_corners
+        ctx.w = (w1, w2)
+        ctx.modes = (int(modes1), int(modes2))
+        ctx.x_dtype = x.dtype
+        ctx.w_complex = (weights1.is_complex(), weights2.is_complex())
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_y: torch.Tensor):
+        need_x, need_w1, need_w2 = ctx.needs_input_grad[:3]
+        gx, gw1, gw2 = spectral_conv_ext.spectral_conv2d_bwd(
+            grad_y.to(torch.float32), ctx.x_corners, ctx.w[0], ctx.w[1], *ctx.modes, need_x=need_x,
+            need_w=need_w1 or need_w2)
+        if gx is not None:
+            gx = gx.to(ctx.x_dtype)
+        if gw1 is not None:
+            gw1 = torch.view_as_complex(gw1) if ctx.w_complex[0] else gw1
+            gw2 = torch.view_as_complex(gw2) if ctx.w_complex[1] else gw2
+        ctx.x_corners = None
+        return gx, (gw1 if need_w1 else None), (gw2 if need_w2 else None), None, None
+
+
+def spectral_conv2d_autograd(x: torch.Tensor, weights1: torch.Tensor, weights2: torch.Tensor, modes1: int,
+                             modes2: int) -> torch.Tensor:
+    """Device-resident SpectralConv2d forward that autograd can differentiate (x a CUDA
+    tensor; weights complex64 [Cin,Cout,m1,m2] or interleaved float32 on its device)."""
+    if not x.is_cuda:
+        raise RuntimeError("spectral_conv2d_autograd needs a CUDA input")
+    return SpectralConv2dFunction.apply(x, weights1, weights2, modes1, modes2)
+
+
 class SpectralConv2d(nn.Module):
     """State-dict compatible with spectral_conv/reference_pytorch.py:12-25; forward runs on
     the module's device (move it with ``.cuda()``) and returns a device tensor."""
@@ -282,4 +327,7 @@ class SpectralConv2d(nn.Module):
                                                         dtype=torch.cfloat))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if torch.is_grad_enabled() and x.is_cuda and (x.requires_grad or self.weights1.requires_grad
+                                                       or self.weights2.requires_grad):
+            return spectral_conv2d_autograd(x, self.weights1, self.weights2, self.modes1, self.modes2)
         return spectral_conv2d(x, self.weights1, self.weights2, self.modes1, self.modes2)

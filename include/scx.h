@@ -109,6 +109,28 @@ int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* 
                             int height, int width, int modes1, int modes2, void* workspace,
                             size_t workspace_bytes, scx_stream_t stream);
 
+/* On return from scx_spectral_conv2d_fwd the workspace starts with the input corner
+ * spectra X1 then X2 ([B][Cin][m1][m2] complex, interleaved float pairs, each); the backward
+ * below takes them as the forward's saved state. */
+
+/* Bytes of device workspace scx_spectral_conv2d_bwd needs; 0 on invalid sizes. */
+size_t scx_spectral_conv2d_bwd_workspace_size(int batch_size, int channels_in, int channels_out,
+                                              int height, int width, int modes1, int modes2);
+
+/* SpectralConv2d backward: the gradients torch autograd gives for the forward of
+ * spectral_conv/reference_pytorch.py:30-47 (the reference differentiates only the mixing,
+ * SpectralMulFunction in spectral_conv/spectral_conv_ops.py:260-286).  grad_y
+ * [B][Cout][H][W]; x_corners: X1 then X2 as the forward left them at the head of its
+ * workspace (needed only for the weight gradients); weights as for the forward.  Outputs:
+ * grad_x [B][Cin][H][W] (NULL to skip), grad_w1 and grad_w2 [Cin][Cout][m1][m2] complex
+ * (both NULL to skip; x_corners may then be NULL).  workspace: device memory of
+ * scx_spectral_conv2d_bwd_workspace_size() bytes, 256-byte aligned. */
+int scx_spectral_conv2d_bwd(const float* grad_y, const float* x_corners, const float* weights1,
+                            const float* weights2, float* grad_x, float* grad_w1, float* grad_w2,
+                            int batch_size, int channels_in, int channels_out, int height, int width,
+                            int modes1, int modes2, void* workspace, size_t workspace_bytes,
+                            scx_stream_t stream);
+
 /* The same forward from host memory to host memory: the host-facing call of
  * spectral_conv2d_supa with a CPU tensor (spectral_conv/spectral_conv_ops.py:480-505, which
  * copies the batch up, runs the forward and copies it down in turn).  x_host

@@ -12,7 +12,8 @@ Three independent restatements of ``spectral_conv/reference_pytorch.py:30-47``:
   fp32 (the path the reference times as its CPU baseline).
 
 and of the FNO forward ``fno_ns/model.py:183-198`` (``FNO2d.forward(use_supa=False)``):
-``fno2d_torch``.  All are pinned against fixtures produced by the reference itself
+``fno2d_torch``.  ``spectral_conv2d_grads_torch`` differentiates the torch recipe (float64
+autograd) for the SpectralConv2d backward.  All are pinned against fixtures produced by the reference itself
 (``tests/golden/make_golden.py``).
 """
 
@@ -123,6 +124,24 @@ def spectral_conv2d_torch(x, w1, w2, modes1: int, modes2: int):
     out_ft[:, :, :modes1, :modes2] = torch.einsum("bixy,ioxy->boxy", x_ft[:, :, :modes1, :modes2], w1)
     out_ft[:, :, -modes1:, :modes2] = torch.einsum("bixy,ioxy->boxy", x_ft[:, :, -modes1:, :modes2], w2)
     return torch.fft.irfft2(out_ft, s=(H, W))
+
+
+def spectral_conv2d_grads_torch(x, w1, w2, modes1: int, modes2: int, grad_y):
+    """Gradients of the reference recipe (``spectral_conv2d_torch``) by torch autograd in
+    float64 / complex128: (grad_x, grad_w1, grad_w2) for the upstream gradient grad_y."""
+    import torch
+
+    x = torch.as_tensor(x).to(torch.float64).clone().requires_grad_(True)
+    w1 = torch.as_tensor(w1).to(torch.complex128).clone().requires_grad_(True)
+    w2 = torch.as_tensor(w2).to(torch.complex128).clone().requires_grad_(True)
+    B, _, H, W = x.shape
+    x_ft = torch.fft.rfft2(x)
+    out_ft = torch.zeros(B, w1.shape[1], H, W // 2 + 1, dtype=torch.complex128)
+    out_ft[:, :, :modes1, :modes2] = torch.einsum("bixy,ioxy->boxy", x_ft[:, :, :modes1, :modes2], w1)
+    out_ft[:, :, -modes1:, :modes2] = torch.einsum("bixy,ioxy->boxy", x_ft[:, :, -modes1:, :modes2], w2)
+    y = torch.fft.irfft2(out_ft, s=(H, W))
+    y.backward(torch.as_tensor(grad_y).to(torch.float64))
+    return x.grad, w1.grad, w2.grad
 
 
 def fno2d_torch(state: dict, x, *, n_layers: int = 4, modes1: int = 12, modes2: int = 12,

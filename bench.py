@@ -387,6 +387,59 @@ def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
             "l2": "256 MiB flush between steps (not timed)"}
 
 
+def run_backward(steps: int, warmup: int, device, world: int, rank: int) -> dict:
+    """SpectralConv2d backward at the headline workload: grad_x and both weight gradients from
+    grad_y and the forward's corner spectra (scx_spectral_conv2d_bwd: forward DFT of grad_y,
+    two conjugate transposes, two dual-corner mixings, inverse DFT, per-ky scale), replayed
+    from a CUDA graph with a 256 MiB L2 flush between steps.  Algorithmic bytes: grad_y read,
+    grad_x written, the weights read and their gradients written, the saved corners read."""
+    import scx_data
+    import scx_dist
+    import spectral_conv_ext as ext
+
+    x, w1, w2, c = scx_data.make_spectral_case(HEADLINE)
+    B, Cin, Cout, H, W, m1, m2 = (c[k] for k in ("B", "Cin", "Cout", "H", "W", "m1", "m2"))
+    w1d = torch.view_as_real(w1.to(device))
+    w2d = torch.view_as_real(w2.to(device))
+    _, xc = ext.spectral_conv2d_fwd_saved(x.to(device), w1d, w2d, m1, m2)
+    gy = scx_data.gaussian((B, Cout, H, W), 77 + rank).to(device)
+    ext.spectral_conv2d_bwd(gy, xc, w1d, w2d, m1, m2)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        ext.spectral_conv2d_bwd(gy, xc, w1d, w2d, m1, m2)
+    torch.cuda.current_stream(device).wait_stream(side)
+    with torch.cuda.graph(graph):
+        grads = ext.spectral_conv2d_bwd(gy, xc, w1d, w2d, m1, m2)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in evs:
+        flush.zero_()
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    t_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
+    t_ms = scx_dist.max_over_ranks(t_ms, device)
+    ms = t_ms / steps
+    del graph, grads
+    nm = m1 * m2
+    nbytes = 4 * B * H * W * (Cin + Cout) + 2 * 2 * 8 * Cin * Cout * nm + 2 * 8 * B * Cin * nm
+    peak, kind = hbm_peak()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    return {"workload": HEADLINE, "ms_per_step": ms, "samples_per_s": world * B / (ms / 1e3),
+            "launches_per_step": 7, "cuda_graph": True, "bytes_per_step": nbytes,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": kind},
+            "l2": "256 MiB flush between steps (not timed)"}
+
+
 def cpu_baseline(name: str, budget_s: float = 12.0) -> dict:
     """The reference's CPU recipe on the same workload, all host threads, bounded sample."""
     import scx_data
@@ -443,6 +496,8 @@ def ours(args) -> None:
                                      dominant_kernel_frac=r["roofline"]["frac"],
                                      kernels_ms={k: v["ms"] for k, v in r["kernels"].items()})
         extras["fno_ns_b20_w32_64x64_m12_l4"] = run_fno(max(10, args.steps // 2), warmup, device, world, rank)
+        extras["spectral_bwd_b20_c32_128x128_m16"] = run_backward(max(10, args.steps // 2), warmup, device,
+                                                                  world, rank)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.workload)

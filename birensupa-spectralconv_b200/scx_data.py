@@ -181,3 +181,24 @@ REFERENCE_IRREGULAR_SHAPES = [
     (4, 32, 64, 40), (4, 32, 40, 64), (4, 32, 48, 48), (4, 32, 72, 72), (4, 32, 96, 96),
     (4, 32, 160, 160), (4, 32, 192, 192), (4, 32, 256, 64), (2, 16, 100, 100),
 ]
+
+
+# spectral_conv_combo/test_3d_accuracy.py:69-72 (name, B, Cin, Cout, D, H, W, (m1, m2, m3), seed)
+REFERENCE_3D_CASES = [
+    ("tiny_8", 2, 2, 3, 8, 8, 8, (2, 2, 2), 11),
+    ("small_16", 2, 4, 4, 16, 16, 16, (4, 4, 4), 22),
+]
+
+
+def reference_3d_case(batch, cin, cout, D, H, W, modes, seed):
+    """The input and weights test_3d_accuracy.py:40-43 draws: x ~ N(0,1) from a generator
+    seeded with ``seed``; weights with real then imaginary parts uniform in [-0.5, 0.5) from a
+    generator seeded with ``seed + 1`` (reference_pytorch.py:85-102), drawn as
+    [Cin, Cout, m1, m2*m3] and reshaped to [Cin, Cout, m1, m2, m3]."""
+    x = torch.randn(batch, cin, D, H, W, generator=_gen(seed))
+    g = _gen(seed + 1)
+    m1, m2, m3 = modes
+    re = torch.empty(cin, cout, m1, m2 * m3, dtype=torch.float32).uniform_(-0.5, 0.5, generator=g)
+    im = torch.empty_like(re).uniform_(-0.5, 0.5, generator=g)
+    w = torch.complex(re, im).reshape(cin, cout, m1, m2, m3)
+    return x, w

@@ -335,6 +335,34 @@ def spectral_conv2d_bwd(grad_y: torch.Tensor, x_corners: torch.Tensor | None, w1
     return grad_x, gw1, gw2
 
 
+def spectral_conv3d_fwd(x: torch.Tensor, w: torch.Tensor, modes1: int, modes2: int, modes3: int) -> torch.Tensor:
+    """Single-corner SpectralConv3d forward on the device (scx_spectral_conv3d_fwd): x
+    [B,Cin,D,H,W] float32 CUDA; w [Cin,Cout,m1,m2,m3] complex64 (or [...,2] float32) on the
+    same device; returns y [B,Cout,D,H,W]."""
+    _check(x.dim() == 5 and x.is_cuda and x.dtype == torch.float32, "x must be float32 CUDA [B,C,D,H,W]")
+    x = x.contiguous()
+    if w.is_complex():
+        w = torch.view_as_real(w.to(torch.complex64).resolve_conj().contiguous())
+    _check(w.dim() == 6 and w.size(-1) == 2 and w.dtype == torch.float32 and w.is_contiguous(),
+           "weights must be [C_in,C_out,m1,m2,m3] complex64 or [...,2] float32")
+    _check(w.device == x.device, "weights must be on x.device")
+    B, Cin, D, H, W = (int(s) for s in x.shape)
+    _check(int(w.size(0)) == Cin and tuple(int(v) for v in w.shape[2:5]) == (modes1, modes2, modes3),
+           "weights shape mismatch")
+    Cout = int(w.size(1))
+    lib = _scx.lib
+    need = lib.scx_spectral_conv3d_workspace_size(B, Cin, Cout, D, H, W, int(modes1), int(modes2), int(modes3))
+    _check(need > 0, "invalid SpectralConv3d sizes (m1 <= D, m2 <= H, m3 <= W/2+1)")
+    ws = workspace(need, x.device)
+    y = torch.empty(B, Cout, D, H, W, device=x.device, dtype=torch.float32)
+    with _scx.device_guard(x.device):
+        _scx.check(lib.scx_spectral_conv3d_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), B, Cin, Cout, D, H, W,
+                                               int(modes1), int(modes2), int(modes3), ws.data_ptr(), ws.numel(),
+                                               _scx.stream_of(x.device)),
+                   "spectral_conv3d_fwd")
+    return y
+
+
 def prepare(height: int, width: int, modes1: int, modes2: int) -> None:
     """Builds the twiddle tables of one shape on the current device (outside capture)."""
     _scx.check(_scx.lib.scx_prepare(int(height), int(width), int(modes1), int(modes2)), "prepare")

@@ -232,6 +232,27 @@ def spectral_conv2d(x: torch.Tensor, weights1: torch.Tensor, weights2: torch.Ten
     return spectral_conv2d_fused(x, weights1, weights2, modes1, modes2, to_cpu=False, synchronize=False)
 
 
+def spectral_conv3d_supa(x: torch.Tensor, weights: torch.Tensor, modes1: int, modes2: int, modes3: int, *,
+                         to_cpu: bool = True) -> torch.Tensor:
+    """spectral_conv_combo/spectral_conv_ops.py:435-472, all on the device: the reference
+    runs rfftn and irfftn on the CPU around a device mixing; here the truncated DFTs, the
+    mixing and the inverse are one library call.  Returns a host tensor like the reference
+    (``to_cpu=False`` keeps it on the device)."""
+    if x.dim() != 5:
+        raise ValueError(f"x must be [B,C,D,H,W], got {tuple(x.shape)}")
+    device = _device_for(x)
+    x_dev = x.detach().to(device=device, dtype=torch.float32).contiguous()
+    w = weights.detach()
+    w_dev = w.to(device=device, dtype=torch.complex64) if w.is_complex() else w.to(device=device)
+    y = spectral_conv_ext.spectral_conv3d_fwd(x_dev, w_dev, int(modes1), int(modes2), int(modes3))
+    if to_cpu:
+        host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        host.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(device).synchronize()
+        return host
+    return y
+
+
 def warmup_spectral_plans(height: int = 256, width: int = 256, channels_in: int = 32, channels_out: int = 64,
                           modes1: int = 16, modes2: int = 16, batch_size: int = 4) -> None:
     """Builds the shape's twiddle tables and runs the fused path once, outside any stream

@@ -131,6 +131,20 @@ int scx_spectral_conv2d_bwd(const float* grad_y, const float* x_corners, const f
                             int modes1, int modes2, void* workspace, size_t workspace_bytes,
                             scx_stream_t stream);
 
+/* Single-corner SpectralConv3d forward (spectral_conv_combo/reference_pytorch.py:51-82):
+ * rfftn over (D, H, W), the corner [:m1, :m2, :m3] mixed per mode, zero-padded irfftn.
+ * Replaces spectral_conv3d_supa (spectral_conv_combo/spectral_conv_ops.py:435-472).  x
+ * [B][Cin][D][H][W], weights [Cin][Cout][m1][m2][m3] complex (interleaved), y
+ * [B][Cout][D][H][W]; device pointers.  Needs m1 <= D, m2 <= H, m3 <= W/2 + 1; workspace of
+ * scx_spectral_conv3d_workspace_size() bytes, 256-byte aligned. */
+size_t scx_spectral_conv3d_workspace_size(int batch_size, int channels_in, int channels_out,
+                                          int depth, int height, int width, int modes1,
+                                          int modes2, int modes3);
+int scx_spectral_conv3d_fwd(const float* x, const float* weights, float* y, int batch_size,
+                            int channels_in, int channels_out, int depth, int height, int width,
+                            int modes1, int modes2, int modes3, void* workspace,
+                            size_t workspace_bytes, scx_stream_t stream);
+
 /* The same forward from host memory to host memory: the host-facing call of
  * spectral_conv2d_supa with a CPU tensor (spectral_conv/spectral_conv_ops.py:480-505, which
  * copies the batch up, runs the forward and copies it down in turn).  x_host

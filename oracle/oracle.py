@@ -12,7 +12,9 @@ Three independent restatements of ``spectral_conv/reference_pytorch.py:30-47``:
   fp32 (the path the reference times as its CPU baseline).
 
 and of the FNO forward ``fno_ns/model.py:183-198`` (``FNO2d.forward(use_supa=False)``):
-``fno2d_torch``.  ``spectral_conv2d_grads_torch`` differentiates the torch recipe (float64
+``fno2d_torch``; and of the single-corner SpectralConv3d
+(``spectral_conv_combo/reference_pytorch.py:51-82``): ``spectral_conv3d_np``.
+``spectral_conv2d_grads_torch`` differentiates the torch recipe (float64
 autograd) for the SpectralConv2d backward.  All are pinned against fixtures produced by the reference itself
 (``tests/golden/make_golden.py``).
 """
@@ -142,6 +144,18 @@ def spectral_conv2d_grads_torch(x, w1, w2, modes1: int, modes2: int, grad_y):
     y = torch.fft.irfft2(out_ft, s=(H, W))
     y.backward(torch.as_tensor(grad_y).to(torch.float64))
     return x.grad, w1.grad, w2.grad
+
+
+def spectral_conv3d_np(x, w, modes1: int, modes2: int, modes3: int) -> np.ndarray:
+    """spectral_conv_combo/reference_pytorch.py:51-82 restated in numpy float64: rfftn over
+    (D, H, W), the single corner [:m1, :m2, :m3] mixed per mode, zero-padded irfftn."""
+    x = np.asarray(x, dtype=np.float64)
+    w = np.asarray(w).astype(np.complex128)
+    B, _, D, H, W = x.shape
+    xf = np.fft.rfftn(x, axes=(-3, -2, -1))
+    out = np.zeros((B, w.shape[1], D, H, W // 2 + 1), dtype=np.complex128)
+    out[:, :, :modes1, :modes2, :modes3] = np.einsum("bixyz,ioxyz->boxyz", xf[:, :, :modes1, :modes2, :modes3], w)
+    return np.fft.irfftn(out, s=(D, H, W), axes=(-3, -2, -1))
 
 
 def fno2d_torch(state: dict, x, *, n_layers: int = 4, modes1: int = 12, modes2: int = 12,

@@ -10,6 +10,8 @@ What runs (all on the CPU, fp32, exactly the reference's code):
   - the five cases of ``spectral_conv_combo/test_accuracy.py:61-65`` (their seed recipe),
   - the nine shapes of ``spectral_conv_combo/test_irregular_shapes.py:22-32``,
   - the named benchmark workloads (seeded synthetic inputs);
+* ``spectral_conv_combo/reference_pytorch.py: spectral_conv3d`` on the two cases of
+  ``spectral_conv_combo/test_3d_accuracy.py:69-72`` (``--only conv3d`` makes just these);
 * ``fno_ns/model.py: FNO2d.forward(x, use_supa=False)`` (imported with a stub for its
   SUPA-only ``spectral_conv_ops`` import) at width 32, modes 12, 4 layers, on the seeded
   Navier-Stokes-like input.
@@ -88,12 +90,32 @@ def spectral_fixture(ref_mod, name, recipe, B, Cin, Cout, H, W, m1, m2, x, w1, w
     print(f"spectral_{name}: y{tuple(y.shape)} |y|={float(y.norm()):.6g}")
 
 
+def conv3d_fixtures(ref: Path) -> None:
+    """spectral_conv_combo/reference_pytorch.py: spectral_conv3d on the two cases of
+    spectral_conv_combo/test_3d_accuracy.py:69-72, with that test's input recipe
+    (make_random_weights of the same file for the weights); stored whole."""
+    mod = _load_module(ref / "spectral_conv_combo" / "reference_pytorch.py", "reference_pytorch_combo")
+    for (name, B, Cin, Cout, D, H, W, modes, seed) in scx_data.REFERENCE_3D_CASES:
+        x, w = scx_data.reference_3d_case(B, Cin, Cout, D, H, W, modes, seed)
+        w_ref = mod.make_random_weights(Cin, Cout, modes[0], modes[1] * modes[2], seed + 1)
+        assert torch.equal(w_ref.reshape(w.shape), w)
+        y = mod.spectral_conv3d(x, w, *modes)
+        np.savez_compressed(HERE / f"conv3d_{name}.npz", name=name, B=B, Cin=Cin, Cout=Cout, D=D, H=H, W=W,
+                            modes=np.array(modes), seed=seed, x=x.numpy(), w=w.numpy(),
+                            y=y.detach().numpy())
+        print(f"conv3d {name}: y{tuple(y.shape)} |y|={float(y.norm()):.6g}")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", choices=["all", "conv3d"], default="all")
     args = ap.parse_args()
     ref = Path(args.reference)
     torch.set_num_threads(8)
+    conv3d_fixtures(ref)
+    if args.only == "conv3d":
+        return
     ref_mod = _load_module(ref / "spectral_conv" / "reference_pytorch.py", "reference_pytorch")
 
     for (name, B, Cin, Cout, H, W, m1, m2, seed) in scx_data.REFERENCE_ACCURACY_CASES:

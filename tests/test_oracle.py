@@ -147,3 +147,18 @@ def test_fno_init_and_oracle_match_reference():
     with torch.no_grad():
         y2 = model(x, use_supa=False)
     check_against_golden(g, y2.numpy(), 2e-5)
+
+
+@pytest.mark.parametrize("name", ["tiny_8", "small_16"])
+def test_conv3d_oracle_matches_reference(name):
+    """The numpy SpectralConv3d restatement against spectral_conv3d's own outputs
+    (spectral_conv_combo/reference_pytorch.py:51-82) on test_3d_accuracy.py's cases, and the
+    input recipe against the stored inputs."""
+    g = load_golden(f"conv3d_{name}.npz")
+    modes = tuple(int(v) for v in g["modes"])
+    x, w = scx_data.reference_3d_case(int(g["B"]), int(g["Cin"]), int(g["Cout"]), int(g["D"]), int(g["H"]),
+                                      int(g["W"]), modes, int(g["seed"]))
+    assert np.array_equal(x.numpy(), g["x"]) and np.array_equal(w.numpy(), g["w"])
+    y = oracle.spectral_conv3d_np(g["x"], g["w"], *modes)
+    fro, mx = oracle.rel_errors(g["y"], y)
+    assert fro <= 1e-5 and mx <= 1e-5, (fro, mx)

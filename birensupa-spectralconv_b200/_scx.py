@@ -64,6 +64,8 @@ _SIGNATURES = {
     "scx_spectral_conv2d_fwd_noalloc": ([_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _p], _i),
     "scx_spectral_conv3d_workspace_size": ([_i, _i, _i, _i, _i, _i, _i, _i, _i], _sz),
     "scx_spectral_conv3d_fwd": ([_p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _sz, _p], _i),
+    "scx_spectral_conv3d_4c_workspace_size": ([_i, _i, _i, _i, _i, _i, _i, _i, _i], _sz),
+    "scx_spectral_conv3d_4c_fwd": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _sz, _p], _i),
     "scx_spectral_conv2d_bwd_workspace_size": ([_i, _i, _i, _i, _i, _i, _i], _sz),
     "scx_spectral_conv2d_bwd": ([_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _p, _sz, _p], _i),
     "scx_spectral_conv2d_fwd_host": ([_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _p, _p, _p, _sz, _i, _p], _i),

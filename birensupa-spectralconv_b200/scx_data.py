@@ -202,3 +202,12 @@ def reference_3d_case(batch, cin, cout, D, H, W, modes, seed):
     im = torch.empty_like(re).uniform_(-0.5, 0.5, generator=g)
     w = torch.complex(re, im).reshape(cin, cout, m1, m2, m3)
     return x, w
+
+
+# Four-corner SpectralConv3d (official_baseline.py:60-100) fixture cases:
+# (name, B, Cin, Cout, D, H, W, (m1, m2, m3), seed); the module is initialised after
+# torch.manual_seed(seed), the input drawn from a generator seeded with seed + 1.
+OFFICIAL_3D_CASES = [
+    ("official3d_8", 2, 3, 4, 8, 8, 8, (3, 3, 3), 31),
+    ("official3d_overlap", 1, 2, 3, 6, 10, 12, (4, 6, 7), 32),  # 2 m1 > D, 2 m2 > H, Nyquist
+]

@@ -363,6 +363,38 @@ def spectral_conv3d_fwd(x: torch.Tensor, w: torch.Tensor, modes1: int, modes2: i
     return y
 
 
+def spectral_conv3d_4c_fwd(x: torch.Tensor, ws: list, modes1: int, modes2: int, modes3: int) -> torch.Tensor:
+    """Four-corner SpectralConv3d forward on the device (scx_spectral_conv3d_4c_fwd): ws =
+    [w1, w2, w3, w4], each [Cin,Cout,m1,m2,m3] complex64 (or [...,2] float32) on x's device."""
+    _check(x.dim() == 5 and x.is_cuda and x.dtype == torch.float32, "x must be float32 CUDA [B,C,D,H,W]")
+    _check(len(ws) == 4, "four corner weights")
+    x = x.contiguous()
+    wr = []
+    for w in ws:
+        if w.is_complex():
+            w = torch.view_as_real(w.to(torch.complex64).resolve_conj().contiguous())
+        _check(w.dim() == 6 and w.size(-1) == 2 and w.dtype == torch.float32 and w.is_contiguous()
+               and w.device == x.device, "weights must be [C_in,C_out,m1,m2,m3] complex on x.device")
+        wr.append(w)
+    B, Cin, D, H, W = (int(s) for s in x.shape)
+    for w in wr:
+        _check(w.shape == wr[0].shape and int(w.size(0)) == Cin
+               and tuple(int(v) for v in w.shape[2:5]) == (modes1, modes2, modes3), "weights shape mismatch")
+    Cout = int(wr[0].size(1))
+    lib = _scx.lib
+    need = lib.scx_spectral_conv3d_4c_workspace_size(B, Cin, Cout, D, H, W, int(modes1), int(modes2), int(modes3))
+    _check(need > 0, "invalid SpectralConv3d sizes (m1 <= D, m2 <= H, m3 <= W/2+1)")
+    wsb = workspace(need, x.device)
+    y = torch.empty(B, Cout, D, H, W, device=x.device, dtype=torch.float32)
+    with _scx.device_guard(x.device):
+        _scx.check(lib.scx_spectral_conv3d_4c_fwd(x.data_ptr(), wr[0].data_ptr(), wr[1].data_ptr(), wr[2].data_ptr(),
+                                                  wr[3].data_ptr(), y.data_ptr(), B, Cin, Cout, D, H, W, int(modes1),
+                                                  int(modes2), int(modes3), wsb.data_ptr(), wsb.numel(),
+                                                  _scx.stream_of(x.device)),
+                   "spectral_conv3d_4c_fwd")
+    return y
+
+
 def prepare(height: int, width: int, modes1: int, modes2: int) -> None:
     """Builds the twiddle tables of one shape on the current device (outside capture)."""
     _scx.check(_scx.lib.scx_prepare(int(height), int(width), int(modes1), int(modes2)), "prepare")

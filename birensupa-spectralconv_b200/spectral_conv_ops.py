@@ -253,6 +253,35 @@ def spectral_conv3d_supa(x: torch.Tensor, weights: torch.Tensor, modes1: int, mo
     return y
 
 
+class SpectralConv3d(nn.Module):
+    """The four-corner 3-D layer of spectral_conv_combo/official_baseline.py:60-100: same
+    parameters (weights1..4 = scale * rand(cfloat), scale = 1/(Cin Cout)) and construction
+    order, so state dicts load; forward runs on the module's device and returns a device
+    tensor (scx_spectral_conv3d_4c_fwd)."""
+
+    def __init__(self, in_channels: int, out_channels: int, modes1: int, modes2: int, modes3: int):
+        super().__init__()
+        self.in_channels = in_channels
+        self.out_channels = out_channels
+        self.modes1 = modes1
+        self.modes2 = modes2
+        self.modes3 = modes3
+        scale = 1.0 / (in_channels * out_channels)
+        shape = (in_channels, out_channels, modes1, modes2, modes3)
+        self.weights1 = nn.Parameter(scale * torch.rand(*shape, dtype=torch.cfloat))
+        self.weights2 = nn.Parameter(scale * torch.rand(*shape, dtype=torch.cfloat))
+        self.weights3 = nn.Parameter(scale * torch.rand(*shape, dtype=torch.cfloat))
+        self.weights4 = nn.Parameter(scale * torch.rand(*shape, dtype=torch.cfloat))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        device = self.weights1.device
+        if device.type != "cuda":
+            raise RuntimeError("SpectralConv3d runs on a CUDA device: move the module with .cuda()")
+        x_dev = x.detach().to(device=device, dtype=torch.float32).contiguous()
+        ws = [w.detach() for w in (self.weights1, self.weights2, self.weights3, self.weights4)]
+        return spectral_conv_ext.spectral_conv3d_4c_fwd(x_dev, ws, self.modes1, self.modes2, self.modes3)
+
+
 def warmup_spectral_plans(height: int = 256, width: int = 256, channels_in: int = 32, channels_out: int = 64,
                           modes1: int = 16, modes2: int = 16, batch_size: int = 4) -> None:
     """Builds the shape's twiddle tables and runs the fused path once, outside any stream

@@ -145,6 +145,20 @@ int scx_spectral_conv3d_fwd(const float* x, const float* weights, float* y, int 
                             int modes1, int modes2, int modes3, void* workspace,
                             size_t workspace_bytes, scx_stream_t stream);
 
+/* Four-corner SpectralConv3d forward (spectral_conv_combo/official_baseline.py:60-100):
+ * corners (low | high kx) x (low | high ky) x low kz with weights w1 (low, low), w2 (high kx),
+ * w3 (high ky), w4 (high, high), each [Cin][Cout][m1][m2][m3] complex; where corners overlap
+ * (2 m1 > D or 2 m2 > H) the later one wins, as in the baseline's assignments.  Other
+ * arguments as scx_spectral_conv3d_fwd. */
+size_t scx_spectral_conv3d_4c_workspace_size(int batch_size, int channels_in, int channels_out,
+                                             int depth, int height, int width, int modes1,
+                                             int modes2, int modes3);
+int scx_spectral_conv3d_4c_fwd(const float* x, const float* w1, const float* w2, const float* w3,
+                               const float* w4, float* y, int batch_size, int channels_in,
+                               int channels_out, int depth, int height, int width, int modes1,
+                               int modes2, int modes3, void* workspace, size_t workspace_bytes,
+                               scx_stream_t stream);
+
 /* The same forward from host memory to host memory: the host-facing call of
  * spectral_conv2d_supa with a CPU tensor (spectral_conv/spectral_conv_ops.py:480-505, which
  * copies the batch up, runs the forward and copies it down in turn).  x_host

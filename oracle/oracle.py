@@ -158,6 +158,23 @@ def spectral_conv3d_np(x, w, modes1: int, modes2: int, modes3: int) -> np.ndarra
     return np.fft.irfftn(out, s=(D, H, W), axes=(-3, -2, -1))
 
 
+def spectral_conv3d_4c_np(x, ws, modes1: int, modes2: int, modes3: int) -> np.ndarray:
+    """official_baseline.py:84-98 (four-corner SpectralConv3d.forward) restated in numpy
+    float64: corners assigned in the baseline's order, later ones overwriting overlaps."""
+    x = np.asarray(x, dtype=np.float64)
+    ws = [np.asarray(w).astype(np.complex128) for w in ws]
+    B, _, D, H, W = x.shape
+    xf = np.fft.rfftn(x, axes=(-3, -2, -1))
+    out = np.zeros((B, ws[0].shape[1], D, H, W // 2 + 1), dtype=np.complex128)
+    sl1 = [slice(None, modes1), slice(D - modes1, None)]
+    sl2 = [slice(None, modes2), slice(H - modes2, None)]
+    for c, w in enumerate(ws):
+        a, b = c & 1, c >> 1
+        idx = (slice(None), slice(None), sl1[a], sl2[b], slice(None, modes3))
+        out[idx] = np.einsum("bixyz,ioxyz->boxyz", xf[idx], w)
+    return np.fft.irfftn(out, s=(D, H, W), axes=(-3, -2, -1))
+
+
 def fno2d_torch(state: dict, x, *, n_layers: int = 4, modes1: int = 12, modes2: int = 12,
                 instance_norm: bool = True, dtype=None):
     """Restatement of FNO2d.forward(use_supa=False) (fno_ns/model.py:183-198).

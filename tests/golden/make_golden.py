@@ -11,7 +11,8 @@ What runs (all on the CPU, fp32, exactly the reference's code):
   - the nine shapes of ``spectral_conv_combo/test_irregular_shapes.py:22-32``,
   - the named benchmark workloads (seeded synthetic inputs);
 * ``spectral_conv_combo/reference_pytorch.py: spectral_conv3d`` on the two cases of
-  ``spectral_conv_combo/test_3d_accuracy.py:69-72`` (``--only conv3d`` makes just these);
+  ``spectral_conv_combo/test_3d_accuracy.py:69-72``, and ``official_baseline.py:
+  SpectralConv3d`` (four corners) on seeded cases (``--only conv3d`` makes just these);
 * ``fno_ns/model.py: FNO2d.forward(x, use_supa=False)`` (imported with a stub for its
   SUPA-only ``spectral_conv_ops`` import) at width 32, modes 12, 4 layers, on the seeded
   Navier-Stokes-like input.
@@ -106,6 +107,22 @@ def conv3d_fixtures(ref: Path) -> None:
         print(f"conv3d {name}: y{tuple(y.shape)} |y|={float(y.norm()):.6g}")
 
 
+def official3d_fixtures(ref: Path) -> None:
+    """spectral_conv_combo/official_baseline.py: SpectralConv3d (four corners) on seeded
+    inputs, initialised under torch.manual_seed; weights, inputs and outputs stored whole."""
+    mod = _load_module(ref / "spectral_conv_combo" / "official_baseline.py", "official_baseline_combo")
+    for (name, B, Cin, Cout, D, H, W, modes, seed) in scx_data.OFFICIAL_3D_CASES:
+        torch.manual_seed(seed)
+        layer = mod.SpectralConv3d(Cin, Cout, *modes)
+        x = torch.randn(B, Cin, D, H, W, generator=torch.Generator().manual_seed(seed + 1))
+        with torch.no_grad():
+            y = layer(x)
+        ws = {f"w{i}": getattr(layer, f"weights{i}").detach().numpy() for i in range(1, 5)}
+        np.savez_compressed(HERE / f"conv3d_{name}.npz", name=name, B=B, Cin=Cin, Cout=Cout, D=D, H=H, W=W,
+                            modes=np.array(modes), seed=seed, x=x.numpy(), y=y.numpy(), **ws)
+        print(f"official 3-D {name}: y{tuple(y.shape)} |y|={float(y.norm()):.6g}")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -114,6 +131,7 @@ def main() -> None:
     ref = Path(args.reference)
     torch.set_num_threads(8)
     conv3d_fixtures(ref)
+    official3d_fixtures(ref)
     if args.only == "conv3d":
         return
     ref_mod = _load_module(ref / "spectral_conv" / "reference_pytorch.py", "reference_pytorch")

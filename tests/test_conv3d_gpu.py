@@ -59,3 +59,29 @@ def test_conv3d_rejects_bad_modes(cuda_device):
         spectral_conv_ops.spectral_conv3d_supa(x, w, 2, 2, 5)
     with pytest.raises(ValueError):
         spectral_conv_ops.spectral_conv3d_supa(torch.randn(2, 4, 4, 6), w, 2, 2, 4)
+
+
+@pytest.mark.parametrize("name", ["official3d_8", "official3d_overlap"])
+def test_official3d_matches_reference_fixture(name, cuda_device):
+    """spectral_conv_ops.SpectralConv3d (four corners) with the baseline module's own weights
+    against official_baseline.py's SpectralConv3d outputs: overlapping corners (later ones
+    win) and the Nyquist bin included."""
+    import spectral_conv_ops
+
+    g = load_golden(f"conv3d_{name}.npz")
+    modes = tuple(int(v) for v in g["modes"])
+    layer = spectral_conv_ops.SpectralConv3d(int(g["Cin"]), int(g["Cout"]), *modes)
+    with torch.no_grad():
+        for i in range(1, 5):
+            getattr(layer, f"weights{i}").copy_(torch.from_numpy(g[f"w{i}"]))
+    layer = layer.to(cuda_device)
+    y = layer(torch.from_numpy(g["x"]).to(cuda_device))
+    assert y.is_cuda and tuple(y.shape) == g["y"].shape
+    _close(g["y"], y.cpu().numpy())
+
+
+def test_official3d_state_dict_matches_baseline_names():
+    import spectral_conv_ops
+
+    layer = spectral_conv_ops.SpectralConv3d(2, 3, 2, 2, 2)
+    assert list(layer.state_dict()) == ["weights1", "weights2", "weights3", "weights4"]

@@ -162,3 +162,14 @@ def test_conv3d_oracle_matches_reference(name):
     y = oracle.spectral_conv3d_np(g["x"], g["w"], *modes)
     fro, mx = oracle.rel_errors(g["y"], y)
     assert fro <= 1e-5 and mx <= 1e-5, (fro, mx)
+
+
+@pytest.mark.parametrize("name", ["official3d_8", "official3d_overlap"])
+def test_official3d_oracle_matches_reference(name):
+    """The numpy four-corner SpectralConv3d restatement against official_baseline.py's
+    SpectralConv3d outputs, overlap and Nyquist cases included."""
+    g = load_golden(f"conv3d_{name}.npz")
+    modes = tuple(int(v) for v in g["modes"])
+    y = oracle.spectral_conv3d_4c_np(g["x"], [g[f"w{i}"] for i in range(1, 5)], *modes)
+    fro, mx = oracle.rel_errors(g["y"], y)
+    assert fro <= 1e-5 and mx <= 1e-5, (fro, mx)

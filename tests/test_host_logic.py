@@ -88,3 +88,40 @@ def test_fno_model_structure():
         fno_model.FNO2d(n_layers=3)
     nn_free = fno_model.FNO2d(instance_norm=False)
     assert list(nn_free.state_dict()) == names
+
+
+def test_official3d_module_construction_matches_baseline_fixture():
+    """SpectralConv3d builds its four weight tensors in official_baseline.py's order: under the
+    same torch.manual_seed they equal the weights the baseline module drew for the fixture."""
+    import numpy as np
+    import scx_data
+    from conftest import load_golden
+
+    for (name, B, Cin, Cout, D, H, W, modes, seed) in scx_data.OFFICIAL_3D_CASES:
+        g = load_golden(f"conv3d_{name}.npz")
+        torch.manual_seed(seed)
+        layer = spectral_conv_ops.SpectralConv3d(Cin, Cout, *modes)
+        assert list(layer.state_dict()) == ["weights1", "weights2", "weights3", "weights4"]
+        for i in range(1, 5):
+            assert np.array_equal(getattr(layer, f"weights{i}").detach().numpy(), g[f"w{i}"])
+        x = torch.randn(B, Cin, D, H, W, generator=torch.Generator().manual_seed(seed + 1))
+        assert np.array_equal(x.numpy(), g["x"])
+
+
+def test_new_entry_points_check_arguments_before_device_use():
+    w3 = torch.zeros(2, 2, 2, 2, 2, dtype=torch.cfloat)
+    with pytest.raises(ValueError):
+        spectral_conv_ops.spectral_conv3d_supa(torch.zeros(2, 4, 4, 6), w3, 2, 2, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        spectral_conv_ext.spectral_conv3d_fwd(torch.zeros(1, 2, 4, 4, 6), w3, 2, 2, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        spectral_conv_ext.spectral_conv2d_bwd(torch.zeros(1, 2, 8, 8), None, w3, w3, 2, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        spectral_conv_ext.spectral_conv2d_fwd_saved(torch.zeros(1, 2, 8, 8), w3, w3, 2, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        spectral_conv_ops.spectral_conv2d_autograd(torch.zeros(1, 2, 8, 8), w3, w3, 2, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        spectral_conv_ops.SpectralConv3d(2, 2, 2, 2, 2)(torch.zeros(1, 2, 4, 4, 6))
+    with pytest.raises(RuntimeError, match="host tensor"):
+        spectral_conv_ext.spectral_conv2d_fwd_host(torch.zeros(1, 2, 8, 8, dtype=torch.float64), w3, w3, 2, 2,
+                                                   torch.device("cpu"))

@@ -17,8 +17,9 @@
 // the inverse drops those rows of grad_X, which are then zero anyway.
 //
 // Kernels: the forward DFT, two dual-corner mixings and the inverse DFT of the forward path,
-// plus three small elementwise passes (conjugate transposes of W and X per mode, the per-ky
-// scale of grad_W, the overlap-row mask).
+// plus small elementwise passes: the conjugate transposes of W and of X per mode (the per-ky
+// scale of grad_W is applied to X^H: it is per mode, so it commutes with the mixing) and, with
+// overlapping corners, the overlap-row mask.
 #include <algorithm>
 
 #include "scx.h"
@@ -30,12 +31,15 @@ constexpr int kThreads = 256;
 
 inline size_t a256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
-// out_c[d1][d0][m] = conj(in_c[d0][d1][m]) for both corners c = blockIdx.y (complex, NM modes
-// contiguous); threads walk the output in order.
+// out_c[d1][d0][m] = f(m) conj(in_c[d0][d1][m]) for both corners c = blockIdx.y (complex
+// [D0][D1][NM], modes contiguous), f(m) = 1, or c_ky / (H W) for mode m = kx m2 + ky when
+// `scaled` (c_ky = 1 for ky = 0 and, W even, ky = W/2, else 2).  Threads walk the output in
+// order.
 __global__ void __launch_bounds__(kThreads) conj_transpose_kernel(const float2* __restrict__ in1,
                                                                   const float2* __restrict__ in2,
                                                                   float2* __restrict__ out1, float2* __restrict__ out2,
-                                                                  int D0, int D1, int NM) {
+                                                                  int D0, int D1, int NM, int scaled, int m2, int W,
+                                                                  float inv_hw) {
     const float2* in = blockIdx.y == 0 ? in1 : in2;
     float2* out = blockIdx.y == 0 ? out1 : out2;
     const long long total = static_cast<long long>(D0) * D1 * NM;
@@ -45,22 +49,12 @@ __global__ void __launch_bounds__(kThreads) conj_transpose_kernel(const float2* 
         const long long r = t / NM;
         const int d0 = static_cast<int>(r % D0), d1 = static_cast<int>(r / D0);
         const float2 v = __ldg(in + (static_cast<long long>(d0) * D1 + d1) * NM + m);
-        out[t] = make_float2(v.x, -v.y);
-    }
-}
-
-// a_c[r][ky] *= c_ky / (H W) over rows r < rows (rows = Cin * Cout * m1) of both corners.
-__global__ void __launch_bounds__(kThreads) scale_ky_kernel(float2* __restrict__ a1, float2* __restrict__ a2,
-                                                            long long rows, int m2, int W, float inv_hw) {
-    float2* a = blockIdx.y == 0 ? a1 : a2;
-    const long long total = rows * m2;
-    for (long long t = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x; t < total;
-         t += static_cast<long long>(gridDim.x) * kThreads) {
-        const int ky = static_cast<int>(t % m2);
-        const bool single = ky == 0 || ((W % 2 == 0) && ky == W / 2);
-        const float f = single ? inv_hw : 2.0f * inv_hw;
-        const float2 v = a[t];
-        a[t] = make_float2(v.x * f, v.y * f);
+        float f = 1.f;
+        if (scaled) {
+            const int ky = m % m2;
+            f = (ky == 0 || ((W % 2) == 0 && ky == W / 2)) ? inv_hw : 2.0f * inv_hw;
+        }
+        out[t] = make_float2(f * v.x, -(f * v.y));
     }
 }
 
@@ -155,33 +149,29 @@ extern "C" int scx_spectral_conv2d_bwd(const float* grad_y, const float* x_corne
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
+    // conjugate transposes per mode: W^H [Cout][Cin] ahead of the grad_x chain, (c_ky / HW) X^H
+    // [Cin][B] after it
+    const float inv_hw = static_cast<float>(1.0 / (static_cast<double>(H) * W));
     if (grad_x) {
-        // grad_x = inv(G W^H): W^H [Cout][Cin] per mode
-        const long long n = static_cast<long long>(Cin) * Cout * NM;
-        conj_transpose_kernel<<<dim3(blocks_for(n), 2), kThreads, 0, s>>>(
-            reinterpret_cast<const float2*>(weights1), reinterpret_cast<const float2*>(weights2), WH1, WH2, Cin,
-            Cout, NM);
+        // grad_x = inv(G W^H)
+        conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(Cin) * Cout * NM), 2), kThreads, 0, s>>>(
+            reinterpret_cast<const float2*>(weights1), reinterpret_cast<const float2*>(weights2), WH1, WH2, Cin, Cout,
+            NM, 0, m2, W, inv_hw);
         e = cudaGetLastError();
         if (e == cudaSuccess) e = scx::launch_mix(G1, G2, WH1, WH2, Z1, Z2, 2, B, Cout, Cin, NM, s);
         if (e == cudaSuccess) e = scx::dft_inv(Z1, Z2, NM, m2, grad_x, B * Cin, H, W, m1, m2, *tw, s, scratch, L.scratch);
         if (e != cudaSuccess) return e;
     }
     if (grad_w1) {
-        // grad_W = (c_ky / HW) X^H G: X^H [Cin][B] per mode
+        // grad_W = ((c_ky / HW) X^H) G; X1 then X2 are contiguous at x_corners
         const float2* X1 = reinterpret_cast<const float2*>(x_corners);
         const float2* X2 = X1 + static_cast<size_t>(B) * Cin * NM;
-        const long long n = static_cast<long long>(B) * Cin * NM;
-        conj_transpose_kernel<<<dim3(blocks_for(n), 2), kThreads, 0, s>>>(X1, X2, XH1, XH2, B, Cin, NM);
+        conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(B) * Cin * NM), 2), kThreads, 0, s>>>(
+            X1, X2, XH1, XH2, B, Cin, NM, 1, m2, W, inv_hw);
         e = cudaGetLastError();
         if (e == cudaSuccess)
             e = scx::launch_mix(XH1, XH2, G1, G2, reinterpret_cast<float2*>(grad_w1), reinterpret_cast<float2*>(grad_w2),
                                 2, Cin, B, Cout, NM, s);
-        if (e != cudaSuccess) return e;
-        const long long rows = static_cast<long long>(Cin) * Cout * m1;
-        scale_ky_kernel<<<dim3(blocks_for(rows * m2), 2), kThreads, 0, s>>>(
-            reinterpret_cast<float2*>(grad_w1), reinterpret_cast<float2*>(grad_w2), rows, m2, W,
-            static_cast<float>(1.0 / (static_cast<double>(H) * W)));
-        e = cudaGetLastError();
     }
     return e;
 }

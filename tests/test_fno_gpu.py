@@ -51,6 +51,7 @@ def test_fno_matches_reference_golden(cuda_device):
     dict(B=1, T=3, H=17, W=23, width=8, m1=5, m2=7, layers=4, norm=True),       # odd sizes
     dict(B=2, T=4, H=88, W=88, width=32, m1=10, m2=12, layers=4, norm=True),    # 8-CTA cluster, partial CTA
     dict(B=2, T=4, H=96, W=96, width=16, m1=8, m2=8, layers=4, norm=True),      # plane too large for a cluster
+    dict(B=2, T=5, H=32, W=32, width=32, m1=8, m2=8, layers=4, norm=False),     # four-pixel skip with GELU
 ])
 def test_fno_shapes_vs_oracle(cfg, cuda_device):
     import fno_model

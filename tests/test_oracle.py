@@ -173,3 +173,78 @@ def test_official3d_oracle_matches_reference(name):
     y = oracle.spectral_conv3d_4c_np(g["x"], [g[f"w{i}"] for i in range(1, 5)], *modes)
     fro, mx = oracle.rel_errors(g["y"], y)
     assert fro <= 1e-5 and mx <= 1e-5, (fro, mx)
+
+
+def test_gradient_oracle_matches_finite_differences():
+    """The backward's oracle (float64 autograd of the reference recipe) against central
+    differences of the forward, on a small case with overlapping corners and odd W."""
+    torch.manual_seed(0)
+    B, Cin, Cout, H, W, m1, m2 = 1, 2, 3, 6, 7, 4, 3
+    x = torch.randn(B, Cin, H, W, dtype=torch.float64)
+    w1 = torch.randn(Cin, Cout, m1, m2, dtype=torch.complex128)
+    w2 = torch.randn(Cin, Cout, m1, m2, dtype=torch.complex128)
+    gy = torch.randn(B, Cout, H, W, dtype=torch.float64)
+    gx, gw1, _ = oracle.spectral_conv2d_grads_torch(x, w1, w2, m1, m2, gy)
+
+    def loss(xx, ww1):
+        x_ft = torch.fft.rfft2(xx)
+        out = torch.zeros(B, Cout, H, W // 2 + 1, dtype=torch.complex128)
+        out[:, :, :m1, :m2] = torch.einsum("bixy,ioxy->boxy", x_ft[:, :, :m1, :m2], ww1)
+        out[:, :, -m1:, :m2] = torch.einsum("bixy,ioxy->boxy", x_ft[:, :, -m1:, :m2], w2)
+        return float((torch.fft.irfft2(out, s=(H, W)) * gy).sum())
+
+    eps = 1e-6
+    for idx in [(0, 1, 2, 3), (0, 0, 5, 6)]:
+        e = torch.zeros_like(x)
+        e[idx] = eps
+        fd = (loss(x + e, w1) - loss(x - e, w1)) / (2 * eps)
+        assert abs(fd - float(gx[idx])) <= 1e-6 * max(1.0, abs(fd))
+    for idx in [(1, 2, 3, 1), (0, 0, 0, 0)]:
+        for part in (1.0, 1j):  # d/dRe and d/dIm: torch's gradient is dL/dRe + i dL/dIm
+            e = torch.zeros_like(w1)
+            e[idx] = eps * part
+            fd = (loss(x, w1 + e) - loss(x, w1 - e)) / (2 * eps)
+            got = float(gw1[idx].real) if part == 1.0 else float(gw1[idx].imag)
+            assert abs(fd - got) <= 1e-6 * max(1.0, abs(fd))
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 4, 20, 23, 12, 7), (1, 2, 3, 16, 16, 5, 9), (2, 3, 2, 12, 10, 4, 6)])
+def test_backward_decomposition_matches_autograd(shape):
+    """The sequence scx_spectral_conv2d_bwd runs, restated in numpy float64: G = forward DFT of
+    grad_y (corner-1 rows that corner 2 overwrites zeroed); grad_x = inverse DFT (with its C2R
+    row weights c_ky / HW) of G W^H; grad_W = ((c_ky / HW) X^H) G.  It equals autograd of the
+    reference recipe, overlap, odd W and the Nyquist column included."""
+    B, Cin, Cout, H, W, m1, m2 = shape
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((B, Cin, H, W))
+    gy = rng.standard_normal((B, Cout, H, W))
+    w1 = rng.standard_normal((Cin, Cout, m1, m2)) + 1j * rng.standard_normal((Cin, Cout, m1, m2))
+    w2 = rng.standard_normal((Cin, Cout, m1, m2)) + 1j * rng.standard_normal((Cin, Cout, m1, m2))
+    gx_ref, gw1_ref, gw2_ref = [t.numpy() for t in oracle.spectral_conv2d_grads_torch(
+        torch.tensor(x), torch.tensor(w1), torch.tensor(w2), m1, m2, torch.tensor(gy))]
+    rows = [np.arange(m1), np.arange(H - m1, H)]
+    c = np.array([1.0 if (k == 0 or (W % 2 == 0 and k == W // 2)) else 2.0 for k in range(m2)]) / (H * W)
+
+    def fwd(a, r):
+        Fh = np.exp(-2j * np.pi * np.outer(r, np.arange(H)) / H)
+        Fw = np.exp(-2j * np.pi * np.outer(np.arange(W), np.arange(m2)) / W)
+        return np.einsum("rh,bchw,wk->bcrk", Fh, a, Fw)
+
+    def inv(Y1, Y2):
+        y = 0
+        for Y, r, drop in ((Y1, rows[0], True), (Y2, rows[1], False)):
+            keep = np.array([not (drop and v >= H - m1) for v in r])
+            Gh = np.exp(2j * np.pi * np.outer(np.arange(H), r) / H) * keep
+            Gw = np.exp(2j * np.pi * np.outer(np.arange(m2), np.arange(W)) / W) * c[:, None]
+            y = y + np.real(np.einsum("hr,bcrk,kw->bchw", Gh, Y, Gw))
+        return y
+
+    X1, X2 = fwd(x, rows[0]), fwd(x, rows[1])
+    G1, G2 = fwd(gy, rows[0]), fwd(gy, rows[1])
+    if 2 * m1 > H:
+        G1[:, :, H - m1:, :] = 0
+    gx = inv(np.einsum("bork,iork->birk", G1, np.conj(w1)), np.einsum("bork,iork->birk", G2, np.conj(w2)))
+    gw1 = np.einsum("birk,bork->iork", np.conj(X1) * c, G1)
+    gw2 = np.einsum("birk,bork->iork", np.conj(X2) * c, G2)
+    for ref, got in ((gx_ref, gx), (gw1_ref, gw1), (gw2_ref, gw2)):
+        assert np.abs(ref - got).max() <= 1e-12 * np.abs(ref).max()

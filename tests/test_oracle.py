@@ -248,3 +248,44 @@ def test_backward_decomposition_matches_autograd(shape):
     gw2 = np.einsum("birk,bork->iork", np.conj(X2) * c, G2)
     for ref, got in ((gx_ref, gx), (gw1_ref, gw1), (gw2_ref, gw2)):
         assert np.abs(ref - got).max() <= 1e-12 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("name", ["official3d_8", "official3d_overlap"])
+def test_official3d_slot_decomposition_matches_baseline(name):
+    """The sequence scx_spectral_conv3d_4c_fwd runs, restated in numpy float64: forward DFTs
+    keep 2 m1 / 2 m2 slot rows (low then high frequencies), the four corners are mixed, the
+    slots are rebuilt with the baseline's overwrite order (a frequency held by several corners
+    keeps the last corner's value, its other slots are zero), and the inverse sums over the
+    slots with the C2R weights.  It equals official_baseline.py's output."""
+    g = load_golden(f"conv3d_{name}.npz")
+    m1, m2, m3 = (int(v) for v in g["modes"])
+    x = g["x"].astype(np.float64)
+    ws = [g[f"w{i}"].astype(np.complex128) for i in range(1, 5)]
+    B, _, D, H, W = x.shape
+
+    def freq(u, m, n):
+        return n - 2 * m + u if u >= m else u
+
+    f1 = np.array([freq(u, m1, D) for u in range(2 * m1)])
+    f2 = np.array([freq(u, m2, H) for u in range(2 * m2)])
+    Fd = np.exp(-2j * np.pi * np.outer(f1, np.arange(D)) / D)
+    Fh = np.exp(-2j * np.pi * np.outer(f2, np.arange(H)) / H)
+    Fw = np.exp(-2j * np.pi * np.outer(np.arange(W), np.arange(m3)) / W)
+    X = np.einsum("ad,bh,icdhw,wk->icabk", Fd, Fh, x, Fw)  # [B][Cin][2 m1][2 m2][m3]
+    Yall = np.zeros((B, ws[0].shape[1], 2 * m1, 2 * m2, m3), dtype=np.complex128)
+    for s1 in range(2 * m1):
+        for s2 in range(2 * m2):
+            a, b = int(s1 >= m1), int(s2 >= m2)
+            c = a + 2 * b
+            kx_in = (f1[s1] < m1, f1[s1] >= D - m1)
+            ky_in = (f2[s2] < m2, f2[s2] >= H - m2)
+            if any(kx_in[c2 & 1] and ky_in[c2 >> 1] for c2 in range(c + 1, 4)):
+                continue
+            Yall[:, :, s1, s2, :] = np.einsum("bik,iok->bok", X[:, :, s1, s2, :], ws[c][:, :, s1 % m1, s2 % m2, :])
+    cw = np.array([1.0 if (k == 0 or (W % 2 == 0 and k == W // 2)) else 2.0 for k in range(m3)]) / (D * H * W)
+    Gd = np.exp(2j * np.pi * np.outer(np.arange(D), f1) / D)
+    Gh = np.exp(2j * np.pi * np.outer(np.arange(H), f2) / H)
+    Gw = np.exp(2j * np.pi * np.outer(np.arange(m3), np.arange(W)) / W) * cw[:, None]
+    y = np.real(np.einsum("da,hb,ocabk,kw->ocdhw", Gd, Gh, Yall, Gw))
+    fro, mx = oracle.rel_errors(g["y"], y)
+    assert fro <= 1e-5 and mx <= 1e-5, (fro, mx)

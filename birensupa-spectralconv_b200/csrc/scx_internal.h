@@ -133,8 +133,9 @@ cudaError_t dft_inv(const float2* in1, const float2* in2, long long in_plane_str
                     int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream,
                     float* scratch = nullptr, size_t scratch_bytes = 0);
 
-// Device watchdog word of the current device (allocated and zeroed on first use, never
-// freed): the tensor-core kernels store a non-zero code there when they give up on a wait.
+// Device watchdog word of the current device (a static device variable, zero at module load,
+// whose address is looked up once per device; no allocation): the tensor-core and TMA-ring
+// kernels store a non-zero code there when they give up on a wait.
 cudaError_t device_watchdog(int** out);
 
 // FNO projection y = b2 + W2 GELU(b1 + W1 h) on the tensor core (scx_fno_proj_tc.cu): h is

@@ -17,7 +17,12 @@
 // Rules of use:
 // * The first call on a device looks up the array's device address with
 //   cudaGetSymbolAddress (with that device current) and caches it per device; make that
-//   first call before any stream capture.
+//   first call before any stream capture.  The cache does not survive a cudaDeviceReset.
+// * The mixing kernel's bounded waits report to the library's watchdog word, which is a
+//   static device variable as well (no allocation); after a call whose result matters, read
+//   scx_watchdog() once the stream has been synchronised.
+// * The truncated DFTs use the FFMA kernels: the tensor-core kernels need operand tables
+//   that the library allocates, so this path is slower on the shapes those kernels cover.
 // * All calls share the array.  Calls that may overlap on the GPU (different streams,
 //   different host threads without ordering) race on it and corrupt each other's results;
 //   order them on one stream.

@@ -99,6 +99,12 @@ cudaError_t prepare_kernel(const void* kernel, size_t bytes, int threads, int* b
     return cudaSuccess;
 }
 
+// The watchdog word: one per device, zero when the module is loaded.  It is a static device
+// variable rather than an allocation, so that finding it needs no cudaMalloc and no copy
+// (the allocation-free entry point reaches it too).  In host code the name only stands for
+// the symbol: the device address comes from cudaGetSymbolAddress.
+static __device__ int g_watchdog_word = 0;
+
 cudaError_t device_watchdog(int** out) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
@@ -111,17 +117,12 @@ cudaError_t device_watchdog(int** out) {
         *out = it->second;
         return cudaSuccess;
     }
-    int* w = nullptr;
-    err = cudaMalloc(&w, sizeof(int));
+    void* w = nullptr;
+    err = cudaGetSymbolAddress(&w, g_watchdog_word);
     if (err != cudaSuccess) return err;
-    const int zero = 0;
-    err = cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice);
-    if (err != cudaSuccess) {
-        cudaFree(w);
-        return err;
-    }
-    words[dev] = w;
-    *out = w;
+    if (w == nullptr) return cudaErrorInvalidSymbol;
+    words[dev] = static_cast<int*>(w);
+    *out = static_cast<int*>(w);
     return cudaSuccess;
 }
 

@@ -241,8 +241,14 @@ int scx_fno2d_fwd(const scx_fno2d_config* cfg, const scx_fno2d_params* params, c
  * i.e. about 16*B*(Cin+Cout)*m1*m2 + 32*(W*m2 + 2*m1*H) bytes; larger shapes return
  * cudaErrorMemoryAllocation (2) without launching.  The first call on a device looks up
  * the array's address (cudaGetSymbolAddress) with that device current: make it before
- * any stream capture.  All calls share the array: calls that overlap on the GPU race, so
- * order them on one stream.  Nothing has to be cleared between calls. */
+ * any stream capture.  The address is cached per device for the life of the process, so it
+ * does not survive a cudaDeviceReset of that device.  All calls share the array: calls that
+ * overlap on the GPU race, so order them on one stream.  Nothing has to be cleared between
+ * calls.  The truncated DFTs run on the FFMA kernels (the tensor-core kernels read operand
+ * tables that the library allocates), so expect lower throughput than
+ * scx_spectral_conv2d_fwd on the shapes where that one uses the tensor cores.  As with every
+ * entry point, a kernel that gave up on a bounded wait leaves y undefined and records a code
+ * that scx_watchdog() returns: read it after synchronising when the result matters. */
 int scx_spectral_conv2d_fwd_noalloc(const float* x, const float* weights1, const float* weights2,
                                     float* y, int batch_size, int channels_in, int channels_out,
                                     int height, int width, int modes1, int modes2,

@@ -46,6 +46,9 @@ import torch  # noqa: E402
 
 HEADLINE = "spectral_b20_c32_128x128_m16_grf"
 EXTRA_WORKLOADS = ["spectral_b20_c32_64x64_m12", "spectral_b16_c64_256x256_m32"]
+IRREGULAR_WORKLOADS = ["spectral_b7_c20to36_96x160_m16x20", "spectral_b3_c24_100x72_m10",
+                       "spectral_b1_c48_130x130_m24"]
+STRONG_WORKLOAD = "spectral_b16_c64_256x256_m32"  # B=16 in total, sharded over the ranks
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 
@@ -57,7 +60,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default=HEADLINE)
-    ap.add_argument("--no-extras", action="store_true", help="skip the 64x64 / 256x256 entries")
+    ap.add_argument("--no-extras", action="store_true", help="skip every extra workload")
+    ap.add_argument("--extras", default="all",
+                    help="comma list of extra workloads to run: 64, 256, irr, c3s, fno, bwd (default: all)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -83,6 +88,43 @@ def spectral_bytes(c: dict) -> dict:
         "dft_inv": 16 * B * Cout * nm + 4 * B * Cout * H * W,
         "fused_path": 4 * B * H * W * (Cin + Cout) + 16 * Cin * Cout * nm,
     }
+
+
+def launches_per_forward(c: dict) -> int:
+    """Kernel launches of one scx_spectral_conv2d_fwd, by the library's dispatch rule: three
+    (forward DFT, mixing, inverse DFT; at 256 x 256 the forward folds its four parity
+    sub-problems in one launch and the inverse computes the four output quadrants in one), or
+    seven when another plane with a 256-point side runs folded (the folding forward, mixing,
+    four inverse sub-transforms, unfold)."""
+    def direct(H, W, m1, m2):  # tc_fwd_supported
+        return (H in (64, 128) and W in (64, 128) and 1 <= m1 and 2 * m1 <= 32 and 1 <= m2 <= 32 and m1 <= H
+                and m2 <= W // 2 + 1)
+
+    H, W, m1, m2 = c["H"], c["W"], c["m1"], c["m2"]
+    split = (H in (128, 256) and W in (128, 256) and m1 % 2 == 0 and m2 % 2 == 0 and 2 * m1 <= H
+             and m1 >= 2 and m2 >= 2 and direct(H // 2, W // 2, m1 // 2, m2 // 2))
+    quad = H == 256 and W == 256 and 1 <= m1 <= 32 and 1 <= m2 <= 32  # tc_quad_supported
+    return 7 if split and not direct(H, W, m1, m2) and not quad else 3
+
+
+def fixture_error(name: str, y: torch.Tensor) -> dict | None:
+    """Error of a device result against the reference's output for the same workload, as
+    committed in tests/golden (4096 sampled outputs, per-plane norms): the margin left under
+    the 1e-4 bound."""
+    import numpy as np
+
+    path = REPO / "tests" / "golden" / f"spectral_{name}.npz"
+    if not path.exists():
+        return None
+    with np.load(path, allow_pickle=False) as z:
+        g = {k: z[k] for k in z.files}
+    yh = y.detach().double().cpu().numpy()
+    flat = yh.reshape(-1)
+    sampled = float(np.abs(flat[g["sample_idx"]] - g["sample_val"].astype(np.float64)).max() / float(g["y_absmax"]))
+    norms = np.sqrt((yh ** 2).sum(axis=(-2, -1)))
+    norm_rel = float(np.abs(norms - g["y_plane_norm"]).max() / max(float(g["y_plane_norm"].max()), 1e-30))
+    return {"max_abs_rel_sampled": sampled, "plane_norm_rel": norm_rel, "tol": 1e-4,
+            "vs": f"tests/golden/spectral_{name}.npz (the reference's reference_pytorch.py output)"}
 
 
 class ClockSampler:
@@ -243,12 +285,15 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
     barrier()
     t_ms_max = scx_dist.max_over_ranks(t_ms, device)
     ms_per_step = t_ms_max / steps
-    # 256-point grids run as a quadrant fold, four tensor-core forwards, the mixing, four
-    # inverses and an unfold; the per-kernel split below covers the three-kernel shapes
-    folded = H > 128 or W > 128
+    # 256-point grids run as a folding tensor-core forward, the mixing, four inverses and an
+    # unfold; the per-kernel split below covers the three-kernel shapes
+    n_launch = launches_per_forward(c)
+    folded = n_launch != 3
     res = {"cfg": c, "ms_per_step": ms_per_step, "samples_per_s": world * B / (ms_per_step / 1e3),
            "ms_per_step_eager": t_eager / steps,
-           "launches_per_step": 11 if folded else 3, "clocks": clocks, "cuda_graph": True}
+           "launches_per_step": n_launch, "clocks": clocks, "cuda_graph": True}
+    if rank == 0:
+        res["accuracy"] = fixture_error(name, ys[0])
 
     nbytes = spectral_bytes(c)
     peak, peak_kind = hbm_peak()
@@ -300,21 +345,21 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
             del g
 
         total = sum(kern.values())
-        res["kernels"] = {k: {"ms": v, "share": v / total, "bytes": nbytes[k],
-                              "gbs": nbytes[k] / (v / 1e3) / 1e9} for k, v in kern.items()}
-        dom = max(kern, key=kern.get)
-        achieved = nbytes[dom] / (kern[dom] / 1e3) / 1e9
-        res["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                           "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
-                           "bytes_per_launch": nbytes[dom], "ms_per_launch": kern[dom]}
+        traffic = {}
         prof = REPO / "profiles" / "ncu_traffic.json"
         if prof.exists():
             try:
-                entry = json.loads(prof.read_text()).get(name, {}).get(dom)
-                if entry is not None:
-                    res["roofline"]["traffic"] = entry
+                traffic = json.loads(prof.read_text()).get(name, {})
             except Exception:
-                pass
+                traffic = {}
+        res["kernels"] = {k: {"ms": v, "share": v / total, "bytes": nbytes[k],
+                              "gbs": nbytes[k] / (v / 1e3) / 1e9, "frac": nbytes[k] / (v / 1e3) / 1e9 / peak,
+                              "traffic": traffic.get(k)} for k, v in kern.items()}
+        dom = max(kern, key=kern.get)
+        achieved = nbytes[dom] / (kern[dom] / 1e3) / 1e9
+        res["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                           "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic.get(dom),
+                           "bytes_per_launch": nbytes[dom], "ms_per_launch": kern[dom]}
 
     if with_e2e:
         # public host API: pinned host input in, host result out, copies inside the region
@@ -342,6 +387,111 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
     return res
 
 
+def run_strong(name: str, steps: int, warmup: int, device, world: int, rank: int) -> dict:
+    """Strong scaling: the workload's whole batch (B=16 at 256x256, C64, m32) is split into
+    contiguous shards over the ranks (16/8/4/2 items per GPU at N = 1/2/4/8); a step is the
+    forward of this rank's shard (one CUDA graph) followed by the gather of every shard into
+    a preallocated [B, Cout, H, W] tensor on rank 0 (one group of NCCL point-to-point
+    transfers).  L2 is flushed (256 MiB write, not timed) before every step; each step has its
+    own CUDA events on the launching stream, and the step time is the max over ranks.
+
+    Rank 0 then runs the whole batch alone with the same protocol: its time is the one-GPU
+    time the scaling efficiency is taken against, and its output is compared with the
+    gathered one (sharded == single)."""
+    import scx_data
+    import scx_dist
+    import spectral_conv_ext as ext
+
+    x_cpu, w1c, w2c, c = scx_data.make_spectral_case(name)
+    B, Cin, Cout, H, W, m1, m2 = (c[k] for k in ("B", "Cin", "Cout", "H", "W", "m1", "m2"))
+    lib = ext._scx.lib
+    w1 = torch.view_as_real(w1c.to(device)).contiguous()
+    w2 = torch.view_as_real(w2c.to(device)).contiguous()
+    ext.prepare(H, W, m1, m2)
+    lo, hi = scx_dist.shard_range(B, world, rank)
+    nb = hi - lo
+    x_loc = x_cpu[lo:hi].contiguous().to(device)
+    out_all = torch.empty(B, Cout, H, W, device=device) if rank == 0 else None
+    # rank 0 computes its shard straight into its slice of the gathered output
+    y_loc = out_all[lo:hi] if rank == 0 else torch.empty(nb, Cout, H, W, device=device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def make_forward(x, y, nbatch):
+        ws_bytes = lib.scx_spectral_conv2d_workspace_size(nbatch, Cin, Cout, H, W, m1, m2)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
+
+        def fwd(h):
+            rc = lib.scx_spectral_conv2d_fwd(x.data_ptr(), w1.data_ptr(), w2.data_ptr(), y.data_ptr(), nbatch, Cin,
+                                             Cout, H, W, m1, m2, ws.data_ptr(), ws_bytes, h)
+            if rc != 0:
+                raise RuntimeError(f"scx_spectral_conv2d_fwd failed: {rc}")
+
+        fwd(stream.cuda_stream)  # first use of the shape builds its tables outside the capture
+        torch.cuda.synchronize(device)
+        graph = capture_graphs(device, [fwd])[0]
+        return graph, ws
+
+    graph, ws_loc = make_forward(x_loc, y_loc, nb)
+
+    def timed(step, n):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        torch.cuda.synchronize(device)
+        return sum(e0.elapsed_time(e1) for e0, e1 in evs) / n
+
+    def step_gather():
+        graph.replay()
+        if world > 1:
+            scx_dist.gather_batch_into(y_loc, out_all, B)
+
+    for _ in range(warmup):
+        step_gather()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    t_fwd = scx_dist.max_over_ranks(timed(graph.replay, steps), device)
+    if world > 1:
+        torch.distributed.barrier()
+    t_step = scx_dist.max_over_ranks(timed(step_gather, steps), device)
+    res = {"workload": name, "batch_total": B, "batch_per_gpu": scx_dist.shard_sizes(B, world),
+           "ms_per_step": t_step, "samples_per_s": B / (t_step / 1e3), "ms_forward_only": t_fwd,
+           "gather_share": max(0.0, (t_step - t_fwd) / t_step) if world > 1 else 0.0,
+           "gather": "NCCL point-to-point group into a preallocated tensor on rank 0" if world > 1 else None,
+           "launches_per_step": launches_per_forward(c), "cuda_graph": True, "scaling": "strong",
+           "l2": "256 MiB flush between steps (not timed)"}
+    if world > 1:
+        torch.distributed.barrier()
+    if rank == 0:
+        if world > 1:
+            x_all = x_cpu.to(device)
+            y_all = torch.empty(B, Cout, H, W, device=device)
+            graph1, ws1 = make_forward(x_all, y_all, B)
+            for _ in range(warmup):
+                graph1.replay()
+            t_single = timed(graph1.replay, steps)
+            del graph1, ws1
+        else:
+            y_all, t_single = out_all, t_step
+        diff = (out_all - y_all).abs().max().item()
+        scale = y_all.abs().max().item()
+        res.update(ms_single_gpu=t_single, efficiency=t_single / (world * t_step),
+                   # the mixing's tile shape (and so its split of the channel sum) depends on
+                   # the batch size: equal up to that rounding, bitwise when the split agrees
+                   sharded_equals_single=bool(diff <= 1e-5 * max(scale, 1e-30)),
+                   sharded_bitwise_equal=bool(torch.equal(out_all, y_all)),
+                   sharded_max_abs_rel_diff=diff / max(scale, 1e-30),
+                   accuracy=fixture_error(name, out_all))
+    if world > 1:
+        torch.distributed.barrier()
+    del graph
+    return res
+
+
 def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
     """FNO-NS forward, B=20 per GPU, [B,64,64,12] channels-last input, width 32, modes 12,
     4 layers, InstanceNorm layers; the whole forward is one libscx call replayed from a CUDA
@@ -357,7 +507,9 @@ def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
                             in_channels=fw["frames"]).to(device)
     B = fw["B"]
     x = scx_data.fno_input(B, fw["seed"] + rank, H=fw["H"], W=fw["W"], frames=fw["frames"]).to(device)
-    out = torch.empty(B, 1, fw["H"], fw["W"], device=device)
+    # the gathered [B * world] output lives on rank 0, which writes its own shard into it
+    out_all = torch.empty(B * world, 1, fw["H"], fw["W"], device=device) if rank == 0 else None
+    out = out_all[:B] if rank == 0 else torch.empty(B, 1, fw["H"], fw["W"], device=device)
     model.forward_device(x, channels_last=True, out=out)
     torch.cuda.synchronize(device)
     graph = torch.cuda.CUDAGraph()
@@ -374,7 +526,7 @@ def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
     def step():
         graph.replay()
         if world > 1:
-            scx_dist.gather_batch(out, B * world)
+            scx_dist.gather_batch_into(out, out_all, B * world)
 
     for _ in range(warmup):
         step()
@@ -396,7 +548,8 @@ def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
             # lift, then per layer forward DFT, mixing, inverse DFT and the fused skip +
             # instance norm + GELU (one cluster launch at 64x64), then the projection
             "launches_per_step": 2 + 4 * fw["layers"], "cuda_graph": True,
-            "gather": "nccl all_gather_into_tensor to rank 0 inside the step" if world > 1 else None,
+            "gather": "NCCL point-to-point group into a preallocated tensor on rank 0, inside the step"
+            if world > 1 else None,
             "l2": "256 MiB flush between steps (not timed)"}
 
 
@@ -495,23 +648,43 @@ def ours(args) -> None:
     res = run_spectral(args.workload, args.steps, warmup, device, world, rank, with_e2e=True,
                        with_breakdown=True, sampler_gpu=local_rank if rank == 0 else None)
     extras = {}
+    wanted = {"64", "256", "fno", "bwd"} if args.extras == "all" else set(args.extras.split(","))
     if not args.no_extras:
         for wname in EXTRA_WORKLOADS:
-            if wname == args.workload:
+            if wname == args.workload or wname.split("_")[3].split("x")[0] not in wanted:
                 continue
             r = run_spectral(wname, max(10, args.steps // 2), warmup, device, world, rank, with_e2e=False,
                              with_breakdown=True, sampler_gpu=None)
             extras[wname] = {"ms_per_step": r["ms_per_step"], "samples_per_s": r["samples_per_s"],
                              "ms_per_step_eager": r["ms_per_step_eager"],
                              "roofline_fused_path_frac": r["roofline_fused_path"]["frac"],
-                             "launches_per_step": r["launches_per_step"], "cuda_graph": True}
+                             "launches_per_step": r["launches_per_step"], "cuda_graph": True,
+                             "accuracy": r.get("accuracy")}
             if "roofline" in r:
                 extras[wname].update(dominant_kernel=r["roofline"]["kernel"],
                                      dominant_kernel_frac=r["roofline"]["frac"],
                                      kernels_ms={k: v["ms"] for k, v in r["kernels"].items()})
-        extras["fno_ns_b20_w32_64x64_m12_l4"] = run_fno(max(10, args.steps // 2), warmup, device, world, rank)
-        extras["spectral_bwd_b20_c32_128x128_m16"] = run_backward(max(10, args.steps // 2), warmup, device,
-                                                                  world, rank)
+        if "irr" in wanted:
+            for wname in IRREGULAR_WORKLOADS:
+                r = run_spectral(wname, max(10, args.steps // 2), warmup, device, world, rank, with_e2e=False,
+                                 with_breakdown=True, sampler_gpu=None)
+                extras[wname] = {"ms_per_step": r["ms_per_step"], "samples_per_s": r["samples_per_s"],
+                                 "ms_per_step_eager": r["ms_per_step_eager"],
+                                 "roofline_fused_path_frac": r["roofline_fused_path"]["frac"],
+                                 "launches_per_step": r["launches_per_step"], "cuda_graph": True,
+                                 "accuracy": r.get("accuracy")}
+                if "roofline" in r:
+                    extras[wname].update(dominant_kernel=r["roofline"]["kernel"],
+                                         dominant_kernel_frac=r["roofline"]["frac"],
+                                         kernels_ms={k: v["ms"] for k, v in r["kernels"].items()})
+        if "c3s" in wanted:
+            extras["c3_strong_" + STRONG_WORKLOAD] = run_strong(STRONG_WORKLOAD, max(10, args.steps // 2), warmup,
+                                                                device, world, rank)
+        if "fno" in wanted:
+            extras["fno_ns_b20_w32_64x64_m12_l4"] = run_fno(max(10, args.steps // 2), warmup, device, world, rank)
+        if "bwd" in wanted:
+            extras["spectral_bwd_b20_c32_128x128_m16"] = run_backward(max(10, args.steps // 2), warmup, device,
+                                                                      world, rank)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.workload)
@@ -531,6 +704,7 @@ def ours(args) -> None:
                        "launch": "CUDA graphs of whole rotations over the buffer sets (three kernels per forward)"},
             "roofline": res.get("roofline"), "roofline_fused_path": res["roofline_fused_path"],
             "kernels": res.get("kernels"), "e2e": res.get("e2e"), "cpu_baseline": cpu,
+            "accuracy": res.get("accuracy"),
             "clocks": res["clocks"], "gpu_launches": res["launches_per_step"] * args.steps,
             "workloads": extras,
         }

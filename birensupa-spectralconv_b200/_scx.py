@@ -55,6 +55,8 @@ _SIGNATURES = {
     "scx_watchdog": ([_i], _i),
     "scx_spectral_mul": ([_p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
     "scx_spectral_mul_dual": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p], _i),
+    "scx_spectral_mul_bwd_workspace_size": ([_i, _i, _i, _i, _i], _sz),
+    "scx_spectral_mul_bwd": ([_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _sz, _p], _i),
     "scx_rfft2_corners": ([_p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
     "scx_irfft2_corners": ([_p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
     "scx_rfft2": ([_p, _p, _i, _i, _i, _i, _p], _i),
@@ -69,6 +71,11 @@ _SIGNATURES = {
     "scx_spectral_conv2d_bwd_workspace_size": ([_i, _i, _i, _i, _i, _i, _i], _sz),
     "scx_spectral_conv2d_bwd": ([_p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _p, _sz, _p], _i),
     "scx_spectral_conv2d_fwd_host": ([_p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _i, _p, _p, _p, _sz, _i, _p], _i),
+    "scx_dft_variants": ([_i, _i, _i, _i], _i),
+    "scx_set_dft_variant": ([_i, _i, _i, _i, _i], _i),
+    "scx_set_mix_variant": ([_i, _i, _i, _i, _i, _i], _i),
+    "scx_get_variant": ([_i, _i, _i, _i, _i, _i], _i),
+    "scx_clear_variants": ([], None),
     "scx_fno2d_workspace_size": ([ctypes.POINTER(FnoConfig)], _sz),
     "scx_fno2d_fwd": ([ctypes.POINTER(FnoConfig), ctypes.POINTER(FnoParams), _p, _p, _p, _sz, _p], _i),
 }

@@ -50,23 +50,14 @@ namespace scx {
 cudaError_t dft_fwd(const float* x, float2* out1, float2* out2, long long out_plane_stride, int out_row_stride,
                     int P, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream, float* scratch,
                     size_t scratch_bytes) {
-    if (!ffma_forced()) {
-        if (tc_fwd_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+    const int v = dft_variant(H, W, m1, m2);
+    if (!ffma_forced() && v != kDftFfma) {
+        if (v != kDftFolded && tc_fwd_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
             return launch_dft_fwd_tc(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, stream);
-        if (scratch != nullptr && tc_split_supported(H, W, m1, m2) && scratch_bytes >= split_scratch_bytes(P, H, W) &&
-            ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scratch)) & 15) == 0) {
-            // fold each plane into four half-size parity sub-planes, then one tensor-core
-            // forward per parity class writing its rows/columns of the two corners
-            const int Hs = H / 2, Ws = W / 2;
-            cudaError_t e = launch_fold(x, scratch, P, Hs, Ws, stream);
-            for (int q = 0; q < 4 && e == cudaSuccess; ++q) {
-                const TcSub sub{H, W, q >> 1, q & 1, m1, m2};
-                const long long off = static_cast<long long>(sub.a) * out_row_stride + sub.b;
-                e = launch_dft_fwd_tc(scratch + static_cast<size_t>(q) * P * Hs * Ws, out1 + off, out2 + off,
-                                      out_plane_stride, 2 * out_row_stride, P, Hs, Ws, m1 / 2, m2 / 2, stream, &sub);
-            }
-            return e;
-        }
+        if (tc_split_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(x) & 15) == 0)
+            // the four parity sub-problems of every plane in one launch, folded in the kernel
+            return launch_dft_fwd_tc_folded(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2,
+                                            stream);
     }
     return launch_dft_fwd(x, out1, out2, out_plane_stride, out_row_stride, P, H, W, m1, m2, tw, stream);
 }
@@ -74,9 +65,13 @@ cudaError_t dft_fwd(const float* x, float2* out1, float2* out2, long long out_pl
 cudaError_t dft_inv(const float2* in1, const float2* in2, long long in_plane_stride, int in_row_stride, float* y,
                     int Q, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream, float* scratch,
                     size_t scratch_bytes) {
-    if (!ffma_forced()) {
-        if (tc_inv_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(y) & 3) == 0)
+    const int v = dft_variant(H, W, m1, m2);
+    if (!ffma_forced() && v != kDftFfma) {
+        if (v != kDftFolded && tc_inv_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(y) & 3) == 0)
             return launch_dft_inv_tc(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, stream);
+        if (v != kDftFolded && tc_quad_supported(H, W, m1, m2) && (reinterpret_cast<uintptr_t>(y) & 3) == 0)
+            // four output quadrants per plane, straight from the corners (no fold, no scratch)
+            return launch_dft_inv_tc_quad(in1, in2, in_plane_stride, in_row_stride, y, Q, H, W, m1, m2, stream);
         if (scratch != nullptr && tc_split_supported(H, W, m1, m2) && scratch_bytes >= split_scratch_bytes(Q, H, W) &&
             ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(scratch)) & 15) == 0) {
             // one tensor-core inverse per parity class of the spectrum into half-size

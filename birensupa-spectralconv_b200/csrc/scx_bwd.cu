@@ -175,3 +175,79 @@ extern "C" int scx_spectral_conv2d_bwd(const float* grad_y, const float* x_corne
     }
     return e;
 }
+
+// ---- backward of the single-corner mixing alone (SpectralMulFunction.backward,
+// spectral_conv/spectral_conv_ops.py:272-278):
+//   grad_x[b][i][k] = sum_o grad_y[b][o][k] conj(w[i][o][k])   = mix(grad_y, W^H)
+//   grad_w[i][o][k] = sum_b conj(x[b][i][k]) grad_y[b][o][k]   = mix(X^H, grad_y)
+// with W^H = [Cout][Cin] and X^H = [Cin][B] per mode (conj_transpose_kernel, one corner).
+
+namespace {
+
+struct MulBwdLayout {
+    size_t wh, xh, total;
+};
+
+MulBwdLayout mul_bwd_layout(int B, int Cin, int Cout, int m1, int m2) {
+    const size_t NM = static_cast<size_t>(m1) * m2;
+    MulBwdLayout L;
+    L.wh = a256(static_cast<size_t>(Cout) * Cin * NM * sizeof(float2));
+    L.xh = a256(static_cast<size_t>(Cin) * B * NM * sizeof(float2));
+    L.total = L.wh + L.xh;
+    return L;
+}
+
+bool mul_bwd_valid(int B, int Cin, int Cout, int m1, int m2) {
+    if (B <= 0 || Cin <= 0 || Cout <= 0 || m1 <= 0 || m2 <= 0) return false;
+    const long long NM = static_cast<long long>(m1) * m2, lim = (1LL << 31) - 1;
+    return NM * B * Cin * 2 <= lim && NM * B * Cout * 2 <= lim && NM * Cin * Cout * 2 <= lim;
+}
+
+}  // namespace
+
+extern "C" size_t scx_spectral_mul_bwd_workspace_size(int batch_size, int channels_in, int channels_out, int modes1,
+                                                      int modes2) {
+    if (!mul_bwd_valid(batch_size, channels_in, channels_out, modes1, modes2)) return 0;
+    return mul_bwd_layout(batch_size, channels_in, channels_out, modes1, modes2).total;
+}
+
+extern "C" int scx_spectral_mul_bwd(const float* x_freq, const float* weights, const float* grad_y, float* grad_x,
+                                    float* grad_w, int batch_size, int channels_in, int channels_out, int modes1,
+                                    int modes2, void* workspace, size_t workspace_bytes, scx_stream_t stream) {
+    if (!grad_y || !workspace || (!grad_x && !grad_w)) return cudaErrorInvalidValue;
+    if ((grad_x && !weights) || (grad_w && !x_freq)) return cudaErrorInvalidValue;
+    const size_t need = scx_spectral_mul_bwd_workspace_size(batch_size, channels_in, channels_out, modes1, modes2);
+    if (need == 0 || workspace_bytes < need) return cudaErrorInvalidValue;
+    auto misaligned = [](const void* p, uintptr_t a) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) % a) != 0; };
+    if (misaligned(x_freq, 8) || misaligned(weights, 8) || misaligned(grad_y, 8) || misaligned(grad_x, 8) ||
+        misaligned(grad_w, 8) || misaligned(workspace, 256))
+        return cudaErrorInvalidValue;
+    const int B = batch_size, Cin = channels_in, Cout = channels_out, NM = modes1 * modes2;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const MulBwdLayout L = mul_bwd_layout(B, Cin, Cout, modes1, modes2);
+    unsigned char* base = static_cast<unsigned char*>(workspace);
+    float2* WH = reinterpret_cast<float2*>(base);
+    float2* XH = reinterpret_cast<float2*>(base + L.wh);
+    const float2* G = reinterpret_cast<const float2*>(grad_y);
+    cudaError_t e = cudaSuccess;
+    if (grad_x) {
+        const float2* Wc = reinterpret_cast<const float2*>(weights);
+        conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(Cin) * Cout * NM), 1), kThreads, 0, s>>>(
+            Wc, nullptr, WH, nullptr, Cin, Cout, NM, 0, modes2, 2, 1.f);  // one corner: grid.y = 1
+        e = cudaGetLastError();
+        if (e == cudaSuccess)
+            e = scx::launch_mix(G, nullptr, WH, nullptr, reinterpret_cast<float2*>(grad_x), nullptr, 1, B, Cout, Cin,
+                                NM, s);
+        if (e != cudaSuccess) return e;
+    }
+    if (grad_w) {
+        const float2* Xc = reinterpret_cast<const float2*>(x_freq);
+        conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(B) * Cin * NM), 1), kThreads, 0, s>>>(
+            Xc, nullptr, XH, nullptr, B, Cin, NM, 0, modes2, 2, 1.f);
+        e = cudaGetLastError();
+        if (e == cudaSuccess)
+            e = scx::launch_mix(XH, nullptr, G, nullptr, reinterpret_cast<float2*>(grad_w), nullptr, 1, Cin, B, Cout,
+                                NM, s);
+    }
+    return e;
+}

@@ -73,6 +73,10 @@ struct FwdArgs {
     const uint4* tab;  // [F_hi; F_lo] then [TW_hi; TW_lo], both K-major SW128
     uint32_t tab_bytes;
     int* watchdog;
+    // folded launches (x holds the full 2H x 2W planes): the table of parity q = 2a + b and the
+    // offset of its first output element (a rows, b columns) within out1 / out2
+    const uint4* tabq[4];
+    long long qoff[4];
 };
 
 struct FwdBars {
@@ -82,14 +86,20 @@ struct FwdBars {
     uint64_t drain[3];
 };
 
-template <int H, int W, int R2>
+// FOLD: the kernel reads full planes of 2H x 2W samples and computes the parity sub-planes
+// (the H x W sub-problems of TcSub) in its converters; a ring chunk then holds CHR rows of the
+// upper half and the same CHR rows of the lower half of each plane, full width.
+template <int H, int W, int R2, bool FOLD>
 struct FwdCfg {
     static constexpr int G1 = 128 / W;  // planes per column tile (TMEM lanes = (plane, w))
     static constexpr int CT = 2 / G1;   // column tiles per 2-plane tile
     static constexpr int N1 = 2 * R2;   // S1 columns per TW part (cos block | -sin block)
-    static constexpr int CPC = H / kChunkRows;  // ring chunks per column tile
-    static constexpr uint32_t PLANE_CHUNK = static_cast<uint32_t>(kChunkRows) * W * 4u;
-    static constexpr uint32_t SLOT = PLANE_CHUNK * G1;  // 16 KB
+    static constexpr int CHR = FOLD ? 16 : kChunkRows;  // (sub-)plane rows per ring chunk
+    static constexpr int RPW = CHR / 2;                  // rows per converter warp per chunk
+    static constexpr int CPC = H / CHR;                  // ring chunks per column tile
+    static constexpr uint32_t HALF_CHUNK = static_cast<uint32_t>(CHR) * (FOLD ? 2 * W : W) * 4u;
+    static constexpr uint32_t PLANE_CHUNK = FOLD ? 2u * HALF_CHUNK : HALF_CHUNK;
+    static constexpr uint32_t SLOT = PLANE_CHUNK * G1;  // 16 KB (32 KB folded)
     static constexpr uint32_t CSB = 128u * W * 2u;      // one CS operand (hi or lo), MN-major
     static constexpr uint32_t OFF_FB = 2u * CSB;        // CS hi | CS lo
     static constexpr uint32_t FB_BYTES = static_cast<uint32_t>(kFRows) * H * 2u;
@@ -112,9 +122,9 @@ struct FwdCfg {
     static_assert(COLS <= 512, "TMEM budget");
 };
 
-template <int H, int W, int R2>
+template <int H, int W, int R2, bool FOLD>
 __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a) {
-    using C = FwdCfg<H, W, R2>;
+    using C = FwdCfg<H, W, R2, FOLD>;
     constexpr int N1 = C::N1;
     extern __shared__ uint8_t smem_raw[];
     __shared__ FwdBars bars;
@@ -122,10 +132,15 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
     uint8_t* base = tc::align1024(smem_raw);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    // this CTA's planes [p0, p1): contiguous, sizes differ by at most one
+    // this CTA's planes [p0, p1): contiguous, sizes differ by at most one.  Folded: CTAs come in
+    // groups of four, one per parity q = 2a + b, that take the same planes in the same order,
+    // so a plane is read from HBM about once and by the other three from L2.
     const int P = a.P;
-    const int p0 = static_cast<int>(static_cast<long long>(blockIdx.x) * P / gridDim.x);
-    const int p1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * P / gridDim.x);
+    const int ngrp = FOLD ? static_cast<int>(gridDim.x) / 4 : static_cast<int>(gridDim.x);
+    const int grp = FOLD ? static_cast<int>(blockIdx.x) / 4 : static_cast<int>(blockIdx.x);
+    const int qpar = FOLD ? static_cast<int>(blockIdx.x) % 4 : 0;
+    const int p0 = static_cast<int>(static_cast<long long>(grp) * P / ngrp);
+    const int p1 = static_cast<int>(static_cast<long long>(grp + 1) * P / ngrp);
     const int NC = (p1 - p0 + C::G1 - 1) / C::G1;  // column tiles
     const int NT = (NC + C::CT - 1) / C::CT;        // 2-plane tiles
     const int NK = NC * C::CPC;                     // ring chunks
@@ -136,10 +151,18 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         const int pa = p0 + c * C::G1, np = min(C::G1, p1 - pa);
         uint8_t* ring = base + C::OFF_RING;
         tc::mbar_arrive_expect_tx(&bars.full[slot], static_cast<uint32_t>(np) * C::PLANE_CHUNK);
-        for (int g = 0; g < np; ++g)
-            tc::bulk_g2s(ring + static_cast<uint32_t>(slot) * C::SLOT + static_cast<uint32_t>(g) * C::PLANE_CHUNK,
-                         a.x + (static_cast<size_t>(pa + g) * H + ch * kChunkRows) * W, C::PLANE_CHUNK,
-                         &bars.full[slot]);
+        for (int g = 0; g < np; ++g) {
+            uint8_t* dst = ring + static_cast<uint32_t>(slot) * C::SLOT + static_cast<uint32_t>(g) * C::PLANE_CHUNK;
+            if (FOLD) {  // rows [CHR ch, CHR ch + CHR) of both halves of the 2H x 2W plane
+                const float* src = a.x + (static_cast<size_t>(pa + g) * (2 * H) + ch * C::CHR) * (2 * W);
+                tc::bulk_g2s(dst, src, C::HALF_CHUNK, &bars.full[slot]);
+                tc::bulk_g2s(dst + C::HALF_CHUNK, src + static_cast<size_t>(H) * (2 * W), C::HALF_CHUNK,
+                             &bars.full[slot]);
+            } else {
+                tc::bulk_g2s(dst, a.x + (static_cast<size_t>(pa + g) * H + ch * C::CHR) * W, C::PLANE_CHUNK,
+                             &bars.full[slot]);
+            }
+        }
     };
     const int k_first = min(NK, C::NS);  // chunks issued before the setup barrier
 
@@ -165,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         for (int i = 0; i < 3; ++i) tc::mbar_init(&bars.drain[i], 1);
         tc::fence_async_smem();
         tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
-        tc::bulk_g2s(base + C::OFF_FB, a.tab, a.tab_bytes, &bars.tab);
+        tc::bulk_g2s(base + C::OFF_FB, FOLD ? a.tabq[qpar] : a.tab, a.tab_bytes, &bars.tab);
         // x may be written by the previous kernel in the stream; the ring starts empty, so the
         // first NS chunks need no slot wait
         tc::grid_dep_wait();
@@ -178,9 +201,12 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
 
     if (warp < kConvWarps) {
         // ------------------------------------------------------------ converters
-        // Warp (q, hf) owns TMEM lanes 32q.. and rows [16 hf, 16 hf + 16) of every ring chunk:
+        // Warp (q, hf) owns TMEM lanes 32q.. and rows [RPW hf, RPW hf + RPW) of every ring chunk:
         // it reads its column of those rows from shared memory, splits them into bf16 hi/lo
-        // pairs and stores 8 packed columns of each into the A operand.
+        // pairs and stores RPW / 2 packed columns of each into the A operand.  Folded, each
+        // value is the parity-q combination of the four quadrant samples, computed with the
+        // additions and subtractions of the fold kernel (scx_fold.cu) in the same order
+        // (a signed sum by fmaf with +-1 rounds exactly as the add or subtract does).
         const int q = warp & 3, hf = warp >> 2;
         const int l = q * 32 + lane, g = l / W, w = l % W;
         const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
@@ -189,20 +215,32 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
         for (int c = 0; c < NC && ok; ++c) {
             const bool live = p0 + c * C::G1 + g < p1;  // warp-uniform
             // read and split the whole column tile while the previous tile's MMAs run
-            uint32_t hi[C::CPC][8], lo[C::CPC][8];
+            uint32_t hi[C::CPC][C::RPW / 2], lo[C::CPC][C::RPW / 2];
 #pragma unroll
             for (int ch = 0; ch < C::CPC; ++ch) {
                 const int k = c * C::CPC + ch, slot = k % C::NS, use = k / C::NS;
                 if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.full[slot], use & 1));
                 if (ok) {
-                    const float* src = reinterpret_cast<const float*>(ring + static_cast<uint32_t>(slot) * C::SLOT +
-                                                                      static_cast<uint32_t>(g) * C::PLANE_CHUNK) +
-                                       (16 * hf) * W + w;
-                    float v[16];
+                    const uint8_t* pc = ring + static_cast<uint32_t>(slot) * C::SLOT + static_cast<uint32_t>(g) * C::PLANE_CHUNK;
+                    float v[C::RPW];
+                    if constexpr (FOLD) {
+                        constexpr int WF = 2 * W;  // full-plane row length
+                        const float sa = (qpar & 2) ? -1.f : 1.f, sb = (qpar & 1) ? -1.f : 1.f;
+                        const float* top = reinterpret_cast<const float*>(pc) + (C::RPW * hf) * WF + w;
+                        const float* bot = reinterpret_cast<const float*>(pc + C::HALF_CHUNK) + (C::RPW * hf) * WF + w;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = live ? src[j * W] : 0.f;
+                        for (int j = 0; j < C::RPW; ++j) {
+                            const float u = fmaf(sb, top[j * WF + W], top[j * WF]);
+                            const float t = fmaf(sb, bot[j * WF + W], bot[j * WF]);
+                            v[j] = live ? fmaf(sa, t, u) : 0.f;
+                        }
+                    } else {
+                        const float* src = reinterpret_cast<const float*>(pc) + (C::RPW * hf) * W + w;
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) tc::split_pair(v[2 * j], v[2 * j + 1], hi[ch][j], lo[ch][j]);
+                        for (int j = 0; j < C::RPW; ++j) v[j] = live ? src[j * W] : 0.f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < C::RPW / 2; ++j) tc::split_pair(v[2 * j], v[2 * j + 1], hi[ch][j], lo[ch][j]);
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&bars.empty[slot]);
                 }
@@ -213,9 +251,14 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
             tc::fence_after_sync();
 #pragma unroll
             for (int ch = 0; ch < C::CPC; ++ch) {
-                const uint32_t col = tmem + lane_addr + static_cast<uint32_t>((ch * kChunkRows + 16 * hf) / 2);
-                tc::tmem_st8(col, hi[ch]);
-                tc::tmem_st8(col + H / 2, lo[ch]);
+                const uint32_t col = tmem + lane_addr + static_cast<uint32_t>((ch * C::CHR + C::RPW * hf) / 2);
+                if constexpr (C::RPW == 16) {
+                    tc::tmem_st8(col, hi[ch]);
+                    tc::tmem_st8(col + H / 2, lo[ch]);
+                } else {
+                    tc::tmem_st4(col, hi[ch]);
+                    tc::tmem_st4(col + H / 2, lo[ch]);
+                }
             }
             tc::tmem_wait_st();
             tc::fence_before_sync();
@@ -306,9 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1) dft_fwd_tc_kernel(const FwdArgs a
             const int p = p0 + 2 * i + pit;
             const bool valid = s < S && p < p1;
             float2* dst = nullptr;
+            const long long qo = FOLD ? a.qoff[qpar] : 0;
             if (valid)
-                dst = (s < m1 ? a.out1 + static_cast<long long>(p) * a.ops + static_cast<long long>(s) * a.ors
-                              : a.out2 + static_cast<long long>(p) * a.ops + static_cast<long long>(s - m1) * a.ors);
+                dst = (s < m1 ? a.out1 + qo + static_cast<long long>(p) * a.ops + static_cast<long long>(s) * a.ors
+                              : a.out2 + qo + static_cast<long long>(p) * a.ops + static_cast<long long>(s - m1) * a.ors);
 #pragma unroll
             for (int k = 0; k < HQ; ++k) {
                 const float uc0 = uc[k], us0 = us[k];
@@ -475,33 +519,49 @@ cudaError_t get_fwd_table(int H, int W, int m1, int m2, const TcSub* sub, const 
     return cudaSuccess;
 }
 
-template <int H, int W, int R2>
+template <int H, int W, int R2, bool FOLD>
 cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
-    using C = FwdCfg<H, W, R2>;
+    using C = FwdCfg<H, W, R2, FOLD>;
     static_assert(C::SMEM <= 227u * 1024u - 512u, "shared memory budget");
     if (a.tab_bytes != C::FB_BYTES + C::TW_BYTES) return cudaErrorInvalidValue;
-    auto kernel = dft_fwd_tc_kernel<H, W, R2>;
+    auto kernel = dft_fwd_tc_kernel<H, W, R2, FOLD>;
     int per_sm = 1;
     cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), C::SMEM, kThreads, &per_sm);
     if (err != cudaSuccess) return err;
-    // Every CTA gets the same number of planes, ceil(P / SMs): 640 planes run as 128 CTAs of 5
-    // rather than 148 CTAs of 4 or 5.  The busiest CTA streams as many planes either way, but
-    // with all ranges equal no CTA finishes its last plane alone after the others (15.7 ->
-    // 14.8 us at B20 C32 128x128).
-    const int per_cta = (a.P + num_sms() - 1) / num_sms();
-    const int grid = std::max(1, (a.P + per_cta - 1) / per_cta);
+    int grid;
+    if (FOLD) {
+        // groups of four CTAs (one per parity), as many groups as fit one per SM, at most one
+        // plane-column tile each
+        const int groups = std::max(1, std::min(num_sms() / 4, (a.P + C::G1 - 1) / C::G1));
+        grid = 4 * groups;
+    } else {
+        // Every CTA gets the same number of planes, ceil(P / SMs): 640 planes run as 128 CTAs of 5
+        // rather than 148 CTAs of 4 or 5.  The busiest CTA streams as many planes either way, but
+        // with all ranges equal no CTA finishes its last plane alone after the others (15.7 ->
+        // 14.8 us at B20 C32 128x128).
+        const int per_cta = (a.P + num_sms() - 1) / num_sms();
+        grid = std::max(1, (a.P + per_cta - 1) / per_cta);
+    }
     return launch_chained(kernel, dim3(grid), dim3(kThreads), C::SMEM, stream, a);
 }
 
-template <int H, int W>
+template <int H, int W, bool FOLD>
 cudaError_t run_fwd_r2(const FwdArgs& a, int R2, cudaStream_t stream) {
     switch (R2) {
-        case 8: return run_fwd<H, W, 8>(a, stream);
-        case 16: return run_fwd<H, W, 16>(a, stream);
-        case 24: return run_fwd<H, W, 24>(a, stream);
-        case 32: return run_fwd<H, W, 32>(a, stream);
+        case 8: return run_fwd<H, W, 8, FOLD>(a, stream);
+        case 16: return run_fwd<H, W, 16, FOLD>(a, stream);
+        case 24: return run_fwd<H, W, 24, FOLD>(a, stream);
+        case 32: return run_fwd<H, W, 32, FOLD>(a, stream);
         default: return cudaErrorInvalidValue;
     }
+}
+
+template <bool FOLD>
+cudaError_t run_fwd_shape(const FwdArgs& a, int H, int W, int R2, cudaStream_t stream) {
+    if (H == 64 && W == 64) return run_fwd_r2<64, 64, FOLD>(a, R2, stream);
+    if (H == 64 && W == 128) return run_fwd_r2<64, 128, FOLD>(a, R2, stream);
+    if (H == 128 && W == 64) return run_fwd_r2<128, 64, FOLD>(a, R2, stream);
+    return run_fwd_r2<128, 128, FOLD>(a, R2, stream);
 }
 
 }  // namespace
@@ -521,7 +581,7 @@ cudaError_t launch_dft_fwd_tc(const float* x, float2* out1, float2* out2, long l
     int* wd = nullptr;
     e = device_watchdog(&wd);
     if (e != cudaSuccess) return e;
-    FwdArgs a;
+    FwdArgs a = {};
     a.x = x;
     a.out1 = out1;
     a.out2 = out2;
@@ -534,11 +594,37 @@ cudaError_t launch_dft_fwd_tc(const float* x, float2* out1, float2* out2, long l
     a.tab = t->data;
     a.tab_bytes = t->bytes;
     a.watchdog = wd;
-    const int R2 = host::round_up(m2, 8);
-    if (H == 64 && W == 64) return run_fwd_r2<64, 64>(a, R2, stream);
-    if (H == 64 && W == 128) return run_fwd_r2<64, 128>(a, R2, stream);
-    if (H == 128 && W == 64) return run_fwd_r2<128, 64>(a, R2, stream);
-    return run_fwd_r2<128, 128>(a, R2, stream);
+    return run_fwd_shape<false>(a, H, W, host::round_up(m2, 8), stream);
+}
+
+cudaError_t launch_dft_fwd_tc_folded(const float* x, float2* out1, float2* out2, long long ops, int ors, int P,
+                                     int Hf, int Wf, int m1f, int m2f, cudaStream_t stream) {
+    if (!tc_split_supported(Hf, Wf, m1f, m2f) || P <= 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+        return cudaErrorInvalidValue;
+    const int H = Hf / 2, W = Wf / 2, m1 = m1f / 2, m2 = m2f / 2;
+    FwdArgs a = {};
+    for (int q = 0; q < 4; ++q) {
+        const TcSub sub{Hf, Wf, q >> 1, q & 1, m1f, m2f};
+        const FwdTable* t = nullptr;
+        cudaError_t e = get_fwd_table(H, W, m1, m2, &sub, &t);
+        if (e != cudaSuccess) return e;
+        a.tabq[q] = t->data;
+        a.tab_bytes = t->bytes;
+        a.qoff[q] = static_cast<long long>(sub.a) * ors + sub.b;
+    }
+    cudaError_t e = device_watchdog(&a.watchdog);
+    if (e != cudaSuccess) return e;
+    a.x = x;
+    a.out1 = out1;
+    a.out2 = out2;
+    a.ops = ops;
+    a.ors = 2 * ors;
+    a.oks = 2;
+    a.P = P;
+    a.m1 = m1;
+    a.m2 = m2;
+    a.tab = a.tabq[0];
+    return run_fwd_shape<true>(a, H, W, host::round_up(m2, 8), stream);
 }
 
 }  // namespace scx

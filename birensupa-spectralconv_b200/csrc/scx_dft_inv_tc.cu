@@ -53,8 +53,6 @@ constexpr int kE5Warp0 = kE4Warp0 + kE4Warps;    // 8
 constexpr int kMmaWarp = kE5Warp0 + kE5Warps;    // 16 (S4), 17 (S5)
 constexpr int kThreads = (kMmaWarp + 2) * 32;    // 576
 constexpr int kBarE5 = 3;                        // named barrier of the E5 warps
-constexpr int kKg = 64;                          // S4 K: (cos|sin) x 32 slots
-
 struct InvArgs {
     const float2* in1;
     const float2* in2;
@@ -62,18 +60,31 @@ struct InvArgs {
     int irs;        // input row stride (float2 units)
     int iks;        // input ky stride (float2 units): 2 for a parity sub-problem of a folded plane
     float* y;
+    long long yps;  // output plane stride (floats)
+    int yrs;        // output row stride (floats)
     int Q, m1, m2;
     const uint4* tab;  // G (hi, lo) then E (hi, lo)
     uint32_t tab_bytes;
     int* watchdog;
+    // quadrant launches: the table and the offset of the first output element of quadrant
+    // (alpha, beta) = (quad >> 1, quad & 1)
+    const uint4* tabq[4];
+    long long yoff[4];
 };
 
 struct InvBars {
     uint64_t yFull[2], yEmpty[2], d4Full, d4Empty, zFull[4], zEmpty[4], d5Full[2], d5Empty[2], drain[2], tab;
 };
 
-template <int H, int W, int N1P>
+// QUAD: one CTA computes one H x W quadrant of a 2H x 2W output plane directly from the full
+// corners (up to 64 spectrum rows, so S4's K is (cos|sin) x 64 slots), with the quadrant's
+// offset in its twiddle tables; CTAs come in groups of four, one per quadrant.  Yr is then
+// single-buffered to fit shared memory.
+template <int H, int W, int N1P, bool QUAD>
 struct InvCfg {
+    static constexpr int KSL = QUAD ? 64 : 32;     // spectrum-row slots per cos / sin block of S4's K
+    static constexpr int KG = 2 * KSL;             // S4 K
+    static constexpr int NYB = QUAD ? 1 : 2;       // Yr buffers
     static constexpr int R2P = N1P / 2;            // ky rows per re/im block
     static constexpr int G4 = 128 / N1P;           // planes per S4 group
     static constexpr int G5 = 128 / W;             // planes per S5 chain
@@ -81,13 +92,13 @@ struct InvCfg {
     static constexpr int WPC = G5 * N1P / 32;      // D4 warps per chain (per half of h)
     static constexpr int K5 = G5 * N1P;            // S5 K (block-diagonal for W = 64)
     static constexpr int K5P = (K5 + 63) / 64 * 64;                      // K-major rows span 64 K
-    static constexpr uint32_t YRB = 128u * kKg * 2u;                     // one Yr part, MN-major
-    static constexpr uint32_t GB = static_cast<uint32_t>(H) * kKg * 2u;  // one G part, K-major
+    static constexpr uint32_t YRB = 128u * KG * 2u;                      // one Yr part, MN-major
+    static constexpr uint32_t GB = static_cast<uint32_t>(H) * KG * 2u;   // one G part, K-major
     static constexpr uint32_t EB = 128u * K5P * 2u;                      // one E part, K-major
     static constexpr uint32_t ZB = static_cast<uint32_t>(H) * K5 * 2u;   // one Z part, MN-major
     static constexpr uint32_t ZSBO = static_cast<uint32_t>(H / 64) * 1024u;  // Z K-group stride
-    static constexpr uint32_t OFF_YR = 0;                        // 2 buffers x (hi, lo)
-    static constexpr uint32_t OFF_G = OFF_YR + 4u * YRB;         // G hi, G lo
+    static constexpr uint32_t OFF_YR = 0;                        // NYB buffers x (hi, lo)
+    static constexpr uint32_t OFF_G = OFF_YR + 2u * NYB * YRB;   // G hi, G lo
     static constexpr uint32_t OFF_E = OFF_G + 2u * GB;           // E hi, E lo
     static constexpr uint32_t OFF_Z = OFF_E + 2u * EB;           // NZ chains x (hi, lo)
     static constexpr uint32_t SMEM = OFF_Z + 2u * NZ * ZB + 1024u;
@@ -97,9 +108,9 @@ struct InvCfg {
     static constexpr uint32_t TMEM_COLS = COLS <= 256 ? 256u : 512u;
 };
 
-template <int H, int W, int N1P>
+template <int H, int W, int N1P, bool QUAD>
 __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a) {
-    using C = InvCfg<H, W, N1P>;
+    using C = InvCfg<H, W, N1P, QUAD>;
     extern __shared__ uint8_t smem_raw[];
     __shared__ InvBars bars;
     __shared__ uint32_t tmem_base;
@@ -107,16 +118,19 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     const int Q = a.Q;
-    const int q0 = static_cast<int>(static_cast<long long>(blockIdx.x) * Q / gridDim.x);
-    const int q1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * Q / gridDim.x);
+    const int ngrp = QUAD ? static_cast<int>(gridDim.x) / 4 : static_cast<int>(gridDim.x);
+    const int grp = QUAD ? static_cast<int>(blockIdx.x) / 4 : static_cast<int>(blockIdx.x);
+    const int quad = QUAD ? static_cast<int>(blockIdx.x) % 4 : 0;
+    const int q0 = static_cast<int>(static_cast<long long>(grp) * Q / ngrp);
+    const int q1 = static_cast<int>(static_cast<long long>(grp + 1) * Q / ngrp);
     const int NG = (q1 - q0 + C::G4 - 1) / C::G4;  // S4 groups
     // S5 chains of group t holding a live plane (fewer than NZ only in a partial last group)
     auto nz_live = [&](int t) { return min(C::NZ, (q1 - q0 - t * C::G4 + C::G5 - 1) / C::G5); };
 
     // loaders: the spectra of one group, 8 consecutive ky per unit, in registers
     constexpr int kKB = C::R2P / 8;                                   // ky blocks per slot
-    constexpr int kUnitsPT = C::G4 * 32 * kKB / (kLoadWarps * 32);    // units per loader thread
-    static_assert(C::G4 * 32 * kKB % (kLoadWarps * 32) == 0, "loader split");
+    constexpr int kUnitsPT = C::G4 * C::KSL * kKB / (kLoadWarps * 32);  // units per loader thread
+    static_assert(C::G4 * C::KSL * kKB % (kLoadWarps * 32) == 0, "loader split");
     float2 v[kUnitsPT][8];
     auto load_group = [&](int t) {
         const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
@@ -124,7 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
         for (int u = 0; u < kUnitsPT; ++u) {
             const int e = tid + u * kLoadWarps * 32;
             const int kb = e % kKB, rest = e / kKB;
-            const int ss = rest % 32, p = rest / 32;
+            const int ss = rest % C::KSL, p = rest / C::KSL;
             const int q = q0 + t * C::G4 + p;
             const bool live = q < q1 && ss < S;
             const float2* src = ss < m1 ? a.in1 + static_cast<long long>(q) * a.ips + static_cast<long long>(ss) * a.irs
@@ -221,8 +235,8 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
         uint8_t* yr0 = base + C::OFF_YR;
         bool ok = true;
         for (int t = 0; t < NG && ok; ++t) {
-            const int yb = t & 1;
-            ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.yEmpty[yb], ((t >> 1) & 1) ^ 1));
+            const int yb = t % C::NYB;
+            ok = __all_sync(0xffffffffu, tc::mbar_wait_bounded(&bars.yEmpty[yb], ((t / C::NYB) & 1) ^ 1));
             if (!ok) break;
             uint8_t* yr_hi = yr0 + static_cast<uint32_t>(yb) * 2u * C::YRB;
             uint8_t* yr_lo = yr_hi + C::YRB;
@@ -230,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
             for (int u = 0; u < kUnitsPT; ++u) {
                 const int e = tid + u * kLoadWarps * 32;
                 const int kb = e % kKB, rest = e / kKB;
-                const int ss = rest % 32, p = rest / 32;
+                const int ss = rest % C::KSL, p = rest / C::KSL;
                 uint32_t re_hi[4], re_lo[4], im_hi[4], im_lo[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -246,9 +260,9 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
                     *reinterpret_cast<uint4*>(yr_lo + off) = make_uint4(lo[0] ^ neg, lo[1] ^ neg, lo[2] ^ neg, lo[3] ^ neg);
                 };
                 put(mre, ss, re_hi, re_lo, 0u);
-                put(mre, 32 + ss, im_hi, im_lo, 0x80008000u);  // -Y_im: bf16 sign bits
+                put(mre, C::KSL + ss, im_hi, im_lo, 0x80008000u);  // -Y_im: bf16 sign bits
                 put(mim, ss, im_hi, im_lo, 0u);
-                put(mim, 32 + ss, re_hi, re_lo, 0u);
+                put(mim, C::KSL + ss, re_hi, re_lo, 0u);
             }
             tc::fence_async_smem();
             __syncwarp();
@@ -283,7 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
                 }
                 tc::fence_after_sync();
                 const int qp = q0 + t * C::G4 + j * C::G5 + g;  // warp-uniform plane
-                float* dst = a.y + (static_cast<size_t>(qp) * H + sub * HH) * W + w;
+                float* dst = a.y + (QUAD ? a.yoff[quad] : 0) + static_cast<long long>(qp) * a.yps +
+                             static_cast<long long>(sub * HH) * a.yrs + w;
                 const uint32_t src = tmem + lane_addr + C::COL_D5 + static_cast<uint32_t>(b * H + sub * HH);
 #pragma unroll
                 for (int h0 = 0; h0 < HH; h0 += 32) {
@@ -292,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
                     tc::tmem_wait_ld();
                     if (qp < q1) {
 #pragma unroll
-                        for (int k = 0; k < 32; ++k) __stcs(dst + static_cast<size_t>(h0 + k) * W, v[k]);
+                        for (int k = 0; k < 32; ++k) __stcs(dst + static_cast<long long>(h0 + k) * a.yrs, v[k]);
                     }
                 }
                 tc::fence_before_sync();
@@ -307,16 +322,16 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
         const uint32_t sb = tc::smem_u32(base);
         if (role == 0) {
             tc::mbar_arrive_expect_tx(&bars.tab, a.tab_bytes);
-            tc::bulk_g2s(base + C::OFF_G, a.tab, a.tab_bytes, &bars.tab);
+            tc::bulk_g2s(base + C::OFF_G, QUAD ? a.tabq[quad] : a.tab, a.tab_bytes, &bars.tab);
         }
         bool ok = tc::mbar_wait_bounded(&bars.tab, 0);
         if (role == 0) {
-            // S4: parts (Yr_hi, G_hi), (Yr_hi, G_lo), (Yr_lo, G_hi), K = 64 each
+            // S4: parts (Yr_hi, G_hi), (Yr_hi, G_lo), (Yr_lo, G_hi), K = KG each
             constexpr uint32_t id4 = tc::idesc_bf16(128, H) | tc::kIdescAMajorMN;
             const uint64_t dG[2] = {tc::desc_sw128(sb + C::OFF_G), tc::desc_sw128(sb + C::OFF_G + C::GB)};
             for (int t = 0; t < NG && ok; ++t) {
-                const int yb = t & 1;
-                ok = tc::mbar_wait_bounded(&bars.yFull[yb], (t >> 1) & 1) &&
+                const int yb = t % C::NYB;
+                ok = tc::mbar_wait_bounded(&bars.yFull[yb], (t / C::NYB) & 1) &&
                      tc::mbar_wait_bounded(&bars.d4Empty, (t & 1) ^ 1);
                 if (!ok) break;
                 tc::fence_after_sync();
@@ -326,8 +341,10 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
                 for (int part = 0; part < 3; ++part) {
                     const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
 #pragma unroll
-                    for (int ks = 0; ks < kKg / 16; ++ks) {
-                        const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4, bo = (static_cast<uint32_t>(ks) * 32u) >> 4;
+                    for (int ks = 0; ks < C::KG / 16; ++ks) {
+                        // G is K-major with 64-element K blocks of H rows each
+                        const uint32_t ao = (static_cast<uint32_t>(ks) * 4096u) >> 4;
+                        const uint32_t bo = (static_cast<uint32_t>(ks >> 2) * H * 128u + (ks & 3) * 32u) >> 4;
                         tc::mma_bf16(tmem, dY[ap] + ao, dG[bp] + bo, id4, (part | ks) ? 1u : 0u);
                     }
                 }
@@ -406,6 +423,7 @@ cudaError_t get_inv_table(int H, int W, int m1, int m2, int N1P, const TcSub* su
         return cudaSuccess;
     }
     const int S = 2 * m1, R2P = N1P / 2, G5 = 128 / W, K5 = G5 * N1P;
+    constexpr int kKg = 64;  // S4 K of the direct kernel: (cos|sin) x 32 slots
     host::KMajor ghi(H, kKg), glo(H, kKg);
     const int Hp = sub ? sub->period_h : H, Wp = sub ? sub->period_w : W;
     for (int s = 0; s < S; ++s) {
@@ -459,21 +477,88 @@ cudaError_t get_inv_table(int H, int W, int m1, int m2, int N1P, const TcSub* su
     return cudaSuccess;
 }
 
-template <int H, int W, int N1P>
+// Quadrant tables for planes of Hf x Wf = 2H x 2W: G for the rows of quadrant alpha (all 2 m1
+// spectrum rows, cos block then sin block, KSL = 64 slots each) and E for the columns of
+// quadrant beta, the angles taken at the full-plane position (h + H alpha, w + W beta).
+cudaError_t get_inv_table_quad(int Hf, int Wf, int m1, int m2, int quad, const InvTable** out) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    const auto key = std::make_tuple(dev, Hf, Wf, m1, m2, -1 - quad);
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_tables.find(key);
+    if (it != g_tables.end()) {
+        *out = &it->second;
+        return cudaSuccess;
+    }
+    using C = InvCfg<128, 128, 64, true>;
+    const int H = Hf / 2, W = Wf / 2, alpha = quad >> 1, beta = quad & 1;
+    host::KMajor ghi(H, C::KG), glo(H, C::KG);
+    for (int s = 0; s < 2 * m1; ++s) {
+        const int kx = host::slot_row(s, Hf, m1);
+        if (s < m1 && kx >= Hf - m1) continue;  // corner-1 row that corner 2 overwrites
+        for (int h = 0; h < H; ++h) {
+            const double t = host::ang(kx, h + H * alpha, Hf);
+            uint16_t hi, lo;
+            host::bf16_split(std::cos(t), hi, lo);
+            ghi.set(h, s, hi);
+            glo.set(h, s, lo);
+            host::bf16_split(std::sin(t), hi, lo);
+            ghi.set(h, C::KSL + s, hi);
+            glo.set(h, C::KSL + s, lo);
+        }
+    }
+    host::KMajor ehi(128, C::K5), elo(128, C::K5);
+    const double inv_hw = 1.0 / (static_cast<double>(Hf) * static_cast<double>(Wf));
+    for (int w = 0; w < W; ++w)
+        for (int ky = 0; ky < m2; ++ky) {
+            const bool single = (ky == 0) || ((Wf % 2 == 0) && (ky == Wf / 2));
+            const double cw = (single ? 1.0 : 2.0) * inv_hw;
+            const double t = host::ang(ky, w + W * beta, Wf);
+            uint16_t hi, lo;
+            host::bf16_split(cw * std::cos(t), hi, lo);
+            ehi.set(w, ky, hi);
+            elo.set(w, ky, lo);
+            host::bf16_split(-cw * std::sin(t), hi, lo);
+            ehi.set(w, C::R2P + ky, hi);
+            elo.set(w, C::R2P + ky, lo);
+        }
+    std::vector<uint16_t> buf(ghi.data);
+    for (const auto* part : {&glo, &ehi, &elo}) buf.insert(buf.end(), part->data.begin(), part->data.end());
+    const size_t bytes = buf.size() * 2;
+    void* d = nullptr;
+    err = cudaMalloc(&d, bytes);
+    if (err != cudaSuccess) return err;
+    err = cudaMemcpy(d, buf.data(), bytes, cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        cudaFree(d);
+        return err;
+    }
+    InvTable t;
+    t.data = static_cast<const uint4*>(d);
+    t.bytes = static_cast<uint32_t>(bytes);
+    auto res = g_tables.emplace(key, t);
+    *out = &res.first->second;
+    return cudaSuccess;
+}
+
+template <int H, int W, int N1P, bool QUAD>
 cudaError_t run_inv(const InvArgs& a, cudaStream_t stream) {
-    using C = InvCfg<H, W, N1P>;
+    using C = InvCfg<H, W, N1P, QUAD>;
     if (a.tab_bytes != 2u * C::GB + 2u * C::EB) return cudaErrorInvalidValue;
-    auto kernel = dft_inv_tc_kernel<H, W, N1P>;
+    auto kernel = dft_inv_tc_kernel<H, W, N1P, QUAD>;
     int per_sm = 1;
     cudaError_t err = prepare_kernel(reinterpret_cast<const void*>(kernel), C::SMEM, kThreads, &per_sm);
     if (err != cudaSuccess) return err;
-    const int grid = std::max(1, std::min(a.Q, num_sms()));
+    // quadrants: groups of four CTAs, at most one per SM, at most one group per S4 group of planes
+    const int grid = QUAD ? 4 * std::max(1, std::min(num_sms() / 4, (a.Q + C::G4 - 1) / C::G4))
+                          : std::max(1, std::min(a.Q, num_sms()));
     return launch_chained(kernel, dim3(grid), dim3(kThreads), C::SMEM, stream, a);
 }
 
 template <int H, int W>
 cudaError_t run_inv_n(const InvArgs& a, int N1P, cudaStream_t stream) {
-    return N1P == 32 ? run_inv<H, W, 32>(a, stream) : run_inv<H, W, 64>(a, stream);
+    return N1P == 32 ? run_inv<H, W, 32, false>(a, stream) : run_inv<H, W, 64, false>(a, stream);
 }
 
 }  // namespace
@@ -494,13 +579,15 @@ cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long ip
     int* wd = nullptr;
     e = device_watchdog(&wd);
     if (e != cudaSuccess) return e;
-    InvArgs a;
+    InvArgs a = {};
     a.in1 = in1;
     a.in2 = in2;
     a.ips = ips;
     a.irs = irs;
     a.iks = sub ? 2 : 1;
     a.y = y;
+    a.yps = static_cast<long long>(H) * W;
+    a.yrs = W;
     a.Q = Q;
     a.m1 = m1;
     a.m2 = m2;
@@ -511,6 +598,40 @@ cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long ip
     if (H == 64 && W == 128) return run_inv_n<64, 128>(a, N1P, stream);
     if (H == 128 && W == 64) return run_inv_n<128, 64>(a, N1P, stream);
     return run_inv_n<128, 128>(a, N1P, stream);
+}
+
+bool tc_quad_supported(int H, int W, int m1, int m2) {
+    return H == 256 && W == 256 && m1 >= 1 && m1 <= 32 && m2 >= 1 && m2 <= 32;
+}
+
+cudaError_t launch_dft_inv_tc_quad(const float2* in1, const float2* in2, long long ips, int irs, float* y, int Q,
+                                   int H, int W, int m1, int m2, cudaStream_t stream) {
+    if (!tc_quad_supported(H, W, m1, m2) || Q <= 0 || (reinterpret_cast<uintptr_t>(y) & 3) != 0)
+        return cudaErrorInvalidValue;
+    InvArgs a = {};
+    for (int q = 0; q < 4; ++q) {
+        const InvTable* t = nullptr;
+        cudaError_t e = get_inv_table_quad(H, W, m1, m2, q, &t);
+        if (e != cudaSuccess) return e;
+        a.tabq[q] = t->data;
+        a.tab_bytes = t->bytes;
+        a.yoff[q] = static_cast<long long>((q >> 1) * (H / 2)) * W + (q & 1) * (W / 2);
+    }
+    cudaError_t e = device_watchdog(&a.watchdog);
+    if (e != cudaSuccess) return e;
+    a.in1 = in1;
+    a.in2 = in2;
+    a.ips = ips;
+    a.irs = irs;
+    a.iks = 1;
+    a.y = y;
+    a.yps = static_cast<long long>(H) * W;
+    a.yrs = W;
+    a.Q = Q;
+    a.m1 = m1;
+    a.m2 = m2;
+    a.tab = a.tabq[0];
+    return run_inv<128, 128, 64, true>(a, stream);
 }
 
 }  // namespace scx

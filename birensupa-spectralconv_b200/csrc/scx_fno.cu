@@ -479,14 +479,15 @@ __global__ void __launch_bounds__(kThreads, 3) fno_skip_norm_kernel(const float*
         const int o = o_begin + t;
         if (o >= o_end) break;
         const float mean = stat[0][t], rstd = stat[1][t];
-        out4[static_cast<size_t>(o) * HW4] =
-            make_float4(gelu_erf((z[t].x - mean) * rstd), gelu_erf((z[t].y - mean) * rstd),
-                        gelu_erf((z[t].z - mean) * rstd), gelu_erf((z[t].w - mean) * rstd));
+        const float2 g01 = scx::tc::gelu_pair((z[t].x - mean) * rstd, (z[t].y - mean) * rstd);
+        const float2 g23 = scx::tc::gelu_pair((z[t].z - mean) * rstd, (z[t].w - mean) * rstd);
+        out4[static_cast<size_t>(o) * HW4] = make_float4(g01.x, g01.y, g23.x, g23.y);
     }
 }
 
 // Largest cluster the fused skip+norm kernel is launched with (portable cluster size).
 constexpr int kMaxNormCluster = 8;
+
 
 // y[b][oc][p] = b2[oc] + sum_j W2[oc][j] GELU(b1[j] + sum_c W1[j][c] h[b][c][p])
 // Each thread takes PX pixels (kThreads apart, so loads and stores stay coalesced): one

@@ -24,8 +24,6 @@ constexpr int kProjThreads = 256;  // 8 warps: two per TMEM sub-partition
 constexpr int kTile = 128;         // pixels per CTA (MMA M)
 constexpr int kMaxOut = 4;
 
-__device__ __forceinline__ float gelu(float z) { return tc::gelu_as(z); }
-
 // W [N][K] (row-major, K = channels) -> tf32 hi/lo (fp32 containers), K-major SW128: 4
 // consecutive k of row n per 16-byte unit.
 __device__ __forceinline__ void stage_weights(const float* __restrict__ w, int N, int K, uint8_t* w_hi,
@@ -96,8 +94,9 @@ __device__ __forceinline__ void finish_units(uint32_t row, int j_begin, int j_en
 #pragma unroll
         for (int k4 = 0; k4 < 4; ++k4) {
             const float4 bb = *reinterpret_cast<const float4*>(b1s + j0 + 4 * k4);
-            const float g0 = gelu(v[4 * k4 + 0] + bb.x), g1 = gelu(v[4 * k4 + 1] + bb.y);
-            const float g2 = gelu(v[4 * k4 + 2] + bb.z), g3 = gelu(v[4 * k4 + 3] + bb.w);
+            const float2 g01 = tc::gelu_pair(v[4 * k4 + 0] + bb.x, v[4 * k4 + 1] + bb.y);
+            const float2 g23 = tc::gelu_pair(v[4 * k4 + 2] + bb.z, v[4 * k4 + 3] + bb.w);
+            const float g0 = g01.x, g1 = g01.y, g2 = g23.x, g3 = g23.y;
 #pragma unroll
             for (int o = 0; o < OC; ++o) {
                 const float4 ww = *reinterpret_cast<const float4*>(w2s + o * ph + j0 + 4 * k4);

@@ -1,13 +1,12 @@
-// Quadrant fold / unfold for the folded tensor-core path (planes of 2Hs x 2Ws samples).
+// Quadrant unfold for the folded tensor-core path (planes of 2Hs x 2Ws samples):
 //
-//   fold:   xs[q][p][h][w] = sum_{alpha,beta} (-1)^(a alpha + b beta) x[p][h + Hs alpha][w + Ws beta]
 //   unfold: y[p][h + Hs alpha][w + Ws beta] = sum_q (-1)^(a alpha + b beta) zs[q][p][h][w]
 //
 // with q = 2a + b.  Because exp(-2 pi i k (n + N/2) / N) = (-1)^k exp(-2 pi i k n / N), the
-// spectrum of folded sub-plane q against the full-period twiddles is the full spectrum at
-// rows kx = a (mod 2) and columns ky = b (mod 2), and the inverse of each parity class,
-// unfolded, is the full inverse.  Both directions apply the same 4 x 4 sign matrix; each
-// thread moves four float4 (one per quadrant / sub-plane) and writes four.
+// inverse of each parity class of the spectrum (rows kx = a, columns ky = b mod 2) against the
+// full-period twiddles, unfolded, is the full inverse.  (The forward direction, the same 4 x 4
+// sign matrix applied to the quadrants, runs inside the tensor-core forward kernel.)  Each
+// thread reads four float4 (one per sub-plane) and writes four.
 #include <algorithm>
 
 #include "scx_internal.h"
@@ -35,10 +34,9 @@ __device__ __forceinline__ void butterfly(const float4& v00, const float4& v01, 
 #undef SCX_BF
 }
 
-// dir 0: fold (quadrants of x -> sub-planes), dir 1: unfold (sub-planes -> quadrants of y).
-template <int DIR>
-__global__ void __launch_bounds__(kThreads) fold_kernel(const float4* __restrict__ in, float4* __restrict__ out, int P,
-                                                        int Hs, int Ws4) {
+// Sub-planes zs[q] -> quadrants of y.
+__global__ void __launch_bounds__(kThreads) unfold_kernel(const float4* __restrict__ in, float4* __restrict__ out,
+                                                          int P, int Hs, int Ws4) {
     const long long per_plane = static_cast<long long>(Hs) * Ws4;  // float4 per sub-plane
     const long long total = per_plane * P;
     const long long sub_stride = total;                             // float4 between sub-planes
@@ -49,49 +47,28 @@ __global__ void __launch_bounds__(kThreads) fold_kernel(const float4* __restrict
         const long long h = r / Ws4, w = r - h * Ws4;
         // full plane: 2Hs rows of 2 Ws4 float4
         const long long row0 = (p * 2 * Hs + h) * (2LL * Ws4), row1 = row0 + static_cast<long long>(Hs) * 2 * Ws4;
+        const float4 z0 = __ldg(in + i), z1 = __ldg(in + sub_stride + i), z2 = __ldg(in + 2 * sub_stride + i),
+                     z3 = __ldg(in + 3 * sub_stride + i);
+        // y quadrant (alpha, beta) = sum_q (-1)^(a alpha + b beta) z_q
         float4 o[4];
-        if (DIR == 0) {
-            butterfly(__ldg(in + row0 + w), __ldg(in + row0 + Ws4 + w), __ldg(in + row1 + w),
-                      __ldg(in + row1 + Ws4 + w), o);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) out[q * sub_stride + i] = o[q];
-        } else {
-            const float4 z0 = __ldg(in + i), z1 = __ldg(in + sub_stride + i), z2 = __ldg(in + 2 * sub_stride + i),
-                         z3 = __ldg(in + 3 * sub_stride + i);
-            // y quadrant (alpha, beta) = sum_q (-1)^(a alpha + b beta) z_q: the same matrix with
-            // the roles of (alpha, beta) and (a, b) exchanged
-            butterfly(z0, z1, z2, z3, o);
-            __stcs(out + row0 + w, o[0]);
-            __stcs(out + row0 + Ws4 + w, o[1]);
-            __stcs(out + row1 + w, o[2]);
-            __stcs(out + row1 + Ws4 + w, o[3]);
-        }
+        butterfly(z0, z1, z2, z3, o);
+        __stcs(out + row0 + w, o[0]);
+        __stcs(out + row0 + Ws4 + w, o[1]);
+        __stcs(out + row1 + w, o[2]);
+        __stcs(out + row1 + Ws4 + w, o[3]);
     }
-}
-
-cudaError_t launch(int dir, const float* in, float* out, int P, int Hs, int Ws, cudaStream_t stream) {
-    if (P <= 0 || Hs <= 0 || Ws % 4 != 0 || ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15))
-        return cudaErrorInvalidValue;
-    const long long total = static_cast<long long>(P) * Hs * (Ws / 4);
-    const long long blocks = std::min<long long>((total + kThreads - 1) / kThreads, 8LL * num_sms());
-    const dim3 grid(static_cast<unsigned>(blocks));
-    if (dir == 0)
-        fold_kernel<0><<<grid, kThreads, 0, stream>>>(reinterpret_cast<const float4*>(in), reinterpret_cast<float4*>(out),
-                                                      P, Hs, Ws / 4);
-    else
-        fold_kernel<1><<<grid, kThreads, 0, stream>>>(reinterpret_cast<const float4*>(in), reinterpret_cast<float4*>(out),
-                                                      P, Hs, Ws / 4);
-    return cudaGetLastError();
 }
 
 }  // namespace
 
-cudaError_t launch_fold(const float* x, float* xs, int P, int Hs, int Ws, cudaStream_t stream) {
-    return launch(0, x, xs, P, Hs, Ws, stream);
-}
-
 cudaError_t launch_unfold(const float* zs, float* y, int P, int Hs, int Ws, cudaStream_t stream) {
-    return launch(1, zs, y, P, Hs, Ws, stream);
+    if (P <= 0 || Hs <= 0 || Ws % 4 != 0 || ((reinterpret_cast<uintptr_t>(zs) | reinterpret_cast<uintptr_t>(y)) & 15))
+        return cudaErrorInvalidValue;
+    const long long total = static_cast<long long>(P) * Hs * (Ws / 4);
+    const long long blocks = std::min<long long>((total + kThreads - 1) / kThreads, 8LL * num_sms());
+    unfold_kernel<<<dim3(static_cast<unsigned>(blocks)), kThreads, 0, stream>>>(
+        reinterpret_cast<const float4*>(zs), reinterpret_cast<float4*>(y), P, Hs, Ws / 4);
+    return cudaGetLastError();
 }
 
 bool tc_split_supported(int H, int W, int m1, int m2) {

@@ -115,17 +115,37 @@ cudaError_t launch_dft_inv_tc(const float2* in1, const float2* in2, long long in
                               int in_row_stride, float* y, int Q, int H, int W, int m1, int m2,
                               cudaStream_t stream, const TcSub* sub = nullptr);
 
-// Folded tensor-core path for 256 x 256 planes (even m1 <= 32, even m2 <= 64): fold, four
-// sub-problem DFTs, and on the inverse side four sub-problem DFTs then unfold.  `scratch`
-// holds P planes of floats (split_scratch_bytes).
+// Folded tensor-core path for 256 x 256 planes (even m1 <= 32, even m2 <= 64).  Forward: one
+// launch of the tensor-core kernel in its folded mode (launch_dft_fwd_tc_folded: CTAs in groups
+// of four, one per parity sub-problem, each folding the full planes in its converters).
+// Inverse: four sub-problem DFTs into `scratch` (P planes of floats, split_scratch_bytes), then
+// the unfold.
 bool tc_split_supported(int H, int W, int m1, int m2);
+// 256 x 256 planes (m1, m2 <= 32) on the inverse side without the fold: one launch whose CTAs,
+// in groups of four, each compute one 128 x 128 quadrant of the output from the full corners
+// (the quadrant's offset is in its twiddle tables).  No scratch.
+bool tc_quad_supported(int H, int W, int m1, int m2);
+cudaError_t launch_dft_inv_tc_quad(const float2* in1, const float2* in2, long long in_plane_stride,
+                                   int in_row_stride, float* y, int Q, int H, int W, int m1, int m2,
+                                   cudaStream_t stream);
+cudaError_t launch_dft_fwd_tc_folded(const float* x, float2* out1, float2* out2, long long out_plane_stride,
+                                     int out_row_stride, int P, int H, int W, int m1, int m2, cudaStream_t stream);
 size_t split_scratch_bytes(long long P, int H, int W);
-cudaError_t launch_fold(const float* x, float* xs, int P, int Hs, int Ws, cudaStream_t stream);
 cudaError_t launch_unfold(const float* zs, float* y, int P, int Hs, int Ws, cudaStream_t stream);
 
+// Per-shape kernel variants chosen by measurement (scx_set_dft_variant / scx_set_mix_variant,
+// filled from a tuning table by the host; scx_variants.cu).  kDftAuto and kMixAuto leave the
+// choice to the library's fixed rules.  A variant that does not apply to a shape (or to the
+// operands' alignment) falls back to those rules, so a table never makes a call fail.
+constexpr int kDftAuto = 0, kDftFfma = 1, kDftTensor = 2, kDftFolded = 3;
+constexpr int kMixAuto = -1, kMixSmem = 7;  // 0 .. 6: the TMA-ring tile shapes of scx_mix.cu
+int dft_variant(int H, int W, int m1, int m2);
+int mix_variant(int ncorner, int B, int Cin, int Cout, int NM);
+
 // Forward / inverse truncated DFT through the fastest kernel for the shape: the
-// tensor-core kernels where supported (unless SCX_VARIANT=ffma), else the FFMA kernels.
-// `scratch` (optional) enables the folded path for shapes that need it.
+// tensor-core kernels where supported (unless SCX_VARIANT=ffma or the shape's variant says
+// otherwise), else the FFMA kernels.  `scratch` (optional) enables the folded path for shapes
+// that need it.
 cudaError_t dft_fwd(const float* x, float2* out1, float2* out2, long long out_plane_stride, int out_row_stride,
                     int P, int H, int W, int m1, int m2, const Twiddles& tw, cudaStream_t stream,
                     float* scratch = nullptr, size_t scratch_bytes = 0);

@@ -288,8 +288,9 @@ struct RingChoice {
 
 // The ring shape with the least modelled time: FMA work (padding included) at a rate that
 // saturates at 16 resident warps per SM, or the staging traffic from L2 at 64 B per SM cycle,
-// whichever is larger, plus a load latency per CTA wave.  ci < 0 when no shape fits.
-cudaError_t choose_ring(int ncorner, int B, int Cin, int Cout, int NM, RingChoice* out) {
+// whichever is larger, plus a load latency per CTA wave.  `only` >= 0 restricts the choice to
+// that shape (a measured variant).  ci < 0 when no shape fits.
+cudaError_t choose_ring(int ncorner, int B, int Cin, int Cout, int NM, int only, RingChoice* out) {
     const int NMT = (NM + kRingTM - 1) / kRingTM;
     const int sms = num_sms();
     const int nch = (Cin + kRingIC - 1) / kRingIC;
@@ -298,6 +299,7 @@ cudaError_t choose_ring(int ncorner, int B, int Cin, int Cout, int NM, RingChoic
     *out = RingChoice{-1, 0, 0};
     double best_t = 0;
     for (int ci = 0; ci < kNumRingCands; ++ci) {
+        if (only >= 0 && ci != only) continue;
         const RingCfg& c = kRingCands[ci];
         const int BB = c.BT * c.NBQ, OC = c.OT * c.NOQ, threads = 16 * c.NBQ * c.NOQ * c.KS;
         if (BB > B || OC > Cout) continue;  // TMA boxes stay inside the tensors
@@ -330,6 +332,11 @@ cudaError_t choose_ring(int ncorner, int B, int Cin, int Cout, int NM, RingChoic
     return cudaSuccess;
 }
 
+// mix_smem_kernel stages one mode's x and w rows (at least) in shared memory.
+bool smem_kernel_fits(int B, int Cin, int Cout) {
+    return (static_cast<size_t>(B) * Cin + static_cast<size_t>(Cin) * Cout) * sizeof(float2) <= 200 * 1024;
+}
+
 // The TMA ring launch; returns cudaErrorNotSupported when the shape or alignment does not fit
 // its boxes (the caller then uses mix_smem_kernel).
 cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1, const float2* w2, float2* y1,
@@ -337,23 +344,33 @@ cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1
     const uintptr_t al = reinterpret_cast<uintptr_t>(x1) | reinterpret_cast<uintptr_t>(w1) |
                          (ncorner == 2 ? (reinterpret_cast<uintptr_t>(x2) | reinterpret_cast<uintptr_t>(w2)) : 0);
     if (NM % 2 != 0 || (al & 15) != 0 || Cin < kRingIC) return cudaErrorNotSupported;
-    // Tile shapes: the one with the least modelled time, chosen once per shape and device.
+    const int forced = mix_variant(ncorner, B, Cin, Cout, NM);
+    // measured: the per-thread kernel wins (when one mode's operands fit its shared memory)
+    if (forced == kMixSmem && smem_kernel_fits(B, Cin, Cout)) return cudaErrorNotSupported;
+    // Tile shapes: the measured one when the variant table names one that fits, else the one
+    // with the least modelled time; chosen once per shape, variant and device.
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     static std::mutex m;
-    static std::map<std::tuple<int, int, int, int, int, int>, RingChoice> chosen;
+    static std::map<std::tuple<int, int, int, int, int, int, int>, RingChoice> chosen;
     RingChoice ch{-1, 0, 0};
     const int nch = (Cin + kRingIC - 1) / kRingIC;
     {
         std::lock_guard<std::mutex> lock(m);
-        const auto key = std::make_tuple(dev, ncorner, B, Cin, Cout, NM);
+        const auto key = std::make_tuple(dev, ncorner, B, Cin, Cout, NM, forced);
         auto it = chosen.find(key);
         if (it != chosen.end()) {
             ch = it->second;
         } else {
-            e = choose_ring(ncorner, B, Cin, Cout, NM, &ch);
-            if (e != cudaSuccess) return e;
+            if (forced >= 0) {
+                e = choose_ring(ncorner, B, Cin, Cout, NM, forced, &ch);
+                if (e != cudaSuccess) return e;
+            }
+            if (ch.ci < 0) {
+                e = choose_ring(ncorner, B, Cin, Cout, NM, -1, &ch);
+                if (e != cudaSuccess) return e;
+            }
             chosen.emplace(key, ch);
         }
     }

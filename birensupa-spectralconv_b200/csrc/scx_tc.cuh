@@ -352,6 +352,13 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
                  : "memory");
 }
 
+// 4 consecutive 32-bit columns of this thread's TMEM lane from registers (not waited for).
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t* r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+
 // 32 consecutive fp32 columns of this thread's TMEM lane; the registers are valid only after
 // tmem_wait_ld().
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, float* v) {
@@ -435,6 +442,74 @@ __device__ __forceinline__ float gelu_as(float z) {
     p = fmaf(p, t, 0.254829592f);
     const float half_erfc = 0.5f * (p * t) * __expf(-x * x);
     return z * (z >= 0.f ? 1.0f - half_erfc : half_erfc);
+}
+
+// ---- packed fp32 pairs (sm_100 f32x2 instructions: two fp32 lanes per 64-bit register)
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t r) {
+    float2 v;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+    return v;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// GELU of two values at once: the formula of gelu_as (Abramowitz & Stegun 7.1.26 for
+// erfc(|z| / sqrt 2), t = 1 / (1 + p x)) with the polynomial, the products and the final
+// blend in packed f32x2 instructions and the reciprocal and exponential as one approximate
+// instruction per value.  The factor 1/2 of Phi's tail is taken into the exponent
+// (exp(-x^2) / 2 = 2^(-x^2 log2 e - 1)), and Phi = s + m * tail with m = -1, s = 1 for
+// z >= 0 and m = 1, s = 0 below, so both branches round once, as in gelu_as.
+__device__ __forceinline__ float2 gelu_pair(float z0, float z1) {
+    const uint64_t z = f2_pack(z0, z1);
+    const float a0 = fabsf(z0), a1 = fabsf(z1);
+    const uint64_t x = f2_mul(f2_pack(a0, a1), f2_pack(0.70710678118654752f, 0.70710678118654752f));
+    const uint64_t den = f2_fma(f2_pack(0.3275911f, 0.3275911f), x, f2_pack(1.0f, 1.0f));
+    const float2 dn = f2_unpack(den);
+    const uint64_t t = f2_pack(rcp_approx(dn.x), rcp_approx(dn.y));
+    uint64_t p = f2_fma(f2_pack(1.061405429f, 1.061405429f), t, f2_pack(-1.453152027f, -1.453152027f));
+    p = f2_fma(p, t, f2_pack(1.421413741f, 1.421413741f));
+    p = f2_fma(p, t, f2_pack(-0.284496736f, -0.284496736f));
+    p = f2_fma(p, t, f2_pack(0.254829592f, 0.254829592f));
+    const uint64_t pt = f2_mul(p, t);
+    const uint64_t xx = f2_mul(x, x);
+    // -log2(e) x^2 - 1
+    const float2 arg = f2_unpack(f2_fma(xx, f2_pack(-1.4426950408889634f, -1.4426950408889634f), f2_pack(-1.0f, -1.0f)));
+    const uint64_t tail = f2_mul(pt, f2_pack(ex2_approx(arg.x), ex2_approx(arg.y)));  // erfc(x) / 2
+    // m = +1 below zero, -1 from zero up (1.0f with the inverted sign of z)
+    const float m0 = __uint_as_float(0x3f800000u | (~__float_as_uint(z0) & 0x80000000u));
+    const float m1 = __uint_as_float(0x3f800000u | (~__float_as_uint(z1) & 0x80000000u));
+    const uint64_t m = f2_pack(m0, m1);
+    const uint64_t s = f2_fma(m, f2_pack(-0.5f, -0.5f), f2_pack(0.5f, 0.5f));
+    const uint64_t phi = f2_fma(m, tail, s);
+    return f2_unpack(f2_mul(z, phi));
 }
 
 }  // namespace tc

@@ -11,6 +11,8 @@ the reference and reference state dicts load unchanged.  Differences:
 * ``FNO2d.forward_supa_chain`` / ``FNO2d.forward_device`` run the whole forward on the
   device through libscx.so's fused FNO entry point (one C call per forward: lift, four
   Fourier layers, projection), optionally replayed from a CUDA graph.
+* ``FNO2d.forward_autograd`` is the differentiable device forward that training uses
+  (fno_train.py): spectral convolutions through the library's forward and backward kernels.
 * ``instance_norm=False`` builds the norm-free layer (SpectralConv + 1x1 skip + GELU).
 """
 
@@ -24,7 +26,15 @@ import torch.nn.functional as F
 
 import _scx
 import spectral_conv_ext
-from spectral_conv_ops import spectral_conv2d_supa
+from spectral_conv_ops import spectral_conv2d_autograd, spectral_conv2d_supa
+
+
+def _conv1x1(conv: nn.Conv2d, x: torch.Tensor) -> torch.Tensor:
+    """A 1x1 Conv2d as an fp32 channel contraction.  On CUDA, nn.Conv2d goes through cuDNN,
+    which computes in TF32 by default (about 1e-3 relative error); the contraction runs as a
+    cuBLAS matmul in full fp32, forward and backward."""
+    out = torch.einsum("oi,bihw->bohw", conv.weight[:, :, 0, 0], x)
+    return out + conv.bias[None, :, None, None] if conv.bias is not None else out
 
 
 class SpectralConv2d(nn.Module):
@@ -135,6 +145,24 @@ class FNO2d(nn.Module):
         for layer in self.fourier_layers:
             x = layer(x, use_supa=False)
         return self.project(x)
+
+    def forward_autograd(self, x: torch.Tensor) -> torch.Tensor:
+        """Differentiable forward on x's CUDA device, for training: the module's own lift,
+        1x1 skips, norms, GELUs and projection run as torch ops on the device, and every
+        spectral convolution runs through the library's forward and backward kernels
+        (SpectralConv2dFunction), so gradients reach every parameter without a host round trip.
+        Same math as forward(use_supa=False) (fno_ns/model.py:183-198)."""
+        if not x.is_cuda:
+            raise RuntimeError("forward_autograd needs a CUDA tensor")
+        if x.dim() != 4:
+            raise ValueError(f"x must be [B,T,H,W], got {tuple(x.shape)}")
+        x = x.to(torch.float32)
+        h = _conv1x1(self.lift, torch.cat([x, self.get_grid(x.shape, x.device)], dim=1))
+        for layer in self.fourier_layers:
+            sc = layer.spectral_conv
+            spectral = spectral_conv2d_autograd(h.contiguous(), sc.weights1, sc.weights2, sc.modes1, sc.modes2)
+            h = F.gelu(layer.norm(spectral + _conv1x1(layer.conv, h)))
+        return _conv1x1(self.project[2], F.gelu(_conv1x1(self.project[0], h)))
 
     def prepare_supa_eval(self) -> None:
         """Moves every parameter to the current CUDA device (fno_ns/model.py:200-217)."""

@@ -11,6 +11,8 @@ shapes and spectra stand in for it.  Every generator runs on the CPU with an exp
                          each field normalised to unit variance
 * ``ns_vorticity``       GRF initial vorticity (spectrum (k^2+49)^-2.5) advanced by a
                          pseudo-spectral 2-D Navier-Stokes vorticity step (nu, dt)
+* ``ns_vorticity_device`` the same on a CUDA device, transforms on the library's DFT kernels
+* ``fno_pairs_device``   (10 frames, next frame) training pairs from it
 * ``fno_input``          [B, H, W, T+2] channels-last: T vorticity frames + 2 grid channels
 """
 
@@ -89,6 +91,63 @@ def ns_vorticity(batch: int, frames: int, H: int, W: int, seed: int, *, nu: floa
             w_hat = ((1.0 - 0.5 * dt * nu * k2) * w_hat + dt * (f_hat - adv_hat)) / (1.0 + 0.5 * dt * nu * k2)
         out[:, t] = torch.fft.irfft2(w_hat, s=(H, W)).to(torch.float32)
     return out
+
+
+def ns_vorticity_device(batch: int, frames: int, H: int, W: int, seed: int, device, *, nu: float = 1e-3,
+                        dt: float = 1e-4, substeps: int = 1) -> torch.Tensor:
+    """``ns_vorticity`` on a CUDA device, in fp32: the same initial field (the GRF noise is
+    drawn on the host from the same seed) and the same pseudo-spectral step, with every
+    transform on the library's own full-spectrum DFT kernels (``spectral_conv_ext.rfft2_sufft``
+    / ``irfft2_sufft``, no torch.fft) and the spectral products as device tensor arithmetic.
+    Per step the four fields u, v, w_x, w_y go through one batched inverse transform."""
+    import spectral_conv_ext as ext
+
+    def rfft2(f):  # [n, H, W] real -> [n, H, W/2+1] complex
+        return torch.view_as_complex(ext.rfft2_sufft(f.unsqueeze(1).contiguous())[:, 0])
+
+    def irfft2(fh):  # [n, C, H, W/2+1] complex -> [n, C, H, W] real
+        return ext.irfft2_sufft(torch.view_as_real(fh).contiguous(), H, W)
+
+    noise = torch.randn(batch, H, W, generator=_gen(seed), dtype=torch.float64).to(torch.float32).to(device)
+    amp = ((_wavenumber_sq(H, W) + 49.0) ** (-2.5 / 2.0))
+    amp[0, 0] = 0.0
+    field = irfft2((rfft2(noise) * amp.to(torch.float32).to(device)).unsqueeze(1))[:, 0]
+    field = field - field.mean(dim=(-2, -1), keepdim=True)
+    w = field / field.std(dim=(-2, -1), keepdim=True).clamp_min(1e-30)
+    Wf = W // 2 + 1
+    kx = torch.fft.fftfreq(H, d=1.0 / H).to(torch.float32)[:, None].expand(H, Wf).to(device)
+    ky = torch.fft.rfftfreq(W, d=1.0 / W).to(torch.float32)[None, :].expand(H, Wf).to(device)
+    two_pi = 2.0 * math.pi
+    k2 = (two_pi ** 2) * (kx ** 2 + ky ** 2)
+    k2_inv = torch.where(k2 > 0, 1.0 / k2.clamp_min(1e-30), torch.zeros_like(k2))
+    dealias = ((kx.abs() <= (2.0 / 3.0) * (H // 2)) & (ky.abs() <= (2.0 / 3.0) * (W // 2))).to(torch.float32)
+    xs = torch.linspace(0, 1, H + 1, dtype=torch.float64)[:-1]
+    ys = torch.linspace(0, 1, W + 1, dtype=torch.float64)[:-1]
+    X, Y = torch.meshgrid(xs, ys, indexing="ij")
+    forcing = (0.1 * (torch.sin(two_pi * (X + Y)) + torch.cos(two_pi * (X + Y)))).to(torch.float32).to(device)
+    f_hat = rfft2(forcing.unsqueeze(0))[0]
+    ikx, iky = (1j * two_pi) * kx, (1j * two_pi) * ky
+    lhs = 1.0 + 0.5 * dt * nu * k2
+    rhs = 1.0 - 0.5 * dt * nu * k2
+    w_hat = rfft2(w)
+    out = torch.empty(batch, frames, H, W, device=device, dtype=torch.float32)
+    for t in range(frames):
+        for _ in range(substeps):
+            psi_hat = w_hat * k2_inv
+            fields = irfft2(torch.stack([iky * psi_hat, -ikx * psi_hat, ikx * w_hat, iky * w_hat], dim=1))
+            u, v, wx, wy = fields.unbind(1)
+            adv_hat = rfft2(u * wx + v * wy) * dealias
+            w_hat = (rhs * w_hat + dt * (f_hat - adv_hat)) / lhs
+        out[:, t] = irfft2(w_hat.unsqueeze(1))[:, 0]
+    return out
+
+
+def fno_pairs_device(n: int, seed: int, device, *, H: int = 64, W: int = 64, frames_in: int = 10):
+    """(x [n, frames_in, H, W], y [n, 1, H, W]) on the device: ``frames_in`` vorticity frames
+    and the next one as the target (the input/target split of fno_ns/dataset.py's sequence
+    dataset), from ``ns_vorticity_device``."""
+    seq = ns_vorticity_device(n, frames_in + 1, H, W, seed, device)
+    return seq[:, :frames_in].contiguous(), seq[:, frames_in:].contiguous()
 
 
 def grid_channels(batch: int, H: int, W: int) -> torch.Tensor:

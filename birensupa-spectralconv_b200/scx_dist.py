@@ -1,8 +1,8 @@
 """Batch sharding across ranks (one process per GPU) and the final output gather.
 
 The SpectralConv2d / FNO forward is independent per batch item and the weights are
-replicated, so the only exchange is one gather of the output shards (NCCL over
-NVLink on GPUs, gloo on CPU in the tests).  Shards are contiguous and ragged when the
+replicated, so the only exchange is one gather of the output shards to rank 0 (one group of
+NCCL point-to-point transfers over NVLink on GPUs, gloo on CPU in the tests).  Shards are contiguous and ragged when the
 batch does not divide: B=20 over 8 ranks -> 3,3,3,3,2,2,2,2.
 """
 
@@ -43,29 +43,47 @@ def init(backend: str, timeout_s: float = 120.0, device: torch.device | None = N
         dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=timeout_s), **kwargs)
 
 
-def gather_batch(local: torch.Tensor, batch: int, dst: int = 0) -> torch.Tensor | None:
-    """Gathers the ragged per-rank batch shards of ``local`` ([b_r, ...]) into one
-    [batch, ...] tensor on rank ``dst`` (None elsewhere).  Every rank pads its shard to
-    the largest shard and joins one all_gather_into_tensor; all ranks take the same
-    collective steps in the same order."""
+def gather_batch_into(local: torch.Tensor, out: torch.Tensor | None, batch: int, dst: int = 0) -> None:
+    """Gathers the ragged per-rank batch shards of ``local`` ([b_r, ...]) into ``out``
+    ([batch, ...], preallocated on rank ``dst``; ignored elsewhere).  Only rank ``dst``
+    receives: every other rank sends its shard once, straight into its contiguous slice of
+    ``out``, and all transfers go in one batched group of point-to-point operations (one
+    NCCL group over NVLink on GPUs).  Nothing is padded, allocated or concatenated, so the
+    call can sit inside a timed step.  Rank ``dst`` may compute its own shard straight into
+    its slice of ``out`` (``local`` a view of it), which saves the local copy.  Every rank
+    calls it once per gather."""
     world = dist.get_world_size()
     rank = dist.get_rank()
     sizes = shard_sizes(batch, world)
     if local.shape[0] != sizes[rank]:
         raise ValueError(f"rank {rank}: shard has {local.shape[0]} items, expected {sizes[rank]}")
-    bmax = max(sizes)
-    tail = tuple(local.shape[1:])
-    if local.shape[0] == bmax:
-        padded = local.contiguous()
+    if not local.is_contiguous():
+        raise ValueError("the local shard must be contiguous")
+    if rank == dst:
+        if out is None or out.shape[0] != batch or tuple(out.shape[1:]) != tuple(local.shape[1:]):
+            raise ValueError(f"rank {dst} needs an output of shape {(batch,) + tuple(local.shape[1:])}")
+        if not out.is_contiguous() or out.dtype != local.dtype or out.device != local.device:
+            raise ValueError("the output must be contiguous, with the shard's dtype and device")
+        lo, hi = shard_range(batch, world, rank)
+        if hi > lo and local.data_ptr() != out[lo:hi].data_ptr():
+            out[lo:hi].copy_(local)
+        ops = [dist.P2POp(dist.irecv, out[slice(*shard_range(batch, world, r))], r)
+               for r in range(world) if r != dst and sizes[r] > 0]
     else:
-        padded = torch.zeros((bmax,) + tail, dtype=local.dtype, device=local.device)
-        padded[: local.shape[0]] = local
-    stacked = torch.empty((world * bmax,) + tail, dtype=local.dtype, device=local.device)
-    dist.all_gather_into_tensor(stacked, padded)
-    if rank != dst:
-        return None
-    parts = [stacked[r * bmax: r * bmax + sizes[r]] for r in range(world)]
-    return torch.cat(parts, dim=0)
+        ops = [dist.P2POp(dist.isend, local, dst)] if sizes[rank] > 0 else []
+    if ops:
+        for work in dist.batch_isend_irecv(ops):
+            work.wait()
+
+
+def gather_batch(local: torch.Tensor, batch: int, dst: int = 0) -> torch.Tensor | None:
+    """Gathers the ragged per-rank batch shards of ``local`` ([b_r, ...]) into one new
+    [batch, ...] tensor on rank ``dst`` (None elsewhere), through ``gather_batch_into``."""
+    out = None
+    if dist.get_rank() == dst:
+        out = torch.empty((batch,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    gather_batch_into(local.contiguous(), out, batch, dst)
+    return out
 
 
 def max_over_ranks(value: float, device: torch.device | None = None) -> float:

@@ -69,6 +69,38 @@ def spectral_mul_out(x_freq: torch.Tensor, weights: torch.Tensor, y_freq: torch.
                    "launch_spectral_mul(out)")
 
 
+def spectral_mul_backward(x_freq: torch.Tensor | None, weights: torch.Tensor | None, grad_y: torch.Tensor,
+                          need_x: bool = True, need_w: bool = True):
+    """Gradients of ``spectral_mul`` (the backward of SpectralMulFunction,
+    spectral_conv/spectral_conv_ops.py:272-278) on the device: grad_x = grad_y W^H and
+    grad_w = X^H grad_y per mode.  Interleaved [...,2] float32 tensors as for spectral_mul;
+    returns (grad_x or None, grad_w or None)."""
+    _check_freq_tensor(grad_y, "grad_y")
+    _check(need_x or need_w, "nothing to compute")
+    B, Cout, m1, m2 = (int(s) for s in grad_y.shape[:4])
+    if need_x:
+        _check_freq_tensor(weights, "weights")
+        Cin = int(weights.size(0))
+        _check(weights.size(1) == Cout and weights.size(2) == m1 and weights.size(3) == m2, "weights shape mismatch")
+    if need_w:
+        _check_freq_tensor(x_freq, "x_freq")
+        Cin = int(x_freq.size(1))
+        _check(x_freq.size(0) == B and x_freq.size(2) == m1 and x_freq.size(3) == m2, "x_freq shape mismatch")
+    dev = grad_y.device
+    gx = torch.empty(B, Cin, m1, m2, 2, device=dev) if need_x else None
+    gw = torch.empty(Cin, Cout, m1, m2, 2, device=dev) if need_w else None
+    nbytes = _scx.lib.scx_spectral_mul_bwd_workspace_size(B, Cin, Cout, m1, m2)
+    _check(nbytes > 0, "invalid sizes")
+    with _scx.device_guard(dev):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        _scx.check(_scx.lib.scx_spectral_mul_bwd(x_freq.data_ptr() if need_w else None,
+                                                 weights.data_ptr() if need_x else None, grad_y.data_ptr(),
+                                                 gx.data_ptr() if need_x else None, gw.data_ptr() if need_w else None,
+                                                 B, Cin, Cout, m1, m2, ws.data_ptr(), nbytes, _scx.stream_of(dev)),
+                   "scx_spectral_mul_bwd")
+    return gx, gw
+
+
 def _check_dual(x1, w1, y1, x2, w2, y2) -> tuple[int, int, int, int, int]:
     def one(xn, wn, yn, prefix):
         _check_freq_tensor(xn, prefix)

@@ -23,8 +23,12 @@ import weakref
 import torch
 import torch.nn as nn
 
+import scx_tune
 import spectral_conv_ext
 
+# Kernel variants measured per shape by scx_tune.py, when a table has been saved
+# ($SCX_TUNE_TABLE, else the package's tune_table.json): applied once, at import.
+TUNED_VARIANTS = scx_tune.load()
 _WEIGHT_DEVICE_CACHE: dict[tuple, torch.Tensor] = {}
 _PARAM_CACHE: dict[tuple, tuple] = {}
 _WEIGHT_CACHE_MAX = 64
@@ -129,8 +133,10 @@ def spectral_mul_supa_out(x_freq_modes_interleaved: torch.Tensor, weights_interl
 
 
 class SpectralMulFunction(torch.autograd.Function):
-    """Device spectral_mul forward; conjugate-transpose einsum backward
-    (spectral_conv/spectral_conv_ops.py:260-278), both on the device."""
+    """Device spectral_mul forward and backward (spectral_conv/spectral_conv_ops.py:260-278):
+    the reference's two conjugate-transpose einsums run as the library's mixing kernel
+    (scx_spectral_mul_bwd: per-mode conjugate transposes of w and x, then grad_y W^H and
+    X^H grad_y), computing only the gradients autograd asks for."""
 
     @staticmethod
     def forward(ctx, x_freq_modes: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
@@ -145,10 +151,15 @@ class SpectralMulFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_output: torch.Tensor):
         x_c, w_c = ctx.saved_tensors
-        grad_y = grad_output.to(x_c.device, torch.complex64)
-        grad_x = torch.einsum("boxy,ioxy->bixy", grad_y, w_c.conj())
-        grad_w = torch.einsum("bixy,boxy->ioxy", x_c.conj(), grad_y)
-        return grad_x.to(ctx.out_device), grad_w.to(ctx.out_device)
+        need_x, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        if not (need_x or need_w):
+            return None, None
+        grad_y = grad_output.to(x_c.device, torch.complex64).resolve_conj().contiguous()
+        gx, gw = spectral_conv_ext.spectral_mul_backward(torch.view_as_real(x_c), torch.view_as_real(w_c),
+                                                         torch.view_as_real(grad_y), need_x, need_w)
+        grad_x = _interleaved_to_complex(gx).to(ctx.out_device) if need_x else None
+        grad_w = _interleaved_to_complex(gw).to(ctx.out_device) if need_w else None
+        return grad_x, grad_w
 
 
 def spectral_mul_autograd(x_freq_modes: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:

@@ -67,6 +67,21 @@ int scx_spectral_mul_dual(const float* x1, const float* x2, const float* w1, con
                           float* y1, float* y2, int batch_size, int channels_in,
                           int channels_out, int modes1, int modes2, scx_stream_t stream);
 
+/* Backward of the single-corner mixing: the gradients of SpectralMulFunction
+ * (spectral_conv/spectral_conv_ops.py:260-278, whose backward is two torch.einsum calls):
+ *   grad_x[b,i,k] = sum_o grad_y[b,o,k] conj(w[i,o,k]),  grad_w[i,o,k] = sum_b conj(x[b,i,k]) grad_y[b,o,k]
+ * x_freq [B][Cin][m1][m2][2], weights [Cin][Cout][m1][m2][2], grad_y [B][Cout][m1][m2][2];
+ * grad_x like x_freq and grad_w like weights, either NULL to skip it (x_freq may then be NULL
+ * when grad_w is, weights when grad_x is).  workspace: device memory of
+ * scx_spectral_mul_bwd_workspace_size() bytes, 256-byte aligned (the per-mode conjugate
+ * transposes of w and x). */
+size_t scx_spectral_mul_bwd_workspace_size(int batch_size, int channels_in, int channels_out,
+                                           int modes1, int modes2);
+int scx_spectral_mul_bwd(const float* x_freq, const float* weights, const float* grad_y,
+                         float* grad_x, float* grad_w, int batch_size, int channels_in,
+                         int channels_out, int modes1, int modes2, void* workspace,
+                         size_t workspace_bytes, scx_stream_t stream);
+
 /* Truncated forward real DFT writing only the two retained corners.
  * Replaces rfft2_sufft followed by the corner gathers x_freq[:, :, :m1, :m2] and
  * x_freq[:, :, -m1:, :m2] (spectral_conv/spectral_conv_ext.cpp:314-347,
@@ -226,6 +241,29 @@ size_t scx_fno2d_workspace_size(const scx_fno2d_config* cfg);
  * tables (see above). */
 int scx_fno2d_fwd(const scx_fno2d_config* cfg, const scx_fno2d_params* params, const float* x,
                   float* y, void* workspace, size_t workspace_bytes, scx_stream_t stream);
+
+/* ---------------------------------------------------------------------------------
+ * Per-shape kernel variants.  Replaces the reference's tuning table: _AUTO_TUNE_TABLE
+ * (spectral_conv_combo/spectral_conv_ops.py:45-63), written by tune.py's sweep
+ * (spectral_conv_combo/tune.py:154-261) and never read back there.  The host-side tuner
+ * (scx_tune.py) measures the variants that apply to a shape, persists the winners as JSON and
+ * sets them through these calls when the Python package is imported.  The table is
+ * process-wide (every device); a variant that does not fit a call (alignment, workspace)
+ * falls back to the library's rule, so setting one never makes a call fail.  No CUDA calls.
+ * --------------------------------------------------------------------------------- */
+/* Truncated-DFT variants: 0 = the library's rule, 1 = FFMA direct DFT, 2 = tensor-core
+ * kernels, 3 = the folded tensor-core path (256-point sides).  scx_dft_variants returns the
+ * bit mask (1 << variant) of the variants 1..3 that apply to the shape. */
+int scx_dft_variants(int H, int W, int modes1, int modes2);
+int scx_set_dft_variant(int H, int W, int modes1, int modes2, int variant);
+/* Mixing variants for (corners, B, Cin, Cout, modes = m1*m2): -1 = the library's cost model,
+ * 0..6 = one of the TMA-ring tile shapes, 7 = the per-thread shared-memory kernel. */
+int scx_set_mix_variant(int ncorner, int batch_size, int channels_in, int channels_out, int modes,
+                        int variant);
+/* kind 0: the DFT variant set for (a, b, c, d) = (H, W, m1, m2); kind 1: the mixing variant for
+ * (a, b, c, d, e) = (corners, B, Cin, Cout, modes). */
+int scx_get_variant(int kind, int a, int b, int c, int d, int e);
+void scx_clear_variants(void);
 
 /* Size of the fixed device scratch used by scx_spectral_conv2d_fwd_noalloc (16 MiB). */
 #define SCX_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)

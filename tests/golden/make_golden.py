@@ -1,9 +1,9 @@
 """Generates the golden fixtures in this folder by running the REFERENCE implementation.
 
-Run once in a container where the reference checkout is mounted (default
-``/root/reference``); the fixtures are committed and the tests never read the reference:
+Run once where a checkout of the reference is available, passing its root (or setting
+``SCX_REFERENCE_ROOT``); the fixtures are committed and the tests never read the reference:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>
 
 What runs (all on the CPU, fp32, exactly the reference's code):
 * ``spectral_conv/reference_pytorch.py: SpectralConv2d`` on
@@ -25,6 +25,7 @@ confirm it regenerated the same inputs.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import sys
 import types
@@ -125,9 +126,12 @@ def official3d_fixtures(ref: Path) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SCX_REFERENCE_ROOT"),
+                    help="root of the reference checkout (default: $SCX_REFERENCE_ROOT)")
     ap.add_argument("--only", choices=["all", "conv3d"], default="all")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference <reference checkout> or set SCX_REFERENCE_ROOT")
     ref = Path(args.reference)
     torch.set_num_threads(8)
     conv3d_fixtures(ref)

@@ -51,7 +51,15 @@ def _worker(rank, world, port, batch, mode, results):
             return
         y = _forward_shard(x[lo:hi], w1, w2, 4, 5)
         try:
-            full = scx_dist.gather_batch(y, batch)
+            if mode == "into":
+                # preallocated output on rank 0; rank 0's shard is computed in place
+                full = torch.full((batch, 4, 12, 10), float("nan")) if rank == 0 else None
+                if rank == 0:
+                    full[lo:hi] = y
+                    y = full[lo:hi]
+                scx_dist.gather_batch_into(y, full, batch)
+            else:
+                full = scx_dist.gather_batch(y, batch)
         except RuntimeError as e:
             results[rank] = f"error: {type(e).__name__}"
             return
@@ -83,9 +91,10 @@ def _run(world, batch, mode, join_s=90):
         return dict(results), len(alive)
 
 
+@pytest.mark.parametrize("mode", ["normal", "into"])
 @pytest.mark.parametrize("batch", [4, 5])  # even and ragged (3, 2) shards
-def test_sharded_forward_gathers_to_rank0(batch):
-    res, hung = _run(2, batch, "normal")
+def test_sharded_forward_gathers_to_rank0(batch, mode):
+    res, hung = _run(2, batch, mode)
     assert hung == 0
     assert isinstance(res[0], tuple), res[0]
     status, equal, shape, tmax = res[0]

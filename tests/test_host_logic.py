@@ -125,3 +125,34 @@ def test_new_entry_points_check_arguments_before_device_use():
     with pytest.raises(RuntimeError, match="host tensor"):
         spectral_conv_ext.spectral_conv2d_fwd_host(torch.zeros(1, 2, 8, 8, dtype=torch.float64), w3, w3, 2, 2,
                                                    torch.device("cpu"))
+
+
+def test_variant_table_round_trip(tmp_path):
+    """scx_tune: a saved table reloads and is applied through the C ABI (no CUDA call);
+    entries that do not apply to their shape are refused; merge replaces a shape's entry."""
+    import _scx
+    import scx_tune
+
+    lib = _scx.lib
+    lib.scx_clear_variants()
+    assert lib.scx_dft_variants(128, 128, 16, 16) == (1 << 1) | (1 << 2) | (1 << 3)
+    assert lib.scx_dft_variants(256, 256, 32, 32) == (1 << 1) | (1 << 3)
+    assert lib.scx_dft_variants(96, 160, 16, 20) == 1 << 1
+    assert lib.scx_dft_variants(64, 64, 65, 12) == 0  # m1 > H: invalid shape
+    table = scx_tune.empty_table()
+    scx_tune.merge(table, {"H": 64, "W": 64, "m1": 12, "m2": 12, "variant": "ffma"}, "dft")
+    scx_tune.merge(table, {"H": 64, "W": 64, "m1": 12, "m2": 12, "variant": "tensor"}, "dft")  # replaces
+    scx_tune.merge(table, {"H": 96, "W": 160, "m1": 16, "m2": 20, "variant": "tensor"}, "dft")  # not applicable
+    scx_tune.merge(table, {"corners": 2, "B": 20, "Cin": 32, "Cout": 32, "modes": 256, "variant": 3}, "mix")
+    assert len(table["dft"]) == 2
+    path = scx_tune.save(table, tmp_path / "table.json")
+    assert scx_tune.load(path) == 2
+    assert lib.scx_get_variant(0, 64, 64, 12, 12, 0) == 2
+    assert lib.scx_get_variant(0, 96, 160, 16, 20, 0) == 0
+    assert lib.scx_get_variant(1, 2, 20, 32, 32, 256) == 3
+    assert lib.scx_get_variant(1, 2, 20, 32, 32, 128) == -1
+    assert lib.scx_set_mix_variant(2, 20, 32, 32, 256, 8) == 1  # out of range
+    assert lib.scx_set_dft_variant(64, 64, 12, 12, 0) == 0 and lib.scx_get_variant(0, 64, 64, 12, 12, 0) == 0
+    lib.scx_clear_variants()
+    assert lib.scx_get_variant(1, 2, 20, 32, 32, 256) == -1
+    assert scx_tune.load(tmp_path / "missing.json") == 0

@@ -245,6 +245,32 @@ def test_spectral_mul_autograd_grads(cuda_device):
             assert_close(torch.view_as_real(ref).numpy(), torch.view_as_real(got).numpy(), 1e-4)
 
 
+@pytest.mark.parametrize("b,ci,co,m1,m2", [(20, 32, 32, 16, 16), (3, 5, 7, 6, 5), (16, 64, 48, 8, 8),
+                                            (1, 9, 2, 3, 4)])
+def test_spectral_mul_backward_entry_point(b, ci, co, m1, m2, cuda_device):
+    """scx_spectral_mul_bwd (SpectralMulFunction's backward on the device) against the
+    reference's two einsums (spectral_conv/spectral_conv_ops.py:272-278) in complex128, with
+    both gradients, and each alone (bitwise the same as with both)."""
+    import spectral_conv_ext
+
+    g = torch.Generator().manual_seed(b * 1000 + ci * 10 + co)
+    x = torch.randn(b, ci, m1, m2, dtype=torch.cfloat, generator=g)
+    w = torch.randn(ci, co, m1, m2, dtype=torch.cfloat, generator=g)
+    gy = torch.randn(b, co, m1, m2, dtype=torch.cfloat, generator=g)
+    c128 = torch.complex128
+    ref_x = torch.einsum("boxy,ioxy->bixy", gy.to(c128), w.to(c128).conj())
+    ref_w = torch.einsum("bixy,boxy->ioxy", x.to(c128).conj(), gy.to(c128))
+    xr, wr, gr = (torch.view_as_real(t).contiguous().to(cuda_device) for t in (x, w, gy))
+    gx, gw = spectral_conv_ext.spectral_mul_backward(xr, wr, gr)
+    torch.cuda.synchronize(cuda_device)
+    assert_close(torch.view_as_real(ref_x).numpy(), gx.cpu().double().numpy())
+    assert_close(torch.view_as_real(ref_w).numpy(), gw.cpu().double().numpy())
+    gx_only, none_w = spectral_conv_ext.spectral_mul_backward(None, wr, gr, need_w=False)
+    none_x, gw_only = spectral_conv_ext.spectral_mul_backward(xr, None, gr, need_x=False)
+    assert none_w is None and none_x is None
+    assert torch.equal(gx_only, gx) and torch.equal(gw_only, gw)
+
+
 @pytest.mark.parametrize("H,W", [(16, 16), (9, 12), (12, 9), (64, 40), (5, 3)])
 def test_full_spectrum_compat(H, W, cuda_device):
     """rfft2_sufft / irfft2_sufft compatibility entry points vs numpy FFT."""
@@ -384,6 +410,12 @@ FWD_TC_SHAPES = [
     (4, 8, 128, 128, 7, 3),      # 8 columns per TW block
     (40, 32, 128, 128, 16, 16),  # several 2-plane tiles per CTA
     (2, 151, 64, 64, 12, 12),    # odd plane count over all SMs
+    # folded: one launch, CTAs in parity groups of four, the quadrants combined in the converters
+    (2, 3, 256, 256, 32, 32),    # 128 x 128 parity sub-planes
+    (1, 5, 128, 256, 16, 20),    # 64 x 128 sub-planes
+    (3, 2, 256, 128, 16, 16),    # 128 x 64 sub-planes: two planes per column tile
+    (2, 2, 128, 128, 24, 20),    # 2*m1 > 32 at 128: 64 x 64 sub-planes
+    (1, 1, 256, 256, 8, 12),     # one plane: most CTA groups have nothing to do
 ]
 
 
@@ -417,6 +449,11 @@ INV_TC_SHAPES = [
     (4, 8, 128, 128, 7, 3),
     (40, 32, 128, 128, 16, 16),  # several groups per CTA
     (2, 151, 64, 64, 12, 12),    # odd plane count over all SMs
+    # 256 x 256: four CTAs per plane group, one per output quadrant, from the full corners
+    (2, 3, 256, 256, 32, 32),    # 64 spectrum rows, 32 columns
+    (1, 5, 256, 256, 16, 20),
+    (3, 7, 256, 256, 7, 3),      # odd plane count: a partial last group
+    (1, 1, 256, 256, 1, 1),      # DC only, one plane
 ]
 
 
@@ -447,6 +484,7 @@ def test_inverse_corners_vs_f64(shape, cuda_device):
     (1, 2, 2, 256, 256, 32, 64),   # m1 = 32, m2 = 64: 16 slots and 32 columns per parity class
     (2, 2, 3, 128, 128, 24, 20),   # 2*m1 > 32 at 128: folded into 64 x 64 sub-planes
     (3, 4, 2, 256, 128, 16, 16),   # non-square folded plane
+    (2, 3, 3, 128, 256, 16, 20),   # non-square, the other way
 ])
 def test_folded_path_vs_f64_oracle(shape, cuda_device):
     """Planes folded into four parity sub-planes (fused forward with its workspace)."""

@@ -20,6 +20,27 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kRpt = 4;    // stage-1 rows per thread
+
+// Cooperative copy of n elements, element i from load(i) to store(i, v): each thread first
+// issues up to LB loads into registers and only then stores them, so a batch of loads is in
+// flight at once (a plain load-store loop waits a full memory latency per element: the
+// compiler cannot move a load above the previous shared-memory store).
+template <int LB, typename T, typename LoadF, typename StoreF>
+__device__ __forceinline__ void batched_copy(int n, LoadF load, StoreF store) {
+    for (int i0 = threadIdx.x; i0 < n; i0 += kThreads * LB) {
+        T v[LB];
+#pragma unroll
+        for (int u = 0; u < LB; ++u) {
+            const int i = i0 + u * kThreads;
+            if (i < n) v[u] = load(i);
+        }
+#pragma unroll
+        for (int u = 0; u < LB; ++u) {
+            const int i = i0 + u * kThreads;
+            if (i < n) store(i, v[u]);
+        }
+    }
+}
 constexpr int kRt = 32;    // inverse: output rows per tile
 constexpr int kSmemBudget = 200 * 1024;
 
@@ -51,10 +72,13 @@ __global__ void __launch_bounds__(kThreads) dft_fwd_ffma_kernel(const FwdArgs a)
     float2* Rs = twc + a.ST * RC;                    // [RC][KT]
     float* xs = reinterpret_cast<float*>(Rs + RC * KT);  // [RC][WP]
 
-    for (int i = tid; i < W * kt; i += kThreads) {
-        const int w = i / kt, k = i - w * kt;
-        twr[i] = a.tw_row[static_cast<size_t>(w) * a.m2 + ky0 + k];
-    }
+    batched_copy<8, float2>(
+        W * kt,
+        [&](int i) {
+            const int w = i / kt, k = i - w * kt;
+            return a.tw_row[static_cast<size_t>(w) * a.m2 + ky0 + k];
+        },
+        [&](int i, float2 v) { twr[i] = v; });
     const int groups = RC / kRpt;
     const int s1_active = groups * kt;
     const int nout = st * kt;
@@ -68,15 +92,19 @@ __global__ void __launch_bounds__(kThreads) dft_fwd_ffma_kernel(const FwdArgs a)
             const int rows = min(RC, H - h0);
             __syncthreads();
             const float* src = xp + static_cast<size_t>(h0) * W;
-            for (int i = tid; i < rows * W; i += kThreads) {
-                const int r = i / W, c = i - r * W;
-                xs[r * WP + c] = __ldcs(src + i);
-            }
-            for (int i = tid; i < st * RC; i += kThreads) {
-                const int s = i / RC, hh = i - s * RC;
-                twc[i] = hh < rows ? a.tw_col[static_cast<size_t>(s0 + s) * H + h0 + hh]
-                                   : make_float2(0.f, 0.f);
-            }
+            batched_copy<16, float>(
+                rows * W, [&](int i) { return __ldcs(src + i); },
+                [&](int i, float v) {
+                    const int r = i / W, c = i - r * W;
+                    xs[r * WP + c] = v;
+                });
+            batched_copy<8, float2>(
+                st * RC,
+                [&](int i) {
+                    const int s = i / RC, hh = i - s * RC;
+                    return hh < rows ? a.tw_col[static_cast<size_t>(s0 + s) * H + h0 + hh] : make_float2(0.f, 0.f);
+                },
+                [&](int i, float2 v) { twc[i] = v; });
             __syncthreads();
             if (tid < s1_active) {
                 const int g = tid / kt, k = tid - g * kt;
@@ -158,9 +186,8 @@ __global__ void __launch_bounds__(kThreads) dft_inv_ffma_kernel(const InvArgs a)
     float2* Zs = twri + KC * W;                     // [kRt][KC]
 
     const bool single_chunk = KC >= a.m2;
-    if (single_chunk) {
-        for (int i = tid; i < a.m2 * W; i += kThreads) twri[i] = a.tw_row[i];
-    }
+    if (single_chunk)
+        batched_copy<8, float2>(a.m2 * W, [&](int i) { return a.tw_row[i]; }, [&](int i, float2 v) { twri[i] = v; });
     const int tpp = (H + kRt - 1) / kRt;
     const int ntiles = a.Q * tpp;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
@@ -173,24 +200,33 @@ __global__ void __launch_bounds__(kThreads) dft_inv_ffma_kernel(const InvArgs a)
 #pragma unroll
             for (int j = 0; j < WPT; ++j) acc[r][j] = 0.f;
         __syncthreads();
-        for (int i = tid; i < kRt * S2; i += kThreads) {
-            const int r = i / S2, s = i - r * S2;
-            twci[i] = r < rows ? a.tw_col[static_cast<size_t>(h0 + r) * S2 + s] : make_float2(0.f, 0.f);
-        }
+        batched_copy<8, float2>(
+            kRt * S2,
+            [&](int i) {
+                const int r = i / S2, s = i - r * S2;
+                return r < rows ? a.tw_col[static_cast<size_t>(h0 + r) * S2 + s] : make_float2(0.f, 0.f);
+            },
+            [&](int i, float2 v) { twci[i] = v; });
         for (int kc0 = 0; kc0 < a.m2; kc0 += KC) {
             const int kc = min(KC, a.m2 - kc0);
             __syncthreads();
-            for (int i = tid; i < S2 * kc; i += kThreads) {
-                const int s = i / kc, k = i - s * kc;
-                const float2* src = s < a.m1 ? a.in1 + static_cast<size_t>(q) * a.ips + static_cast<size_t>(s) * a.irs
-                                             : a.in2 + static_cast<size_t>(q) * a.ips +
-                                                   static_cast<size_t>(s - a.m1) * a.irs;
-                Ys[s * KC + k] = src[kc0 + k];
-            }
-            if (!single_chunk) {
-                for (int i = tid; i < kc * W; i += kThreads)
-                    twri[i] = a.tw_row[static_cast<size_t>(kc0) * W + i];
-            }
+            batched_copy<8, float2>(
+                S2 * kc,
+                [&](int i) {
+                    const int s = i / kc, k = i - s * kc;
+                    const float2* src = s < a.m1 ? a.in1 + static_cast<size_t>(q) * a.ips + static_cast<size_t>(s) * a.irs
+                                                 : a.in2 + static_cast<size_t>(q) * a.ips +
+                                                       static_cast<size_t>(s - a.m1) * a.irs;
+                    return src[kc0 + k];
+                },
+                [&](int i, float2 v) {
+                    const int s = i / kc, k = i - s * kc;
+                    Ys[s * KC + k] = v;
+                });
+            if (!single_chunk)
+                batched_copy<8, float2>(
+                    kc * W, [&](int i) { return a.tw_row[static_cast<size_t>(kc0) * W + i]; },
+                    [&](int i, float2 v) { twri[i] = v; });
             __syncthreads();
             for (int o = tid; o < kRt * kc; o += kThreads) {
                 const int r = o / kc, k = o - r * kc;

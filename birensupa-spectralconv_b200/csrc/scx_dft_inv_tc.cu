@@ -129,14 +129,17 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
 
     // loaders: the spectra of one group, 8 consecutive ky per unit, in registers
     constexpr int kKB = C::R2P / 8;                                   // ky blocks per slot
-    constexpr int kUnitsPT = C::G4 * C::KSL * kKB / (kLoadWarps * 32);  // units per loader thread
-    static_assert(C::G4 * C::KSL * kKB % (kLoadWarps * 32) == 0, "loader split");
+    // loader warps: the first four, and in quadrant mode (twice the spectrum rows) the four E4
+    // warps as well, so that a thread's prefetched units stay in registers
+    constexpr int kLW = QUAD ? kLoadWarps + kE4Warps : kLoadWarps;
+    constexpr int kUnitsPT = C::G4 * C::KSL * kKB / (kLW * 32);  // units per loader thread
+    static_assert(C::G4 * C::KSL * kKB % (kLW * 32) == 0, "loader split");
     float2 v[kUnitsPT][8];
     auto load_group = [&](int t) {
         const int m1 = a.m1, m2 = a.m2, S = 2 * m1;
 #pragma unroll
         for (int u = 0; u < kUnitsPT; ++u) {
-            const int e = tid + u * kLoadWarps * 32;
+            const int e = tid + u * kLW * 32;
             const int kb = e % kKB, rest = e / kKB;
             const int ss = rest % C::KSL, p = rest / C::KSL;
             const int q = q0 + t * C::G4 + p;
@@ -151,7 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
         }
     };
     if (tid == 0) tc::grid_dep_launch();  // the next kernel's CTAs may start their prologue
-    if (warp < kLoadWarps && NG > 0) {
+    if (warp < kLW && NG > 0) {
         tc::grid_dep_wait();  // the spectra come from the previous kernel in the stream
         load_group(0);        // in flight during the setup below
     }
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
     }
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) {
-            tc::mbar_init(&bars.yFull[i], kLoadWarps);
+            tc::mbar_init(&bars.yFull[i], kLW);
             tc::mbar_init(&bars.yEmpty[i], 1);
             tc::mbar_init(&bars.d5Full[i], 1);
             tc::mbar_init(&bars.d5Empty[i], 1);
@@ -227,8 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
         return true;
     };
 
-    if (warp < kLoadWarps) {
-        // ------------------------------------------------------------ loaders
+    if (warp < kLW) {
+        // ------------------------------------------------------------ loaders (and E4)
         // Unit (p, s, kb) = 8 consecutive ky of slot s of group plane p feeds four 16-byte
         // vectors of Yr (MN-major, rows contiguous): rows (p, re, ky) at K = s [Y_re] and
         // K = 32 + s [-Y_im], rows (p, im, ky) at K = s [Y_im] and K = 32 + s [Y_re].
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
             uint8_t* yr_lo = yr_hi + C::YRB;
 #pragma unroll
             for (int u = 0; u < kUnitsPT; ++u) {
-                const int e = tid + u * kLoadWarps * 32;
+                const int e = tid + u * kLW * 32;
                 const int kb = e % kKB, rest = e / kKB;
                 const int ss = rest % C::KSL, p = rest / C::KSL;
                 uint32_t re_hi[4], re_lo[4], im_hi[4], im_lo[4];
@@ -268,9 +271,9 @@ __global__ void __launch_bounds__(kThreads, 1) dft_inv_tc_kernel(const InvArgs a
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&bars.yFull[yb]);
             if (t + 1 < NG) load_group(t + 1);
-            ok = e4(t, H / 2);
+            ok = e4(t, warp < kLoadWarps ? H / 2 : 0);
         }
-        if (!ok && lane == 0) atomicExch(a.watchdog, 30);
+        if (!ok && lane == 0) atomicExch(a.watchdog, warp < kLoadWarps ? 30 : 31);
     } else if (warp < kE5Warp0) {
         // ------------------------------------------------------------ E4 (lower half of h)
         bool ok = true;

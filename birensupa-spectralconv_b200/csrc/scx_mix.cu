@@ -50,14 +50,33 @@ __global__ void __launch_bounds__(kThreads) mix_smem_kernel(const MixArgs a) {
     const float2* __restrict__ Wt = a.w[corner];
     float2* __restrict__ Y = a.y[corner];
 
-    for (int idx = threadIdx.x; idx < B * Cin * tm; idx += kThreads) {
-        const int row = idx / tm, kk = idx - row * tm;
-        Xs[row * TM + kk] = __ldg(X + static_cast<size_t>(row) * NM + k0 + kk);
-    }
-    for (int idx = threadIdx.x; idx < Cin * Cout * tm; idx += kThreads) {
-        const int row = idx / tm, kk = idx - row * tm;
-        Ws[row * TM + kk] = __ldg(Wt + static_cast<size_t>(row) * NM + k0 + kk);
-    }
+    // staged in batches of 8 loads per thread before their stores, so that a batch is in flight
+    // at once (a load-store loop waits a full memory latency per element)
+    constexpr int LB = 8;
+    auto stage = [&](const float2* __restrict__ src, float2* dst, int nrow) {
+        const int n = nrow * tm;
+        for (int i0 = threadIdx.x; i0 < n; i0 += kThreads * LB) {
+            float2 v[LB];
+#pragma unroll
+            for (int u = 0; u < LB; ++u) {
+                const int i = i0 + u * kThreads;
+                if (i < n) {
+                    const int row = i / tm, kk = i - row * tm;
+                    v[u] = __ldg(src + static_cast<size_t>(row) * NM + k0 + kk);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < LB; ++u) {
+                const int i = i0 + u * kThreads;
+                if (i < n) {
+                    const int row = i / tm, kk = i - row * tm;
+                    dst[row * TM + kk] = v[u];
+                }
+            }
+        }
+    };
+    stage(X, Xs, B * Cin);
+    stage(Wt, Ws, Cin * Cout);
     __syncthreads();
 
     const int nog = (Cout + kOT - 1) / kOT;

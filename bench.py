@@ -648,7 +648,7 @@ def ours(args) -> None:
     res = run_spectral(args.workload, args.steps, warmup, device, world, rank, with_e2e=True,
                        with_breakdown=True, sampler_gpu=local_rank if rank == 0 else None)
     extras = {}
-    wanted = {"64", "256", "fno", "bwd"} if args.extras == "all" else set(args.extras.split(","))
+    wanted = {"64", "256", "irr", "c3s", "fno", "bwd"} if args.extras == "all" else set(args.extras.split(","))
     if not args.no_extras:
         for wname in EXTRA_WORKLOADS:
             if wname == args.workload or wname.split("_")[3].split("x")[0] not in wanted:

@@ -139,6 +139,7 @@ cudaError_t launch_unfold(const float* zs, float* y, int P, int Hs, int Ws, cuda
 // operands' alignment) falls back to those rules, so a table never makes a call fail.
 constexpr int kDftAuto = 0, kDftFfma = 1, kDftTensor = 2, kDftFolded = 3;
 constexpr int kMixAuto = -1, kMixSmem = 7;  // 0 .. 6: the TMA-ring tile shapes of scx_mix.cu
+constexpr int kMixTc = 8;                    // the tcgen05 3xTF32 kernel of scx_mix_tc.cu
 int dft_variant(int H, int W, int m1, int m2);
 int mix_variant(int ncorner, int B, int Cin, int Cout, int NM);
 
@@ -171,5 +172,12 @@ cudaError_t read_watchdog(int* value, bool reset);
 cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, const float2* w2,
                        float2* y1, float2* y2, int ncorner, int B, int Cin, int Cout, int NM,
                        cudaStream_t stream);
+
+// The same contraction on the tensor core (3xTF32), used where the variant table selects it
+// (variant kMixTc): B <= 16, Cin a multiple of 8, Cout a multiple of 64, an even mode count and
+// 16-byte aligned operands.  Returns cudaErrorNotSupported for anything else.
+bool mix_tc_supported(int B, int Cin, int Cout, int NM);
+cudaError_t launch_mix_tc(const float2* x1, const float2* x2, const float2* w1, const float2* w2, float2* y1,
+                          float2* y2, int ncorner, int B, int Cin, int Cout, int NM, cudaStream_t stream);
 
 }  // namespace scx

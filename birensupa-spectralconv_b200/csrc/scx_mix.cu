@@ -432,6 +432,14 @@ cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1
 cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, const float2* w2,
                        float2* y1, float2* y2, int ncorner, int B, int Cin, int Cout, int NM,
                        cudaStream_t stream) {
+    // The tensor-core kernel only where the variant table names it: with B <= 16 each weight
+    // element feeds 2B real products, and its conversion into tf32 operands costs more than the
+    // FFMA work it replaces (B16 C64 m32: 61 us against 45 us for the TMA-ring kernel).
+    const int forced = mix_variant(ncorner, B, Cin, Cout, NM);
+    if (forced == kMixTc) {
+        const cudaError_t ce = launch_mix_tc(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream);
+        if (ce != cudaErrorNotSupported) return ce;
+    }
     const cudaError_t te = launch_mix_ring(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream);
     if (te != cudaErrorNotSupported) return te;
     MixArgs a;

@@ -514,3 +514,65 @@ __device__ __forceinline__ float2 gelu_pair(float z0, float z1) {
 
 }  // namespace tc
 }  // namespace scx
+
+namespace scx {
+namespace tc {
+
+// Shared-memory descriptor of a K-major operand with the 32-byte swizzle: rows of 32 bytes
+// (8 tf32 values), 8-row groups 256 bytes apart (SBO), the two 16-byte halves of row r swapped
+// when (r / 4) is odd (address bit 4 ^= bit 7, so the base is 256-byte aligned).  One tf32 MMA
+// (K = 8) covers a whole row.  Layout type 6 = SWIZZLE_32B in the sm_100 descriptor format.
+__device__ __forceinline__ uint64_t desc_sw32(uint32_t saddr) {
+    uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1u) << 16;
+    d |= static_cast<uint64_t>(256u >> 4) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    d |= static_cast<uint64_t>(6u) << 61;
+    return d;
+}
+
+// Waits for the phase of parity `parity` with try_wait and no suspend-time hint (the thread
+// blocks in the instruction for a short system-dependent time and retries), for short
+// hand-offs where a suspended thread would wake late; gives up after ~2^31 SM cycles like
+// mbar_wait_bounded.
+__device__ __forceinline__ bool mbar_try_wait_nohint(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+    const long long start = clock64();
+    while (!mbar_try_wait_nohint(bar, parity)) {
+        if (clock64() - start > (1LL << 31)) return false;
+    }
+    return true;
+}
+
+// Byte offset of the 16-byte unit `half` (values 4*half .. 4*half + 3) of row r in a K-major
+// SW32 operand (see desc_sw32).
+__host__ __device__ __forceinline__ uint32_t sw32_offset(int r, int half) {
+    return static_cast<uint32_t>(r >> 3) * 256u + static_cast<uint32_t>(r & 7) * 32u +
+           (static_cast<uint32_t>(half ^ ((r >> 2) & 1)) << 4);
+}
+
+// 3-D tiled TMA store of a shared-memory box to (c0, c1, c2) of `tmap` (elements outside the
+// tensor are not written); completion tracked by the bulk-group of the issuing thread.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(tmap),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk store of this thread has finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+}  // namespace tc
+}  // namespace scx

@@ -61,7 +61,7 @@ int scx_set_dft_variant(int H, int W, int modes1, int modes2, int variant) {
 int scx_set_mix_variant(int ncorner, int batch_size, int channels_in, int channels_out, int modes, int variant) {
     if (ncorner < 1 || ncorner > 2 || batch_size <= 0 || channels_in <= 0 || channels_out <= 0 || modes <= 0)
         return cudaErrorInvalidValue;
-    if (variant < scx::kMixAuto || variant > scx::kMixSmem) return cudaErrorInvalidValue;
+    if (variant < scx::kMixAuto || variant > scx::kMixTc) return cudaErrorInvalidValue;
     std::lock_guard<std::mutex> lock(scx::g_mutex);
     const auto key = std::make_tuple(ncorner, batch_size, channels_in, channels_out, modes);
     if (variant == scx::kMixAuto)

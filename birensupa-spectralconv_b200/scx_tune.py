@@ -8,7 +8,8 @@ really differ for a shape, each timed on the device, and the table is persisted 
 
 * truncated DFTs, per (H, W, m1, m2): FFMA direct DFT, tensor-core kernels, or the folded
   tensor-core path (``scx_dft_variants`` says which apply);
-* mixing, per (corners, B, Cin, Cout, m1*m2): each TMA-ring tile shape or the per-thread kernel.
+* mixing, per (corners, B, Cin, Cout, m1*m2): each TMA-ring tile shape, the per-thread kernel
+  or the tensor-core (3xTF32) kernel.
 
 Every candidate is timed as the whole fused forward (CUDA graph of rotating input sets larger
 than L2, CUDA events) and its output is checked against the library's default choice before it
@@ -40,6 +41,7 @@ TABLE_ENV = "SCX_TUNE_TABLE"
 DFT_NAMES = {0: "auto", 1: "ffma", 2: "tensor", 3: "folded"}
 DFT_CODES = {v: k for k, v in DFT_NAMES.items()}
 MIX_SMEM = 7
+MIX_TC = 8  # the tcgen05 3xTF32 kernel (wide channel counts; other shapes fall back to the default)
 MIX_RING_SHAPES = 7  # tile shapes 0..6 of the TMA-ring mixing kernel
 L2_BYTES = 126 * 1024 * 1024
 TOL = 1e-5  # a variant may differ from the default choice only by rounding
@@ -174,7 +176,7 @@ def tune_spectral(x_cpu, w1, w2, c: dict, device, reps: int = 20, log=None) -> t
             best_dft, best_t = code, t
     lib.scx_set_dft_variant(H, W, m1, m2, best_dft)
     best_mix = -1
-    for v in list(range(MIX_RING_SHAPES)) + [MIX_SMEM]:
+    for v in list(range(MIX_RING_SHAPES)) + [MIX_SMEM, MIX_TC]:
         lib.scx_set_mix_variant(*mix_key, v)
         t = fwd.time_ms(reps)
         ok = _close(ref, fwd.output())

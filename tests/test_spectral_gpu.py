@@ -225,6 +225,54 @@ def test_dual_mix_shapes(shape, cuda_device):
         assert_close(torch.view_as_real(ref).numpy(), y.cpu().numpy(), 1e-5)
 
 
+@pytest.mark.parametrize("shape", [
+    (16, 64, 64, 32, 32),  # the 256x256 workload's mixing: B16, C64, 1024 modes per corner
+    (1, 8, 64, 3, 2),      # one batch item, one K step, 6 modes (a partial 4-mode tile)
+    (7, 24, 128, 5, 4),    # odd batch, two 64-channel output blocks, 20 modes
+    (8, 64, 64, 12, 12),   # N = 2B = 16 exactly
+    (9, 40, 64, 4, 5),     # 2B = 18 padded to 32 columns
+])
+def test_tensor_core_mix_vs_einsum(shape, cuda_device):
+    """The tcgen05 3xTF32 mixing (variant 8) against a complex128 einsum, every output written
+    (NaN-poisoned), bitwise repeatable, and not the FFMA kernel's result (so the tensor-core
+    kernel did run): both corners, then one corner."""
+    import _scx
+    import spectral_conv_ext
+
+    B, Cin, Cout, m1, m2 = shape
+    NM = m1 * m2
+    g = torch.Generator().manual_seed(7 * sum(shape))
+    xs = [torch.randn(B, Cin, m1, m2, dtype=torch.cfloat, generator=g) for _ in range(2)]
+    ws = [torch.randn(Cin, Cout, m1, m2, dtype=torch.cfloat, generator=g) for _ in range(2)]
+    xd = [torch.view_as_real(t.to(cuda_device)).contiguous() for t in xs]
+    wd = [torch.view_as_real(t.to(cuda_device)).contiguous() for t in ws]
+    lib = _scx.lib
+
+    def run(variant):
+        for nc in (1, 2):
+            assert lib.scx_set_mix_variant(nc, B, Cin, Cout, NM, variant) == 0
+        ys = [torch.full((B, Cout, m1, m2, 2), float("nan"), device=cuda_device) for _ in range(2)]
+        spectral_conv_ext.spectral_mul_dual_out(xd[0], wd[0], xd[1], wd[1], ys[0], ys[1])
+        single = spectral_conv_ext.spectral_mul(xd[1], wd[1])
+        torch.cuda.synchronize(cuda_device)
+        return ys, single
+
+    try:
+        ys, single = run(8)
+        ys_again, _ = run(8)
+        ffma, _ = run(7)
+    finally:
+        for nc in (1, 2):
+            lib.scx_set_mix_variant(nc, B, Cin, Cout, NM, -1)
+    for x, w, y, y2, yf in zip(xs, ws, ys, ys_again, ffma):
+        ref = torch.einsum("bixy,ioxy->boxy", x.to(torch.complex128), w.to(torch.complex128))
+        assert torch.isfinite(y).all()
+        assert_close(torch.view_as_real(ref).numpy(), y.cpu().numpy(), 1e-5)
+        assert torch.equal(y, y2)
+        assert not torch.equal(y, yf)
+    assert torch.equal(single, ys[1])
+
+
 def test_spectral_mul_autograd_grads(cuda_device):
     """spectral_conv_combo/test_backward.py:27-54 cases."""
     import spectral_conv_ops

@@ -35,7 +35,7 @@ def test_every_variant_matches_the_default(name, cuda_device):
                 got = _forward(x, w1, w2, c, cuda_device)
                 assert (got - ref).abs().max().item() <= 1e-5 * scale, code
         lib.scx_set_dft_variant(H, W, m1, m2, 0)
-        for v in range(scx_tune.MIX_RING_SHAPES + 1):
+        for v in list(range(scx_tune.MIX_RING_SHAPES + 1)) + [scx_tune.MIX_TC]:
             assert lib.scx_set_mix_variant(2, c["B"], c["Cin"], c["Cout"], m1 * m2, v) == 0
             got = _forward(x, w1, w2, c, cuda_device)
             assert (got - ref).abs().max().item() <= 1e-5 * scale, v

@@ -138,8 +138,8 @@ cudaError_t launch_unfold(const float* zs, float* y, int P, int Hs, int Ws, cuda
 // choice to the library's fixed rules.  A variant that does not apply to a shape (or to the
 // operands' alignment) falls back to those rules, so a table never makes a call fail.
 constexpr int kDftAuto = 0, kDftFfma = 1, kDftTensor = 2, kDftFolded = 3;
-constexpr int kMixAuto = -1, kMixSmem = 7;  // 0 .. 6: the TMA-ring tile shapes of scx_mix.cu
-constexpr int kMixTc = 8;                    // the tcgen05 3xTF32 kernel of scx_mix_tc.cu
+constexpr int kMixAuto = -1, kMixSmem = 8;  // 0 .. 7: the TMA-ring tile shapes of scx_mix.cu
+constexpr int kMixTc = 9;                    // the tcgen05 3xTF32 kernel of scx_mix_tc.cu
 int dft_variant(int H, int W, int m1, int m2);
 int mix_variant(int ncorner, int B, int Cin, int Cout, int NM);
 

@@ -284,8 +284,9 @@ struct RingCfg {
     int BT, OT, NBQ, NOQ, KS;
 };
 
+// the last shape takes one batch item per CTA (B = 1: a matrix-vector product per mode)
 const RingCfg kRingCands[] = {{5, 2, 4, 4, 2}, {5, 2, 4, 2, 4}, {4, 4, 4, 4, 2}, {4, 4, 4, 2, 4},
-                              {4, 2, 4, 4, 2}, {2, 2, 4, 4, 2}, {1, 2, 2, 4, 2}};
+                              {4, 2, 4, 4, 2}, {2, 2, 4, 4, 2}, {1, 2, 2, 4, 2}, {1, 2, 1, 8, 2}};
 constexpr int kNumRingCands = static_cast<int>(sizeof(kRingCands) / sizeof(kRingCands[0]));
 
 const void* ring_kernel(int ci) {
@@ -296,7 +297,8 @@ const void* ring_kernel(int ci) {
         case 3: return reinterpret_cast<const void*>(mix_ring_kernel<4, 4, 4, 2, 4>);
         case 4: return reinterpret_cast<const void*>(mix_ring_kernel<4, 2, 4, 4, 2>);
         case 5: return reinterpret_cast<const void*>(mix_ring_kernel<2, 2, 4, 4, 2>);
-        default: return reinterpret_cast<const void*>(mix_ring_kernel<1, 2, 2, 4, 2>);
+        case 6: return reinterpret_cast<const void*>(mix_ring_kernel<1, 2, 2, 4, 2>);
+        default: return reinterpret_cast<const void*>(mix_ring_kernel<1, 2, 1, 8, 2>);
     }
 }
 

@@ -40,9 +40,9 @@ import _scx  # noqa: E402
 TABLE_ENV = "SCX_TUNE_TABLE"
 DFT_NAMES = {0: "auto", 1: "ffma", 2: "tensor", 3: "folded"}
 DFT_CODES = {v: k for k, v in DFT_NAMES.items()}
-MIX_SMEM = 7
-MIX_TC = 8  # the tcgen05 3xTF32 kernel (wide channel counts; other shapes fall back to the default)
-MIX_RING_SHAPES = 7  # tile shapes 0..6 of the TMA-ring mixing kernel
+MIX_SMEM = 8
+MIX_TC = 9  # the tcgen05 3xTF32 kernel (wide channel counts; other shapes fall back to the default)
+MIX_RING_SHAPES = 8  # tile shapes 0..7 of the TMA-ring mixing kernel
 L2_BYTES = 126 * 1024 * 1024
 TOL = 1e-5  # a variant may differ from the default choice only by rounding
 MARGIN = 0.02  # a variant replaces the current best only when it is faster by more than this

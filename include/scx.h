@@ -257,8 +257,8 @@ int scx_fno2d_fwd(const scx_fno2d_config* cfg, const scx_fno2d_params* params, c
 int scx_dft_variants(int H, int W, int modes1, int modes2);
 int scx_set_dft_variant(int H, int W, int modes1, int modes2, int variant);
 /* Mixing variants for (corners, B, Cin, Cout, modes = m1*m2): -1 = the library's cost model
- * (FFMA kernels), 0..6 = one of the TMA-ring tile shapes, 7 = the per-thread shared-memory kernel,
- * 8 = the tcgen05 3xTF32 kernel (B <= 16, Cin a multiple of 8, Cout a multiple of 64, an even
+ * (FFMA kernels), 0..7 = one of the TMA-ring tile shapes, 8 = the per-thread shared-memory kernel,
+ * 9 = the tcgen05 3xTF32 kernel (B <= 16, Cin a multiple of 8, Cout a multiple of 64, an even
  * mode count, 16-byte aligned operands; other calls fall back to the library's choice). */
 int scx_set_mix_variant(int ncorner, int batch_size, int channels_in, int channels_out, int modes,
                         int variant);

@@ -151,9 +151,9 @@ def test_variant_table_round_trip(tmp_path):
     assert lib.scx_get_variant(0, 96, 160, 16, 20, 0) == 0
     assert lib.scx_get_variant(1, 2, 20, 32, 32, 256) == 3
     assert lib.scx_get_variant(1, 2, 20, 32, 32, 128) == -1
-    assert lib.scx_set_mix_variant(2, 20, 32, 32, 256, 9) == 1  # out of range
-    assert lib.scx_set_mix_variant(2, 20, 32, 32, 256, 8) == 0  # the tensor-core kernel
-    assert lib.scx_get_variant(1, 2, 20, 32, 32, 256) == 8
+    assert lib.scx_set_mix_variant(2, 20, 32, 32, 256, 10) == 1  # out of range
+    assert lib.scx_set_mix_variant(2, 20, 32, 32, 256, 9) == 0  # the tensor-core kernel
+    assert lib.scx_get_variant(1, 2, 20, 32, 32, 256) == 9
     assert lib.scx_set_mix_variant(2, 20, 32, 32, 256, 3) == 0
     assert lib.scx_set_dft_variant(64, 64, 12, 12, 0) == 0 and lib.scx_get_variant(0, 64, 64, 12, 12, 0) == 0
     lib.scx_clear_variants()

@@ -233,7 +233,7 @@ def test_dual_mix_shapes(shape, cuda_device):
     (9, 40, 64, 4, 5),     # 2B = 18 padded to 32 columns
 ])
 def test_tensor_core_mix_vs_einsum(shape, cuda_device):
-    """The tcgen05 3xTF32 mixing (variant 8) against a complex128 einsum, every output written
+    """The tcgen05 3xTF32 mixing (variant 9) against a complex128 einsum, every output written
     (NaN-poisoned), bitwise repeatable, and not the FFMA kernel's result (so the tensor-core
     kernel did run): both corners, then one corner."""
     import _scx
@@ -258,9 +258,9 @@ def test_tensor_core_mix_vs_einsum(shape, cuda_device):
         return ys, single
 
     try:
-        ys, single = run(8)
-        ys_again, _ = run(8)
-        ffma, _ = run(7)
+        ys, single = run(9)
+        ys_again, _ = run(9)
+        ffma, _ = run(8)  # the per-thread FFMA kernel
     finally:
         for nc in (1, 2):
             lib.scx_set_mix_variant(nc, B, Cin, Cout, NM, -1)

@@ -13,6 +13,8 @@
 // Zero padding is implicit and the 1/(HW) scale lives in the twiddles.
 #include <algorithm>
 
+#include <cooperative_groups.h>
+
 #include "scx_internal.h"
 
 namespace scx {
@@ -162,134 +164,170 @@ __global__ void __launch_bounds__(kThreads) dft_fwd_ffma_kernel(const FwdArgs a)
     }
 }
 
-// Register-tiled forward for the shapes the tensor-core kernels do not take (W <= kTileMaxW,
-// m2 <= 32, 2*m1 <= 64).  One CTA per (plane, ky tile); the ky range is split only as far as
-// needed for the grid to cover the SMs (a tile computes only its own stage-1 columns, so the
-// split adds no work; each tile reads its plane again, from L2).  Rows go in chunks of RC.
-//   stage 1  R[h][ky] = sum_w x[h][w] T[w][ky]  thread tile 4 rows x 2 ky, w in steps of 4:
-//            x as one 16-byte read per row, two complex twiddles per 16-byte read, 64 FMAs
-//            per 8 shared-memory reads
-//   stage 2  X[s][ky] += sum_h F[s][h] R[h][ky]  thread tile 2 slots x 2 ky, 16 FMAs per
-//            3 reads, accumulated over the chunks in registers
-// Per output the sums run over w, then over h, in order, as in dft_fwd_ffma_kernel.
-constexpr int kTileMaxW = 320;
-constexpr int kTileMaxRC = 128;
+// Row-split forward for the shapes the tensor-core kernels do not take (W <= kRowsMaxW,
+// m2 <= 32, 2*m1 <= 64).  A thread-block cluster of HB CTAs takes one plane and CTA r of it the
+// rows [r*RB, r*RB + RB), in chunks of RC rows, so a plane's work spreads over up to 8 SMs
+// (48 planes at 130 x 130 used to run as 48 CTAs).  Per chunk:
+//   stage 1  R[h][ky] = sum_w x[h][w] T[w][ky]   thread tile RT rows x 2 ky, w in steps of 4
+//            (one 16-byte read per row, two complex twiddles per 16-byte read); the w range is
+//            split over WS thread groups so that the small per-chunk tile count still fills the
+//            CTA, and their partial sums are added in group order.  RT = 1 (three CTAs per SM)
+//            where a chunk's row tiles fit the CTA's threads, RT = 4 (two CTAs per SM, four
+//            times the FMAs per shared-memory read) where they do not
+//   stage 2  Xp[s][ky] += sum_h F[s][h] R[h][ky]  thread tile 2 slots x 2 ky, kept in shared
+//            memory across the chunks (each element owned by one thread)
+// Then the cluster adds the CTAs' partial spectra Xp through distributed shared memory, rank
+// 0 first, each CTA finishing its share of the outputs.  Every sum runs in a fixed order, so
+// results are bitwise reproducible.  Row pitches are padded so that the rows a warp reads at
+// once fall in different banks (x: a pitch of an odd number of 16-byte units; F: an odd
+// number of 8-byte elements).
+constexpr int kRowsMaxW = 320;
+constexpr int kRowsMaxCluster = 8;
 
-struct TileArgs {
+struct RowsArgs {
     const float* x;
     float2* out1;
     float2* out2;
     long long ops;  // output plane stride (float2)
     int ors;        // output row stride (float2)
     int P, H, W, m1, m2;
-    int KPT;        // ky pairs per tile
-    int RC;         // rows per chunk (multiple of 4)
-    int WP;         // shared-memory row pitch of x (multiple of 4, >= W + 4 columns of zeros)
+    int RB;         // rows per CTA (the last CTA of a plane may hold fewer, or none)
+    int RC;         // rows per chunk (a multiple of the stage-1 row tile)
+    int WP;         // shared-memory row pitch of x (4 times an odd number, >= W, zero past W)
+    int WS, WR;     // stage-1 w splits, and the w range of each (a multiple of 4)
     const float2* tw_row;  // [W][m2]
     const float2* tw_col;  // [2 m1][H]
 };
 
-__global__ void __launch_bounds__(kThreads) dft_fwd_tile_kernel(const TileArgs a) {
+template <int RT>
+__global__ void __launch_bounds__(kThreads, RT == 1 ? 3 : 2) dft_fwd_rows_kernel(const RowsArgs a) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(16) unsigned char smem[];
     const int tid = threadIdx.x;
-    const int W = a.W, H = a.H, m2 = a.m2, S = 2 * a.m1, WP = a.WP, RC = a.RC, KPT = a.KPT;
-    const int K2 = 2 * KPT;       // ky per tile
-    const int SP = (S + 1) / 2;   // slot pairs
-    const int ky0 = blockIdx.y * K2;
-    float2* T = reinterpret_cast<float2*>(smem);          // [WP][K2], zero past W and m2
-    float2* F = T + WP * K2;                               // [2 SP][RC], zero past S and the chunk
-    float2* R = F + 2 * SP * RC;                           // [RC][K2]
-    float* xs = reinterpret_cast<float*>(R + RC * K2);     // [RC][WP], zero past W
+    const int W = a.W, H = a.H, m2 = a.m2, S = 2 * a.m1, WP = a.WP, RC = a.RC, WS = a.WS, WR = a.WR;
+    const int FP = RC + 1;                     // F row pitch (odd)
+    const int KP = (m2 + 1) / 2, K2 = 2 * KP;  // ky pairs, ky padded to pairs
+    const int SP = (S + 1) / 2, S2 = 2 * SP;   // slot pairs, slots padded to pairs
+    const int p = blockIdx.y;
+    const int rank = static_cast<int>(cluster.block_rank()), HB = static_cast<int>(cluster.num_blocks());
+    const int h0 = rank * a.RB;
+    const int my_rows = max(0, min(a.RB, H - h0));
+    float2* T = reinterpret_cast<float2*>(smem);       // [WP][K2], zero past W and m2
+    float2* F = T + WP * K2;                            // [S2][FP], zero past S and the chunk
+    float2* Rp = F + S2 * FP;                           // [WS][RC][K2] stage-1 partial sums
+    float2* R = WS > 1 ? Rp + WS * RC * K2 : Rp;        // [RC][K2] (the partial sums themselves if WS = 1)
+    float2* Xp = R + RC * K2;                           // [S2][K2] this CTA's partial spectrum
+    float* xs = reinterpret_cast<float*>(Xp + S2 * K2);  // [RC][WP], zero past W and the chunk
     batched_copy<8, float2>(
         WP * K2,
         [&](int i) {
             const int w = i / K2, k = i - w * K2;
-            return (w < W && ky0 + k < m2) ? a.tw_row[static_cast<size_t>(w) * m2 + ky0 + k] : make_float2(0.f, 0.f);
+            return (w < W && k < m2) ? a.tw_row[static_cast<size_t>(w) * m2 + k] : make_float2(0.f, 0.f);
         },
         [&](int i, float2 v) { T[i] = v; });
-    const int n1 = (RC / 4) * KPT;  // stage-1 threads
-    const int kp1 = tid % KPT, r0 = 4 * (tid / KPT);
-    const int n2 = SP * KPT;        // stage-2 threads
-    const int kp2 = tid % KPT, s0 = 2 * (tid / KPT);
-    for (int p = blockIdx.x; p < a.P; p += gridDim.x) {
-        float2 acc2[2][2];
+    for (int i = tid; i < S2 * K2; i += kThreads) Xp[i] = make_float2(0.f, 0.f);
+    const float* xp = a.x + static_cast<size_t>(p) * H * W;
+    const int RG = RC / RT;
+    for (int c0 = 0; c0 < my_rows; c0 += RC) {
+        const int rows = min(RC, my_rows - c0), hb = h0 + c0;
+        __syncthreads();  // the previous chunk's readers are done
+        batched_copy<16, float>(
+            RC * WP,
+            [&](int i) {
+                const int r = i / WP, c = i - r * WP;
+                return (r < rows && c < W) ? __ldcs(xp + static_cast<size_t>(hb + r) * W + c) : 0.f;
+            },
+            [&](int i, float v) { xs[i] = v; });
+        batched_copy<8, float2>(
+            S2 * FP,
+            [&](int i) {
+                const int sl = i / FP, r = i - sl * FP;
+                return (sl < S && r < rows) ? a.tw_col[static_cast<size_t>(sl) * H + hb + r] : make_float2(0.f, 0.f);
+            },
+            [&](int i, float2 v) { F[i] = v; });
+        __syncthreads();
+        for (int t = tid; t < RG * KP * WS; t += kThreads) {
+            const int kp = t % KP, rg = (t / KP) % RG, ws = t / (KP * RG);
+            const int r0 = RT * rg, w0 = ws * WR, w1 = min(WP, w0 + WR);
+            float2 acc[RT][2];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) acc2[i][0] = acc2[i][1] = make_float2(0.f, 0.f);
-        const float* xp = a.x + static_cast<size_t>(p) * H * W;
-        for (int h0 = 0; h0 < H; h0 += RC) {
-            const int rows = min(RC, H - h0);
-            __syncthreads();  // the previous chunk's readers are done
-            batched_copy<16, float>(
-                RC * WP,
-                [&](int i) {
-                    const int r = i / WP, c = i - r * WP;
-                    return (r < rows && c < W) ? __ldcs(xp + static_cast<size_t>(h0 + r) * W + c) : 0.f;
-                },
-                [&](int i, float v) { xs[i] = v; });
-            batched_copy<8, float2>(
-                2 * SP * RC,
-                [&](int i) {
-                    const int sl = i / RC, hh = i - sl * RC;
-                    return (sl < S && hh < rows) ? a.tw_col[static_cast<size_t>(sl) * H + h0 + hh] : make_float2(0.f, 0.f);
-                },
-                [&](int i, float2 v) { F[i] = v; });
-            __syncthreads();
-            if (tid < n1) {
-                float2 acc[4][2];
+            for (int i = 0; i < RT; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
+            for (int w = w0; w < w1; w += 4) {
+                float4 xv[RT];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
-                for (int w = 0; w < WP; w += 4) {
-                    float4 xv[4];
+                for (int i = 0; i < RT; ++i) xv[i] = *reinterpret_cast<const float4*>(xs + (r0 + i) * WP + w);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(xs + (r0 + i) * WP + w);
+                for (int u = 0; u < 4; ++u) {
+                    const float4 tv = *reinterpret_cast<const float4*>(T + (w + u) * K2 + 2 * kp);
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const float4 tv = *reinterpret_cast<const float4*>(T + (w + u) * K2 + 2 * kp1);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float xval = u == 0 ? xv[i].x : (u == 1 ? xv[i].y : (u == 2 ? xv[i].z : xv[i].w));
-                            acc[i][0].x = fmaf(xval, tv.x, acc[i][0].x);
-                            acc[i][0].y = fmaf(xval, tv.y, acc[i][0].y);
-                            acc[i][1].x = fmaf(xval, tv.z, acc[i][1].x);
-                            acc[i][1].y = fmaf(xval, tv.w, acc[i][1].y);
-                        }
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    *reinterpret_cast<float4*>(R + (r0 + i) * K2 + 2 * kp1) =
-                        make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
-            }
-            __syncthreads();
-            if (tid < n2) {
-                for (int hh = 0; hh < rows; ++hh) {
-                    const float4 rv = *reinterpret_cast<const float4*>(R + hh * K2 + 2 * kp2);
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        const float2 f = F[(s0 + i) * RC + hh];
-                        acc2[i][0].x = fmaf(f.x, rv.x, fmaf(-f.y, rv.y, acc2[i][0].x));
-                        acc2[i][0].y = fmaf(f.x, rv.y, fmaf(f.y, rv.x, acc2[i][0].y));
-                        acc2[i][1].x = fmaf(f.x, rv.z, fmaf(-f.y, rv.w, acc2[i][1].x));
-                        acc2[i][1].y = fmaf(f.x, rv.w, fmaf(f.y, rv.z, acc2[i][1].y));
+                    for (int i = 0; i < RT; ++i) {
+                        const float xval = u == 0 ? xv[i].x : (u == 1 ? xv[i].y : (u == 2 ? xv[i].z : xv[i].w));
+                        acc[i][0].x = fmaf(xval, tv.x, acc[i][0].x);
+                        acc[i][0].y = fmaf(xval, tv.y, acc[i][0].y);
+                        acc[i][1].x = fmaf(xval, tv.z, acc[i][1].x);
+                        acc[i][1].y = fmaf(xval, tv.w, acc[i][1].y);
                     }
                 }
             }
+#pragma unroll
+            for (int i = 0; i < RT; ++i)
+                *reinterpret_cast<float4*>(Rp + (ws * RC + r0 + i) * K2 + 2 * kp) =
+                    make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
         }
-        if (tid < n2) {
-#pragma unroll
-            for (int i = 0; i < 2; ++i)
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int sl = s0 + i, ky = ky0 + 2 * kp2 + j;
-                    if (sl < S && ky < m2) {
-                        float2* dst = sl < a.m1 ? a.out1 + static_cast<size_t>(p) * a.ops + static_cast<size_t>(sl) * a.ors
-                                                : a.out2 + static_cast<size_t>(p) * a.ops +
-                                                      static_cast<size_t>(sl - a.m1) * a.ors;
-                        dst[ky] = acc2[i][j];
-                    }
+        __syncthreads();
+        if (WS > 1) {
+            for (int i = tid; i < RC * KP; i += kThreads) {
+                const int r = i / KP, kp = i - r * KP;
+                float4 v = *reinterpret_cast<const float4*>(Rp + r * K2 + 2 * kp);
+                for (int ws = 1; ws < WS; ++ws) {
+                    const float4 u = *reinterpret_cast<const float4*>(Rp + (ws * RC + r) * K2 + 2 * kp);
+                    v.x += u.x;
+                    v.y += u.y;
+                    v.z += u.z;
+                    v.w += u.w;
                 }
+                *reinterpret_cast<float4*>(R + r * K2 + 2 * kp) = v;
+            }
+            __syncthreads();
+        }
+        for (int t = tid; t < SP * KP; t += kThreads) {
+            const int kp = t % KP, s0 = 2 * (t / KP);
+            float4 acc2[2];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) acc2[i] = *reinterpret_cast<const float4*>(Xp + (s0 + i) * K2 + 2 * kp);
+            for (int r = 0; r < rows; ++r) {
+                const float4 rv = *reinterpret_cast<const float4*>(R + r * K2 + 2 * kp);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const float2 f = F[(s0 + i) * FP + r];
+                    acc2[i].x = fmaf(f.x, rv.x, fmaf(-f.y, rv.y, acc2[i].x));
+                    acc2[i].y = fmaf(f.x, rv.y, fmaf(f.y, rv.x, acc2[i].y));
+                    acc2[i].z = fmaf(f.x, rv.z, fmaf(-f.y, rv.w, acc2[i].z));
+                    acc2[i].w = fmaf(f.x, rv.w, fmaf(f.y, rv.z, acc2[i].w));
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 2; ++i) *reinterpret_cast<float4*>(Xp + (s0 + i) * K2 + 2 * kp) = acc2[i];
         }
     }
+    cluster.sync();  // every CTA's partial spectrum is complete and visible cluster-wide
+    const int n = S * m2;
+    const int o_begin = static_cast<int>(static_cast<long long>(n) * rank / HB);
+    const int o_end = static_cast<int>(static_cast<long long>(n) * (rank + 1) / HB);
+    for (int o = o_begin + tid; o < o_end; o += kThreads) {
+        const int sl = o / m2, ky = o - sl * m2;
+        float2 sum = make_float2(0.f, 0.f);
+        for (int q = 0; q < HB; ++q) {
+            const float2 v = cluster.map_shared_rank(Xp, q)[sl * K2 + ky];
+            sum.x += v.x;
+            sum.y += v.y;
+        }
+        float2* dst = sl < a.m1 ? a.out1 + static_cast<size_t>(p) * a.ops + static_cast<size_t>(sl) * a.ors
+                                : a.out2 + static_cast<size_t>(p) * a.ops + static_cast<size_t>(sl - a.m1) * a.ors;
+        dst[ky] = sum;
+    }
+    cluster.sync();  // no CTA leaves while another still reads its partial spectrum
 }
 
 struct InvArgs {
@@ -418,8 +456,8 @@ __global__ void __launch_bounds__(kThreads) dft_inv_ffma_kernel(const InvArgs a)
 cudaError_t launch_dft_fwd(const float* x, float2* out1, float2* out2, long long out_plane_stride,
                            int out_row_stride, int P, int H, int W, int m1, int m2, const Twiddles& tw,
                            cudaStream_t stream) {
-    if (W <= kTileMaxW && m2 <= 32 && 2 * m1 <= 64) {
-        TileArgs t;
+    if (W <= kRowsMaxW && m2 <= 32 && 2 * m1 <= 64) {
+        RowsArgs t;
         t.x = x;
         t.out1 = out1;
         t.out2 = out2;
@@ -432,34 +470,57 @@ cudaError_t launch_dft_fwd(const float* x, float2* out1, float2* out2, long long
         t.m2 = m2;
         t.tw_row = tw.row_fwd;
         t.tw_col = tw.col_fwd;
-        t.WP = (W + 3) / 4 * 4 + 4;
-        const int KP = (m2 + 1) / 2, SP = m1;  // ky pairs, slot pairs (2 m1 slots)
-        // ky tiles: as few as give the grid one CTA per SM (or all of them)
-        int ntile = 1;
-        while (ntile < KP && static_cast<long long>(P) * ntile < num_sms()) ++ntile;
-        t.KPT = (KP + ntile - 1) / ntile;
-        ntile = (KP + t.KPT - 1) / t.KPT;
-        // rows per chunk: enough for every thread in stage 1, within the shared-memory budget
-        int RC = std::min({4 * (kThreads / t.KPT), (H + 3) / 4 * 4, kTileMaxRC});
-        const int K2 = 2 * t.KPT;
-        auto smem_of = [&](int rc) {
-            return static_cast<size_t>(t.WP) * K2 * 8 + static_cast<size_t>(2 * SP) * rc * 8 +
-                   static_cast<size_t>(rc) * K2 * 8 + static_cast<size_t>(rc) * t.WP * 4;
+        t.WP = (W + 3) / 4 * 4;
+        if ((t.WP / 4) % 2 == 0) t.WP += 4;  // an odd number of 16-byte units per row
+        const int KP = (m2 + 1) / 2, K2 = 2 * KP, S2 = 2 * m1;
+        // One-row tiles with three CTAs per SM (about three per SM over the whole batch) where a
+        // chunk's tiles fit the CTA's threads; else four-row tiles with two CTAs per SM, as many
+        // CTAs per plane as fit one such wave.  At least 8 rows per CTA.
+        const int hb_cap = std::min(kRowsMaxCluster, (H + 7) / 8);
+        int HB = std::max(1, std::min(hb_cap, static_cast<int>((2LL * num_sms() + P - 1) / P)));
+        int RT = 1;
+        if (((H + HB - 1) / HB) * KP > kThreads) {
+            RT = 4;
+            HB = std::max(1, std::min(hb_cap, static_cast<int>(2LL * num_sms() / P)));
+        }
+        t.RB = (H + HB - 1) / HB;
+        auto smem_of = [&](int rc, int ws) {
+            return (static_cast<size_t>(t.WP) * K2 + static_cast<size_t>(S2) * (rc + 1) +
+                    static_cast<size_t>(ws + (ws > 1 ? 1 : 0)) * rc * K2 + static_cast<size_t>(S2) * K2) * 8 +
+                   static_cast<size_t>(rc) * t.WP * 4;
         };
-        // two CTAs per SM when the chunk can shrink to fit (at least 32 rows), else one
-        int rc2 = RC;
-        while (smem_of(rc2) > static_cast<size_t>(kSmemBudget) / 2 && rc2 > 32) rc2 -= 4;
-        if (smem_of(rc2) <= static_cast<size_t>(kSmemBudget) / 2) RC = rc2;
-        while (smem_of(RC) > static_cast<size_t>(kSmemBudget) && RC > 4) RC -= 4;
+        int RC = (t.RB + RT - 1) / RT * RT;
+        // w splits: as many as keep the stage-1 tiles within the CTA's threads, 16 columns each at least
+        auto splits = [&](int rc) {
+            const int tiles = (rc / RT) * KP;
+            return std::max(1, std::min({8, kThreads / tiles, t.WP / 16}));
+        };
+        while (smem_of(RC, splits(RC)) > static_cast<size_t>(kSmemBudget) / (RT == 1 ? 3 : 2) && RC > 4 * RT)
+            RC -= RT;
         t.RC = RC;
-        const size_t smem = smem_of(RC);
-        if (smem <= static_cast<size_t>(kSmemBudget) && SP * t.KPT <= kThreads) {
-            int per_sm = 1;
-            cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(dft_fwd_tile_kernel), smem, kThreads, &per_sm);
-            if (e != cudaSuccess) return e;
-            const int gx = std::max(1, std::min(P, (per_sm * num_sms() + ntile - 1) / ntile));
-            dft_fwd_tile_kernel<<<dim3(gx, ntile), kThreads, smem, stream>>>(t);
-            return cudaGetLastError();
+        t.WS = splits(RC);
+        t.WR = (t.WP / 4 + t.WS - 1) / t.WS * 4;
+        const size_t smem = smem_of(RC, t.WS);
+        if (smem <= static_cast<size_t>(kSmemBudget) / 2) {
+            auto launch = [&](auto kernel) -> cudaError_t {
+                int per_sm = 1;
+                cudaError_t e = prepare_kernel(reinterpret_cast<const void*>(kernel), smem, kThreads, &per_sm);
+                if (e != cudaSuccess) return e;
+                cudaLaunchConfig_t lc = {};
+                lc.gridDim = dim3(HB, P);
+                lc.blockDim = dim3(kThreads);
+                lc.dynamicSmemBytes = smem;
+                lc.stream = stream;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = HB;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                lc.attrs = attr;
+                lc.numAttrs = 1;
+                return cudaLaunchKernelEx(&lc, kernel, t);
+            };
+            return RT == 4 ? launch(dft_fwd_rows_kernel<4>) : launch(dft_fwd_rows_kernel<1>);
         }
     }
     FwdArgs a;

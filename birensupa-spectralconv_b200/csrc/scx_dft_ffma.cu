@@ -342,78 +342,107 @@ struct InvArgs {
     const float2* tw_row;  // [m2][W]
 };
 
-// grid = persistent over (plane, 32-row tile).  In stage 5 a thread owns a register block of
-// RB rows x CB columns: rows RB*rg .. RB*rg + RB - 1 and columns c, c + NC, ..., c + (CB-1) NC
-// with NC = ceil(W / CB) and thread = rg * NC + c, so one ky step reads CB twiddles and RB
-// spectrum values (broadcast) for RB*CB*2 FMAs; consecutive threads take consecutive columns
-// (conflict-free twiddle reads, coalesced stores).  Needs NC * (kRt / RB) <= kThreads.
+// grid = persistent over (plane, 32-row tile).
+// Stage 4: thread tile 2 rows x 2 ky over the slots (16 FMAs per three shared-memory reads);
+// the twiddle rows have an odd pitch, so a warp's row pairs fall in different banks.
+// Stage 5 uses the symmetry of the row twiddles: E[ky][W-w] = conj(E[ky][w]), so with
+// A = sum_ky Zr Er and B = sum_ky Zi Ei over one pass, y[w] = A - B and y[W-w] = A + B
+// (w = 0 and w = W/2 are their own partners).  A thread owns a register block of RB rows x
+// CB column pairs: rows RB*rg .. RB*rg + RB - 1 and pairs c, c + NC, ..., c + (CB-1) NC with
+// NC = ceil(NPW / CB), NPW = W/2 + 1, thread = rg * NC + c, so one ky step reads CB twiddles
+// and RB spectrum values (broadcast) for 2*RB*CB FMAs covering 2*RB*CB outputs; consecutive
+// threads take consecutive columns (conflict-free twiddle reads, coalesced stores).  Needs
+// NC * (kRt / RB) <= kThreads.
 template <int RB, int CB>
 __global__ void __launch_bounds__(kThreads) dft_inv_ffma_kernel(const InvArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int tid = threadIdx.x;
     const int S2 = 2 * a.m1, KC = a.KC, W = a.W, H = a.H;
-    float2* Ys = reinterpret_cast<float2*>(smem);  // [S2][KC]
-    float2* twci = Ys + S2 * KC;                    // [kRt][S2]
-    float2* twri = twci + kRt * S2;                 // [KC][W]
-    float2* Zs = twri + KC * W;                     // [kRt][KC]
+    const int GP = S2 + 1;                // twiddle row pitch (odd)
+    constexpr int ZP = kRt + 1;           // Zs row pitch (odd)
+    const int KCP = (KC + 1) / 2 * 2;     // spectrum row pitch (pairs)
+    const int NPW = W / 2 + 1;            // column pairs
+    // Ys, read as 16-byte vectors, first (its size is a multiple of 16 bytes, an even pitch)
+    float2* Ys = reinterpret_cast<float2*>(smem);  // [S2][KCP], zero past kc
+    float2* twci = Ys + S2 * KCP;                   // [kRt][GP]
+    float2* Zs = twci + kRt * GP;                   // [KCP][ZP] (ky-major: a warp's row groups in different banks)
+    float2* twri = Zs + KCP * ZP;                   // [KC][NPW]
 
     const bool single_chunk = KC >= a.m2;
     if (single_chunk)
-        batched_copy<8, float2>(a.m2 * W, [&](int i) { return a.tw_row[i]; }, [&](int i, float2 v) { twri[i] = v; });
+        batched_copy<8, float2>(
+            a.m2 * NPW,
+            [&](int i) {
+                const int k = i / NPW, w = i - k * NPW;
+                return a.tw_row[static_cast<size_t>(k) * W + w];
+            },
+            [&](int i, float2 v) { twri[i] = v; });
     const int tpp = (H + kRt - 1) / kRt;
     const int ntiles = a.Q * tpp;
-    const int NC = (W + CB - 1) / CB;
+    const int NC = (NPW + CB - 1) / CB;
     const int my_c = tid % NC, my_rg = tid / NC;
     const bool active = my_rg < kRt / RB;  // warp-uniform except in the warp that straddles the end
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
         const int q = t / tpp;
         const int h0 = (t - q * tpp) * kRt;
         const int rows = min(kRt, H - h0);
-        float acc[RB][CB];
+        float accA[RB][CB], accB[RB][CB];
 #pragma unroll
         for (int r = 0; r < RB; ++r)
 #pragma unroll
-            for (int j = 0; j < CB; ++j) acc[r][j] = 0.f;
+            for (int j = 0; j < CB; ++j) accA[r][j] = accB[r][j] = 0.f;
         __syncthreads();
         batched_copy<8, float2>(
-            kRt * S2,
+            kRt * GP,
             [&](int i) {
-                const int r = i / S2, s = i - r * S2;
-                return r < rows ? a.tw_col[static_cast<size_t>(h0 + r) * S2 + s] : make_float2(0.f, 0.f);
+                const int r = i / GP, s = i - r * GP;
+                return (r < rows && s < S2) ? a.tw_col[static_cast<size_t>(h0 + r) * S2 + s] : make_float2(0.f, 0.f);
             },
             [&](int i, float2 v) { twci[i] = v; });
         for (int kc0 = 0; kc0 < a.m2; kc0 += KC) {
             const int kc = min(KC, a.m2 - kc0);
+            const int kpc = (kc + 1) / 2;
             __syncthreads();
             batched_copy<8, float2>(
-                S2 * kc,
+                S2 * KCP,
                 [&](int i) {
-                    const int s = i / kc, k = i - s * kc;
+                    const int s = i / KCP, k = i - s * KCP;
+                    if (k >= kc) return make_float2(0.f, 0.f);
                     const float2* src = s < a.m1 ? a.in1 + static_cast<size_t>(q) * a.ips + static_cast<size_t>(s) * a.irs
                                                  : a.in2 + static_cast<size_t>(q) * a.ips +
                                                        static_cast<size_t>(s - a.m1) * a.irs;
                     return src[kc0 + k];
                 },
-                [&](int i, float2 v) {
-                    const int s = i / kc, k = i - s * kc;
-                    Ys[s * KC + k] = v;
-                });
+                [&](int i, float2 v) { Ys[i] = v; });
             if (!single_chunk)
                 batched_copy<8, float2>(
-                    kc * W, [&](int i) { return a.tw_row[static_cast<size_t>(kc0) * W + i]; },
+                    kc * NPW,
+                    [&](int i) {
+                        const int k = i / NPW, w = i - k * NPW;
+                        return a.tw_row[static_cast<size_t>(kc0 + k) * W + w];
+                    },
                     [&](int i, float2 v) { twri[i] = v; });
             __syncthreads();
-            for (int o = tid; o < kRt * kc; o += kThreads) {
-                const int r = o / kc, k = o - r * kc;
-                const float2* tc = twci + r * S2;
-                float2 z = make_float2(0.f, 0.f);
+            for (int o = tid; o < (kRt / 2) * kpc; o += kThreads) {
+                const int kp = o % kpc, r0 = 2 * (o / kpc);
+                float4 z[2];
+                z[0] = z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
                 for (int s = 0; s < S2; ++s) {
-                    const float2 tv = tc[s];
-                    const float2 v = Ys[s * KC + k];
-                    z.x = fmaf(tv.x, v.x, fmaf(-tv.y, v.y, z.x));
-                    z.y = fmaf(tv.x, v.y, fmaf(tv.y, v.x, z.y));
+                    const float4 v = *reinterpret_cast<const float4*>(Ys + s * KCP + 2 * kp);
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const float2 g = twci[(r0 + i) * GP + s];
+                        z[i].x = fmaf(g.x, v.x, fmaf(-g.y, v.y, z[i].x));
+                        z[i].y = fmaf(g.x, v.y, fmaf(g.y, v.x, z[i].y));
+                        z[i].z = fmaf(g.x, v.z, fmaf(-g.y, v.w, z[i].z));
+                        z[i].w = fmaf(g.x, v.w, fmaf(g.y, v.z, z[i].w));
+                    }
                 }
-                Zs[r * KC + k] = z;
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    Zs[(2 * kp) * ZP + r0 + i] = make_float2(z[i].x, z[i].y);
+                    Zs[(2 * kp + 1) * ZP + r0 + i] = make_float2(z[i].z, z[i].w);
+                }
             }
             __syncthreads();
             if (active) {
@@ -422,14 +451,16 @@ __global__ void __launch_bounds__(kThreads) dft_inv_ffma_kernel(const InvArgs a)
 #pragma unroll
                     for (int j = 0; j < CB; ++j) {
                         const int w = my_c + j * NC;
-                        tw[j] = w < W ? twri[k * W + w] : make_float2(0.f, 0.f);
+                        tw[j] = w < NPW ? twri[k * NPW + w] : make_float2(0.f, 0.f);
                     }
 #pragma unroll
                     for (int r = 0; r < RB; ++r) {
-                        const float2 z = Zs[(my_rg * RB + r) * KC + k];
+                        const float2 z = Zs[k * ZP + my_rg * RB + r];
 #pragma unroll
-                        for (int j = 0; j < CB; ++j)
-                            acc[r][j] = fmaf(z.x, tw[j].x, fmaf(-z.y, tw[j].y, acc[r][j]));
+                        for (int j = 0; j < CB; ++j) {
+                            accA[r][j] = fmaf(z.x, tw[j].x, accA[r][j]);
+                            accB[r][j] = fmaf(z.y, tw[j].y, accB[r][j]);
+                        }
                     }
                 }
             }
@@ -443,7 +474,11 @@ __global__ void __launch_bounds__(kThreads) dft_inv_ffma_kernel(const InvArgs a)
 #pragma unroll
                     for (int j = 0; j < CB; ++j) {
                         const int w = my_c + j * NC;
-                        if (w < W) __stcs(yp + static_cast<size_t>(row) * W + w, acc[r][j]);
+                        if (w < NPW && 2 * w <= W) {
+                            __stcs(yp + static_cast<size_t>(row) * W + w, accA[r][j] - accB[r][j]);
+                            if (w > 0 && 2 * w < W)
+                                __stcs(yp + static_cast<size_t>(row) * W + (W - w), accA[r][j] + accB[r][j]);
+                        }
                     }
                 }
             }
@@ -589,14 +624,18 @@ cudaError_t launch_dft_inv(const float2* in1, const float2* in2, long long in_pl
     a.m2 = m2;
     a.tw_col = tw.col_inv;
     a.tw_row = tw.row_inv;
-    const int S2 = 2 * m1;
-    const long long fixed = static_cast<long long>(kRt) * S2 * 8;
-    const long long per_k = static_cast<long long>(S2) * 8 + static_cast<long long>(W) * 8 + kRt * 8;
-    long long KC = (kSmemBudget - fixed) / per_k;
-    if (KC < 1) return cudaErrorInvalidValue;
-    KC = std::min<long long>(KC, m2);
+    const int S2 = 2 * m1, NPW = W / 2 + 1;
+    // shared memory: Ys [S2][KCP] + twci [kRt][S2+1] + Zs [KCP][kRt+1] + twri [KC][NPW], KCP = KC
+    // rounded up to even
+    auto smem_of = [&](long long kc) {
+        const long long kcp = (kc + 1) / 2 * 2;
+        return static_cast<size_t>(S2 * kcp + kRt * (S2 + 1LL) + kcp * (kRt + 1LL) + kc * NPW) * 8;
+    };
+    long long KC = std::max<long long>(1, m2);
+    while (KC > 1 && smem_of(KC) > static_cast<size_t>(kSmemBudget)) --KC;
+    if (smem_of(KC) > static_cast<size_t>(kSmemBudget)) return cudaErrorInvalidValue;
     a.KC = static_cast<int>(KC);
-    const size_t smem = static_cast<size_t>(fixed + per_k * KC);
+    const size_t smem = smem_of(KC);
     const int tiles = Q * ((H + kRt - 1) / kRt);
     auto run = [&](auto kernel) -> cudaError_t {
         int per_sm = 1;
@@ -608,10 +647,11 @@ cudaError_t launch_dft_inv(const float2* in1, const float2* in2, long long in_pl
     };
     // the register block with the most threads busy (at most kThreads) and, among equals, the
     // most FMAs per shared-memory read; wide planes fall back to all 32 rows per thread
-    auto threads_for = [&](int rb, int cb) { return ((W + cb - 1) / cb) * (kRt / rb); };
+    auto threads_for = [&](int rb, int cb) { return ((NPW + cb - 1) / cb) * (kRt / rb); };
     if (threads_for(4, 2) <= kThreads) return run(dft_inv_ffma_kernel<4, 2>);
-    const int t82 = threads_for(8, 2), t84 = threads_for(8, 4);
-    if (t82 <= kThreads && (t84 > kThreads || t82 > t84)) return run(dft_inv_ffma_kernel<8, 2>);
+    const int t82 = threads_for(8, 2), t44 = threads_for(4, 4), t84 = threads_for(8, 4);
+    if (t82 <= kThreads && t82 >= t44) return run(dft_inv_ffma_kernel<8, 2>);
+    if (t44 <= kThreads) return run(dft_inv_ffma_kernel<4, 4>);
     if (t84 <= kThreads) return run(dft_inv_ffma_kernel<8, 4>);
     if (threads_for(16, 4) <= kThreads) return run(dft_inv_ffma_kernel<16, 4>);
     if (threads_for(kRt, 1) <= kThreads) return run(dft_inv_ffma_kernel<kRt, 1>);

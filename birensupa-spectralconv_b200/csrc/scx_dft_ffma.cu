@@ -168,8 +168,12 @@ __global__ void __launch_bounds__(kThreads) dft_fwd_ffma_kernel(const FwdArgs a)
 // m2 <= 32, 2*m1 <= 64).  A thread-block cluster of HB CTAs takes one plane and CTA r of it the
 // rows [r*RB, r*RB + RB), in chunks of RC rows, so a plane's work spreads over up to 8 SMs
 // (48 planes at 130 x 130 used to run as 48 CTAs).  Per chunk:
-//   stage 1  R[h][ky] = sum_w x[h][w] T[w][ky]   thread tile RT rows x 2 ky, w in steps of 4
-//            (one 16-byte read per row, two complex twiddles per 16-byte read); the w range is
+//   stage 1  R[h][ky] = sum_w x[h][w] T[w][ky] from the symmetry T[W-w] = conj(T[w]): with
+//            u[w] = x[w] + x[W-w] and v[w] = x[w] - x[W-w] for 0 < w < W/2 (u = x, v = 0 at
+//            w = 0 and W/2), Re R = sum u Re T and Im R = sum v Im T over w <= W/2, half the
+//            FMAs and twiddles of the direct sum.  The chunk is stored as u and v rows.
+//            Thread tile RT rows x 2 ky, w in steps of 4 (16-byte reads of u and v per row, two
+//            complex twiddles per 16-byte read); the w range is
 //            split over WS thread groups so that the small per-chunk tile count still fills the
 //            CTA, and their partial sums are added in group order.  RT = 1 (three CTAs per SM)
 //            where a chunk's row tiles fit the CTA's threads, RT = 4 (two CTAs per SM, four
@@ -193,7 +197,7 @@ struct RowsArgs {
     int P, H, W, m1, m2;
     int RB;         // rows per CTA (the last CTA of a plane may hold fewer, or none)
     int RC;         // rows per chunk (a multiple of the stage-1 row tile)
-    int WP;         // shared-memory row pitch of x (4 times an odd number, >= W, zero past W)
+    int WP;         // shared-memory row pitch of u and v (4 times an odd number, >= W/2 + 1, zero past it)
     int WS, WR;     // stage-1 w splits, and the w range of each (a multiple of 4)
     const float2* tw_row;  // [W][m2]
     const float2* tw_col;  // [2 m1][H]
@@ -213,7 +217,8 @@ __global__ void __launch_bounds__(kThreads, RT == 1 ? 3 : 2) dft_fwd_rows_kernel
     const int rank = static_cast<int>(cluster.block_rank()), HB = static_cast<int>(cluster.num_blocks());
     const int h0 = rank * a.RB;
     const int my_rows = max(0, min(a.RB, H - h0));
-    float2* T = reinterpret_cast<float2*>(smem);       // [WP][K2], zero past W and m2
+    const int NPW = W / 2 + 1;                          // w = 0 .. W/2
+    float2* T = reinterpret_cast<float2*>(smem);       // [WP][K2], zero past NPW and m2
     float2* F = T + WP * K2;                            // [S2][FP], zero past S and the chunk
     float2* Rp = F + S2 * FP;                           // [WS][RC][K2] stage-1 partial sums
     float2* R = WS > 1 ? Rp + WS * RC * K2 : Rp;        // [RC][K2] (the partial sums themselves if WS = 1)
@@ -223,22 +228,33 @@ __global__ void __launch_bounds__(kThreads, RT == 1 ? 3 : 2) dft_fwd_rows_kernel
         WP * K2,
         [&](int i) {
             const int w = i / K2, k = i - w * K2;
-            return (w < W && k < m2) ? a.tw_row[static_cast<size_t>(w) * m2 + k] : make_float2(0.f, 0.f);
+            return (w < NPW && k < m2) ? a.tw_row[static_cast<size_t>(w) * m2 + k] : make_float2(0.f, 0.f);
         },
         [&](int i, float2 v) { T[i] = v; });
     for (int i = tid; i < S2 * K2; i += kThreads) Xp[i] = make_float2(0.f, 0.f);
+    float* vs = xs + RC * WP;                           // [RC][WP]: v rows (xs holds the u rows)
     const float* xp = a.x + static_cast<size_t>(p) * H * W;
     const int RG = RC / RT;
     for (int c0 = 0; c0 < my_rows; c0 += RC) {
         const int rows = min(RC, my_rows - c0), hb = h0 + c0;
         __syncthreads();  // the previous chunk's readers are done
-        batched_copy<16, float>(
+        batched_copy<8, float2>(
             RC * WP,
             [&](int i) {
+                // both samples loaded unconditionally (a self-partner column loads itself twice), so
+                // the batch's loads are all in flight before any is used
                 const int r = i / WP, c = i - r * WP;
-                return (r < rows && c < W) ? __ldcs(xp + static_cast<size_t>(hb + r) * W + c) : 0.f;
+                if (r >= rows || c >= NPW) return make_float2(0.f, 0.f);
+                const float* row = xp + static_cast<size_t>(hb + r) * W;
+                const int c1 = c == 0 ? 0 : W - c;
+                return make_float2(__ldcs(row + c), __ldcs(row + c1));
             },
-            [&](int i, float v) { xs[i] = v; });
+            [&](int i, float2 x2) {
+                const int c = i % WP;
+                const bool self = c == 0 || 2 * c == W;
+                xs[i] = self ? x2.x : x2.x + x2.y;
+                vs[i] = self ? 0.f : x2.x - x2.y;
+            });
         batched_copy<8, float2>(
             S2 * FP,
             [&](int i) {
@@ -254,19 +270,23 @@ __global__ void __launch_bounds__(kThreads, RT == 1 ? 3 : 2) dft_fwd_rows_kernel
 #pragma unroll
             for (int i = 0; i < RT; ++i) acc[i][0] = acc[i][1] = make_float2(0.f, 0.f);
             for (int w = w0; w < w1; w += 4) {
-                float4 xv[RT];
+                float4 uv[RT], vv[RT];
 #pragma unroll
-                for (int i = 0; i < RT; ++i) xv[i] = *reinterpret_cast<const float4*>(xs + (r0 + i) * WP + w);
+                for (int i = 0; i < RT; ++i) {
+                    uv[i] = *reinterpret_cast<const float4*>(xs + (r0 + i) * WP + w);
+                    vv[i] = *reinterpret_cast<const float4*>(vs + (r0 + i) * WP + w);
+                }
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const float4 tv = *reinterpret_cast<const float4*>(T + (w + u) * K2 + 2 * kp);
 #pragma unroll
                     for (int i = 0; i < RT; ++i) {
-                        const float xval = u == 0 ? xv[i].x : (u == 1 ? xv[i].y : (u == 2 ? xv[i].z : xv[i].w));
-                        acc[i][0].x = fmaf(xval, tv.x, acc[i][0].x);
-                        acc[i][0].y = fmaf(xval, tv.y, acc[i][0].y);
-                        acc[i][1].x = fmaf(xval, tv.z, acc[i][1].x);
-                        acc[i][1].y = fmaf(xval, tv.w, acc[i][1].y);
+                        const float uval = u == 0 ? uv[i].x : (u == 1 ? uv[i].y : (u == 2 ? uv[i].z : uv[i].w));
+                        const float vval = u == 0 ? vv[i].x : (u == 1 ? vv[i].y : (u == 2 ? vv[i].z : vv[i].w));
+                        acc[i][0].x = fmaf(uval, tv.x, acc[i][0].x);
+                        acc[i][0].y = fmaf(vval, tv.y, acc[i][0].y);
+                        acc[i][1].x = fmaf(uval, tv.z, acc[i][1].x);
+                        acc[i][1].y = fmaf(vval, tv.w, acc[i][1].y);
                     }
                 }
             }
@@ -505,7 +525,7 @@ cudaError_t launch_dft_fwd(const float* x, float2* out1, float2* out2, long long
         t.m2 = m2;
         t.tw_row = tw.row_fwd;
         t.tw_col = tw.col_fwd;
-        t.WP = (W + 3) / 4 * 4;
+        t.WP = (W / 2 + 1 + 3) / 4 * 4;
         if ((t.WP / 4) % 2 == 0) t.WP += 4;  // an odd number of 16-byte units per row
         const int KP = (m2 + 1) / 2, K2 = 2 * KP, S2 = 2 * m1;
         // One-row tiles with three CTAs per SM (about three per SM over the whole batch) where a
@@ -522,7 +542,7 @@ cudaError_t launch_dft_fwd(const float* x, float2* out1, float2* out2, long long
         auto smem_of = [&](int rc, int ws) {
             return (static_cast<size_t>(t.WP) * K2 + static_cast<size_t>(S2) * (rc + 1) +
                     static_cast<size_t>(ws + (ws > 1 ? 1 : 0)) * rc * K2 + static_cast<size_t>(S2) * K2) * 8 +
-                   static_cast<size_t>(rc) * t.WP * 4;
+                   2 * static_cast<size_t>(rc) * t.WP * 4;
         };
         int RC = (t.RB + RT - 1) / RT * RT;
         // w splits: as many as keep the stage-1 tiles within the CTA's threads, 16 columns each at least

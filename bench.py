@@ -444,7 +444,14 @@ def run_strong(name: str, steps: int, warmup: int, device, world: int, rank: int
         torch.cuda.synchronize(device)
         return sum(e0.elapsed_time(e1) for e0, e1 in evs) / n
 
+    peer = scx_dist.PeerGather(y_loc, out_all, B) if world > 1 else None
+
     def step_gather():
+        graph.replay()
+        if world > 1:
+            peer.push(stream.cuda_stream)
+
+    def step_nccl():
         graph.replay()
         if world > 1:
             scx_dist.gather_batch_into(y_loc, out_all, B)
@@ -455,13 +462,22 @@ def run_strong(name: str, steps: int, warmup: int, device, world: int, rank: int
     if world > 1:
         torch.distributed.barrier()
     t_fwd = scx_dist.max_over_ranks(timed(graph.replay, steps), device)
+    t_nccl = None
     if world > 1:
         torch.distributed.barrier()
+        for _ in range(warmup):
+            step_nccl()
+        t_nccl = scx_dist.max_over_ranks(timed(step_nccl, steps), device)
+        torch.distributed.barrier()
     t_step = scx_dist.max_over_ranks(timed(step_gather, steps), device)
+    if world > 1:
+        peer.sync()  # every push has landed before rank 0 reads the gathered output
     res = {"workload": name, "batch_total": B, "batch_per_gpu": scx_dist.shard_sizes(B, world),
            "ms_per_step": t_step, "samples_per_s": B / (t_step / 1e3), "ms_forward_only": t_fwd,
            "gather_share": max(0.0, (t_step - t_fwd) / t_step) if world > 1 else 0.0,
-           "gather": "NCCL point-to-point group into a preallocated tensor on rank 0" if world > 1 else None,
+           "gather": "one peer copy per rank into a preallocated tensor on rank 0 (CUDA IPC, copy engines over "
+                     "NVLink)" if world > 1 else None,
+           "ms_per_step_nccl_gather": t_nccl,
            "launches_per_step": launches_per_forward(c), "cuda_graph": True, "scaling": "strong",
            "l2": "256 MiB flush between steps (not timed)"}
     if world > 1:
@@ -488,6 +504,7 @@ def run_strong(name: str, steps: int, warmup: int, device, world: int, rank: int
                    accuracy=fixture_error(name, out_all))
     if world > 1:
         torch.distributed.barrier()
+        peer.close()
     del graph
     return res
 
@@ -523,10 +540,12 @@ def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
 
+    peer = scx_dist.PeerGather(out, out_all, B * world) if world > 1 else None
+
     def step():
         graph.replay()
         if world > 1:
-            scx_dist.gather_batch_into(out, out_all, B * world)
+            peer.push(stream.cuda_stream)
 
     for _ in range(warmup):
         step()
@@ -543,13 +562,16 @@ def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
     t_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
     t_ms = scx_dist.max_over_ranks(t_ms, device)
     ms = t_ms / steps
+    if world > 1:
+        peer.sync()
+        peer.close()
     del graph
     return {"ms_per_step": ms, "samples_per_s": world * B / (ms / 1e3), "batch_per_gpu": B,
             # lift, then per layer forward DFT, mixing, inverse DFT and the fused skip +
             # instance norm + GELU (one cluster launch at 64x64), then the projection
             "launches_per_step": 2 + 4 * fw["layers"], "cuda_graph": True,
-            "gather": "NCCL point-to-point group into a preallocated tensor on rank 0, inside the step"
-            if world > 1 else None,
+            "gather": "one peer copy per rank into a preallocated tensor on rank 0 (CUDA IPC, copy engines over "
+                      "NVLink), inside the step" if world > 1 else None,
             "l2": "256 MiB flush between steps (not timed)"}
 
 

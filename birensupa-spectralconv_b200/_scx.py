@@ -78,6 +78,11 @@ _SIGNATURES = {
     "scx_clear_variants": ([], None),
     "scx_fno2d_workspace_size": ([ctypes.POINTER(FnoConfig)], _sz),
     "scx_fno2d_fwd": ([ctypes.POINTER(FnoConfig), ctypes.POINTER(FnoParams), _p, _p, _p, _sz, _p], _i),
+    "scx_ipc_handle_bytes": ([], _i),
+    "scx_ipc_export": ([_p, _p, ctypes.POINTER(ctypes.c_ulonglong)], _i),
+    "scx_ipc_import": ([_p, ctypes.POINTER(ctypes.c_void_p)], _i),
+    "scx_ipc_close": ([_p], _i),
+    "scx_copy_async": ([_p, _p, _sz, _p], _i),
 }
 
 for _name, (_args, _ret) in _SIGNATURES.items():

@@ -1,13 +1,15 @@
 """Batch sharding across ranks (one process per GPU) and the final output gather.
 
 The SpectralConv2d / FNO forward is independent per batch item and the weights are
-replicated, so the only exchange is one gather of the output shards to rank 0 (one group of
-NCCL point-to-point transfers over NVLink on GPUs, gloo on CPU in the tests).  Shards are contiguous and ragged when the
-batch does not divide: B=20 over 8 ranks -> 3,3,3,3,2,2,2,2.
+replicated, so the only exchange is one gather of the output shards to rank 0: one group of
+NCCL point-to-point transfers (``gather_batch_into``; gloo on CPU in the tests), or, on GPUs,
+one peer copy per rank straight into rank 0's output over NVLink (``PeerGather``).  Shards are
+contiguous and ragged when the batch does not divide: B=20 over 8 ranks -> 3,3,3,3,2,2,2,2.
 """
 
 from __future__ import annotations
 
+import ctypes
 import datetime
 import os
 
@@ -74,6 +76,73 @@ def gather_batch_into(local: torch.Tensor, out: torch.Tensor | None, batch: int,
     if ops:
         for work in dist.batch_isend_irecv(ops):
             work.wait()
+
+
+class PeerGather:
+    """Gather of the ragged per-rank shards of ``local`` into ``out`` on rank ``dst`` by peer
+    copies (GPUs, one process per GPU).  Built once, collectively: rank ``dst`` exports its
+    preallocated ``out`` ([batch, ...]) through CUDA IPC (scx_ipc_export), every other rank
+    imports it and keeps the address of its own slice.  ``push(stream)`` then copies this rank's
+    shard into that slice with one device-to-device copy (copy engines, over NVLink), ordered on
+    ``stream`` after the kernels that wrote ``local``; rank ``dst`` copies its shard locally
+    unless ``local`` is already a view of its slice.  No collective runs per step: a push is
+    complete when its stream reaches it, so the step time is the max over ranks of their
+    stream times, and rank ``dst`` may read ``out`` once every rank has synchronised its
+    stream and passed a host barrier (``sync()`` does both).  ``close()`` releases the import."""
+
+    def __init__(self, local: torch.Tensor, out: torch.Tensor | None, batch: int, dst: int = 0):
+        import _scx
+
+        self.lib = _scx.lib
+        self.world = dist.get_world_size()
+        self.rank = dist.get_rank()
+        self.dst = dst
+        sizes = shard_sizes(batch, self.world)
+        if local.shape[0] != sizes[self.rank] or not local.is_contiguous() or local.device.type != "cuda":
+            raise ValueError(f"rank {self.rank}: needs a contiguous CUDA shard of {sizes[self.rank]} items")
+        self.local = local
+        self.nbytes = local.numel() * local.element_size()
+        item = self.nbytes // max(1, sizes[self.rank]) if sizes[self.rank] else 0
+        nh = self.lib.scx_ipc_handle_bytes()
+        payload = [None]
+        if self.rank == dst:
+            if out is None or out.shape[0] != batch or tuple(out.shape[1:]) != tuple(local.shape[1:]) \
+                    or not out.is_contiguous() or out.dtype != local.dtype or out.device != local.device:
+                raise ValueError(f"rank {dst} needs a contiguous output of shape {(batch,) + tuple(local.shape[1:])}")
+            handle = (ctypes.c_char * nh)()
+            offset = ctypes.c_ulonglong(0)
+            _scx.check(self.lib.scx_ipc_export(out.data_ptr(), handle, ctypes.byref(offset)), "scx_ipc_export")
+            payload = [(bytes(handle), int(offset.value), out.numel() * out.element_size() // batch)]
+        dist.broadcast_object_list(payload, src=dst)
+        handle_bytes, offset, item_bytes = payload[0]
+        self.base = None
+        lo, _ = shard_range(batch, self.world, self.rank)
+        if self.rank == dst:
+            self.dst_ptr = out.data_ptr() + lo * item_bytes
+        else:
+            base = ctypes.c_void_p(0)
+            buf = (ctypes.c_char * nh).from_buffer_copy(handle_bytes)
+            _scx.check(self.lib.scx_ipc_import(buf, ctypes.byref(base)), "scx_ipc_import")
+            self.base = base.value
+            self.dst_ptr = self.base + offset + lo * item_bytes
+        if item and item != item_bytes:
+            raise ValueError("shard items and output items differ in size")
+
+    def push(self, stream: int) -> None:
+        if self.nbytes and self.dst_ptr != self.local.data_ptr():
+            import _scx
+
+            _scx.check(self.lib.scx_copy_async(self.dst_ptr, self.local.data_ptr(), self.nbytes, stream),
+                       "scx_copy_async")
+
+    def sync(self) -> None:
+        torch.cuda.synchronize(self.local.device)
+        dist.barrier()
+
+    def close(self) -> None:
+        if self.base is not None:
+            self.lib.scx_ipc_close(self.base)
+            self.base = None
 
 
 def gather_batch(local: torch.Tensor, batch: int, dst: int = 0) -> torch.Tensor | None:

@@ -270,6 +270,22 @@ void scx_clear_variants(void);
 /* Size of the fixed device scratch used by scx_spectral_conv2d_fwd_noalloc (16 MiB). */
 #define SCX_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
+/* Peer-memory plumbing for the multi-GPU output gather (one process per GPU).  No counterpart
+ * in the reference, which has no multi-GPU path; it replaces the NCCL point-to-point gather of
+ * the output shards to one rank.  The gathering rank exports its output buffer once
+ * (scx_ipc_export: an IPC handle of scx_ipc_handle_bytes() bytes for the allocation that
+ * contains dev_ptr, plus dev_ptr's byte offset in it).  Every other rank imports the handle
+ * (scx_ipc_import, peer access enabled on first use), and each step pushes its shard with
+ * scx_copy_async into base + offset + its slice: one device-to-device copy over NVLink, run by
+ * the copy engines and ordered on the caller's stream after the kernels that produced it.  The
+ * push is complete when that stream reaches it; the gathering rank reads the buffer only after
+ * every pusher has synchronised (a host barrier).  scx_ipc_close releases an import. */
+int scx_ipc_handle_bytes(void);
+int scx_ipc_export(const void* dev_ptr, void* handle_out, unsigned long long* offset_out);
+int scx_ipc_import(const void* handle, void** base_out);
+int scx_ipc_close(void* base);
+int scx_copy_async(void* dst, const void* src, size_t bytes, scx_stream_t stream);
+
 /* Allocation-free variant of scx_spectral_conv2d_fwd.  No counterpart in the reference:
  * it exists for callers that cannot let a library call cudaMalloc (a process whose
  * memory pool already owns the GPU's memory, or a latency-critical loop that cannot

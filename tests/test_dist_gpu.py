@@ -5,7 +5,7 @@
 * Two or more GPUs (skipped otherwise): one process per GPU under torchrun, NCCL; each rank
   runs its shard on its own GPU, the shards are gathered into a preallocated tensor on rank 0
   (scx_dist.gather_batch_into), and rank 0 compares them with the whole batch run alone on its
-  GPU.
+  GPU; the peer-copy gather (scx_dist.PeerGather) must give the NCCL gather's bits.
 
 Per plane the transforms are computed the same way whatever the batch; the mixing kernel's
 tile shape is chosen per batch size and may split the channel sum into a different number of
@@ -80,7 +80,16 @@ if rank == 0:
                                                    use_sufft="fused", to_cpu=False)
     torch.cuda.synchronize(dev)
     scale = whole.abs().max().item()
-    print(json.dumps({"rel": (out - whole).abs().max().item() / scale, "bitwise": bool(torch.equal(out, whole))}))
+# the same gather by peer copies (CUDA IPC) into a NaN-poisoned output, twice
+out2 = torch.full((B,) + tuple(y.shape[1:]), float("nan"), device=dev) if rank == 0 else None
+peer = scx_dist.PeerGather(y.contiguous(), out2, B)
+for _ in range(2):
+    peer.push(torch.cuda.current_stream(dev).cuda_stream)
+peer.sync()
+if rank == 0:
+    print(json.dumps({"rel": (out - whole).abs().max().item() / scale, "bitwise": bool(torch.equal(out, whole)),
+                      "peer_equal": bool(torch.equal(out2, out))}))
+peer.close()
 torch.distributed.barrier()
 torch.distributed.destroy_process_group()
 """
@@ -111,3 +120,4 @@ def test_nccl_sharded_equals_single_gpu(name, tmp_path):
     lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
     r = json.loads(lines[-1])
     assert r["rel"] <= TOL, r
+    assert r["peer_equal"], r

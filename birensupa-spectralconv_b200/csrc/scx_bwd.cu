@@ -16,10 +16,12 @@
 // 2 overwrites in the forward (2 m1 > H) do not reach y, so their G rows are zeroed first;
 // the inverse drops those rows of grad_X, which are then zero anyway.
 //
-// Kernels: the forward DFT, two dual-corner mixings and the inverse DFT of the forward path,
-// plus small elementwise passes: the conjugate transposes of W and of X per mode (the per-ky
-// scale of grad_W is applied to X^H: it is per mode, so it commutes with the mixing) and, with
-// overlapping corners, the overlap-row mask.
+// Kernels: the forward DFT, two dual-corner mixings and the inverse DFT of the forward path.
+// The mixings read W^H and X^H straight from the weights and the saved corners (the TMA-ring
+// kernel with transposed tensor maps, conjugating in registers; the per-ky scale of grad_W is
+// per mode, so it commutes with the mixing and is applied to its result).  Where the ring
+// kernel does not apply, conjugate-transpose passes write W^H and (c_ky / HW) X^H first.  With
+// overlapping corners a small pass masks the overlap rows.
 #include <algorithm>
 
 #include "scx.h"
@@ -152,13 +154,20 @@ extern "C" int scx_spectral_conv2d_bwd(const float* grad_y, const float* x_corne
     // conjugate transposes per mode: W^H [Cout][Cin] ahead of the grad_x chain, (c_ky / HW) X^H
     // [Cin][B] after it
     const float inv_hw = static_cast<float>(1.0 / (static_cast<double>(H) * W));
+    // The TMA-ring mixing reads W^H and X^H straight from W and X (transposed tensor maps,
+    // conjugated in the kernel, the per-ky scale in its epilogue); where it does not apply the
+    // conjugate transposes run as separate passes.
+    const float2* W1 = reinterpret_cast<const float2*>(weights1);
+    const float2* W2 = reinterpret_cast<const float2*>(weights2);
     if (grad_x) {
         // grad_x = inv(G W^H)
-        conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(Cin) * Cout * NM), 2), kThreads, 0, s>>>(
-            reinterpret_cast<const float2*>(weights1), reinterpret_cast<const float2*>(weights2), WH1, WH2, Cin, Cout,
-            NM, 0, m2, W, inv_hw);
-        e = cudaGetLastError();
-        if (e == cudaSuccess) e = scx::launch_mix(G1, G2, WH1, WH2, Z1, Z2, 2, B, Cout, Cin, NM, s);
+        e = scx::launch_mix_ring_ct(G1, G2, W1, W2, Z1, Z2, 2, B, Cout, Cin, NM, 1, m2, W, inv_hw, s);
+        if (e == cudaErrorNotSupported) {
+            conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(Cin) * Cout * NM), 2), kThreads, 0, s>>>(
+                W1, W2, WH1, WH2, Cin, Cout, NM, 0, m2, W, inv_hw);
+            e = cudaGetLastError();
+            if (e == cudaSuccess) e = scx::launch_mix(G1, G2, WH1, WH2, Z1, Z2, 2, B, Cout, Cin, NM, s);
+        }
         if (e == cudaSuccess) e = scx::dft_inv(Z1, Z2, NM, m2, grad_x, B * Cin, H, W, m1, m2, *tw, s, scratch, L.scratch);
         if (e != cudaSuccess) return e;
     }
@@ -166,12 +175,15 @@ extern "C" int scx_spectral_conv2d_bwd(const float* grad_y, const float* x_corne
         // grad_W = ((c_ky / HW) X^H) G; X1 then X2 are contiguous at x_corners
         const float2* X1 = reinterpret_cast<const float2*>(x_corners);
         const float2* X2 = X1 + static_cast<size_t>(B) * Cin * NM;
-        conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(B) * Cin * NM), 2), kThreads, 0, s>>>(
-            X1, X2, XH1, XH2, B, Cin, NM, 1, m2, W, inv_hw);
-        e = cudaGetLastError();
-        if (e == cudaSuccess)
-            e = scx::launch_mix(XH1, XH2, G1, G2, reinterpret_cast<float2*>(grad_w1), reinterpret_cast<float2*>(grad_w2),
-                                2, Cin, B, Cout, NM, s);
+        float2* gw1 = reinterpret_cast<float2*>(grad_w1);
+        float2* gw2 = reinterpret_cast<float2*>(grad_w2);
+        e = scx::launch_mix_ring_ct(X1, X2, G1, G2, gw1, gw2, 2, Cin, B, Cout, NM, 2, m2, W, inv_hw, s);
+        if (e == cudaErrorNotSupported) {
+            conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(B) * Cin * NM), 2), kThreads, 0, s>>>(
+                X1, X2, XH1, XH2, B, Cin, NM, 1, m2, W, inv_hw);
+            e = cudaGetLastError();
+            if (e == cudaSuccess) e = scx::launch_mix(XH1, XH2, G1, G2, gw1, gw2, 2, Cin, B, Cout, NM, s);
+        }
     }
     return e;
 }
@@ -230,24 +242,30 @@ extern "C" int scx_spectral_mul_bwd(const float* x_freq, const float* weights, c
     float2* XH = reinterpret_cast<float2*>(base + L.wh);
     const float2* G = reinterpret_cast<const float2*>(grad_y);
     cudaError_t e = cudaSuccess;
+    // as in scx_spectral_conv2d_bwd: W^H and X^H read in place by the TMA-ring mixing where it
+    // applies (no scale: W = 0), else written by conjugate-transpose passes first
     if (grad_x) {
         const float2* Wc = reinterpret_cast<const float2*>(weights);
-        conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(Cin) * Cout * NM), 1), kThreads, 0, s>>>(
-            Wc, nullptr, WH, nullptr, Cin, Cout, NM, 0, modes2, 2, 1.f);  // one corner: grid.y = 1
-        e = cudaGetLastError();
-        if (e == cudaSuccess)
-            e = scx::launch_mix(G, nullptr, WH, nullptr, reinterpret_cast<float2*>(grad_x), nullptr, 1, B, Cout, Cin,
-                                NM, s);
+        float2* gx = reinterpret_cast<float2*>(grad_x);
+        e = scx::launch_mix_ring_ct(G, G, Wc, Wc, gx, gx, 1, B, Cout, Cin, NM, 1, modes2, 0, 1.f, s);
+        if (e == cudaErrorNotSupported) {
+            conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(Cin) * Cout * NM), 1), kThreads, 0, s>>>(
+                Wc, nullptr, WH, nullptr, Cin, Cout, NM, 0, modes2, 2, 1.f);  // one corner: grid.y = 1
+            e = cudaGetLastError();
+            if (e == cudaSuccess) e = scx::launch_mix(G, nullptr, WH, nullptr, gx, nullptr, 1, B, Cout, Cin, NM, s);
+        }
         if (e != cudaSuccess) return e;
     }
     if (grad_w) {
         const float2* Xc = reinterpret_cast<const float2*>(x_freq);
-        conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(B) * Cin * NM), 1), kThreads, 0, s>>>(
-            Xc, nullptr, XH, nullptr, B, Cin, NM, 0, modes2, 2, 1.f);
-        e = cudaGetLastError();
-        if (e == cudaSuccess)
-            e = scx::launch_mix(XH, nullptr, G, nullptr, reinterpret_cast<float2*>(grad_w), nullptr, 1, Cin, B, Cout,
-                                NM, s);
+        float2* gw = reinterpret_cast<float2*>(grad_w);
+        e = scx::launch_mix_ring_ct(Xc, Xc, G, G, gw, gw, 1, Cin, B, Cout, NM, 2, modes2, 0, 1.f, s);
+        if (e == cudaErrorNotSupported) {
+            conj_transpose_kernel<<<dim3(blocks_for(static_cast<long long>(B) * Cin * NM), 1), kThreads, 0, s>>>(
+                Xc, nullptr, XH, nullptr, B, Cin, NM, 0, modes2, 2, 1.f);
+            e = cudaGetLastError();
+            if (e == cudaSuccess) e = scx::launch_mix(XH, nullptr, G, nullptr, gw, nullptr, 1, Cin, B, Cout, NM, s);
+        }
     }
     return e;
 }

@@ -173,6 +173,17 @@ cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, con
                        float2* y1, float2* y2, int ncorner, int B, int Cin, int Cout, int NM,
                        cudaStream_t stream);
 
+// The mixing with one operand read as the conjugate transpose of a stored tensor, on the
+// TMA-ring kernel only (the backward's W^H and X^H without a transpose pass).  B, Cin, Cout are
+// the product's: y[b][o] = sum_i x'[b][i] w'[i][o] per mode.  mode 1: w' = conj(w)^T with w stored
+// [Cout][Cin] per mode; mode 2: x' = conj(x)^T with x stored [Cin][B] per mode, and, for W > 0,
+// y scaled per mode by c_ky * inv_hw (c_ky = 1 for ky = 0 and, W even, ky = W/2, else 2;
+// ky = mode % m2).
+// Returns cudaErrorNotSupported where the ring kernel does not apply.
+cudaError_t launch_mix_ring_ct(const float2* x1, const float2* x2, const float2* w1, const float2* w2, float2* y1,
+                               float2* y2, int ncorner, int B, int Cin, int Cout, int NM, int mode, int m2, int W,
+                               float inv_hw, cudaStream_t stream);
+
 // The same contraction on the tensor core (3xTF32), used where the variant table selects it
 // (variant kMixTc): B <= 16, Cin a multiple of 8, Cout a multiple of 64, an even mode count and
 // 16-byte aligned operands.  Returns cudaErrorNotSupported for anything else.

@@ -128,6 +128,8 @@ struct MixRingArgs {
     int NCH, NS, n_os;  // channel chunks, ring stages, output-channel blocks
     uint32_t stage_bytes;
     int* watchdog;
+    int m2, W;          // CJ = 2: the per-mode output scale c_ky * inv_hw (ky = mode % m2)
+    float inv_hw;
 };
 
 // x_c viewed as [B][Cin][2*NM] floats, w_c as [Cin][Cout][2*NM].  Chunk c of the ring holds
@@ -138,7 +140,12 @@ struct MixRingArgs {
 // own slots); within a group, thread (g, mode k) keeps BT batch items x OT output channels,
 // and the two half-warps share their batch items, so an x read is one broadcast line.  The
 // groups' partial sums are added in group order at the end.
-template <int BT, int OT, int NBQ, int NOQ, int KS>
+// CJ selects what the staged operands mean (the boxes are the same; the tensor maps decide which
+// stored tensor and order they come from): 0 = x and w as stored; 1 = w is the conjugate of the
+// staged values (the backward's W^H, read through a transposed map); 2 = x is the conjugate of
+// the staged values (X^H) and the result is scaled per mode by c_ky * inv_hw (c_ky = 1 for
+// ky = 0 and, W even, ky = W/2, else 2).
+template <int BT, int OT, int NBQ, int NOQ, int KS, int CJ>
 __global__ void __launch_bounds__(16 * NBQ * NOQ * KS) mix_ring_kernel(const __grid_constant__ CUtensorMap tx0,
                                                                        const __grid_constant__ CUtensorMap tx1,
                                                                        const __grid_constant__ CUtensorMap tw0,
@@ -196,9 +203,15 @@ __global__ void __launch_bounds__(16 * NBQ * NOQ * KS) mix_ring_kernel(const __g
         for (int i = 0; i < IC; ++i) {
             float2 xv[BT], wv[OT];
 #pragma unroll
-            for (int q = 0; q < BT; ++q) xv[q] = xp[(q * IC + i) * kRingTM];
+            for (int q = 0; q < BT; ++q) {
+                xv[q] = xp[(q * IC + i) * kRingTM];
+                if (CJ == 2) xv[q].y = -xv[q].y;
+            }
 #pragma unroll
-            for (int p = 0; p < OT; ++p) wv[p] = wp[(i * OC + p) * kRingTM];
+            for (int p = 0; p < OT; ++p) {
+                wv[p] = wp[(i * OC + p) * kRingTM];
+                if (CJ == 1) wv[p].y = -wv[p].y;
+            }
 #pragma unroll
             for (int q = 0; q < BT; ++q)
 #pragma unroll
@@ -238,6 +251,17 @@ __global__ void __launch_bounds__(16 * NBQ * NOQ * KS) mix_ring_kernel(const __g
     }
     const int kk = k0 + k;
     if (kk >= a.NM) return;
+    if (CJ == 2 && a.W > 0) {
+        const int ky = kk % a.m2;
+        const float f = (ky == 0 || ((a.W % 2) == 0 && 2 * ky == a.W)) ? a.inv_hw : 2.0f * a.inv_hw;
+#pragma unroll
+        for (int q = 0; q < BT; ++q)
+#pragma unroll
+            for (int p = 0; p < OT; ++p) {
+                acc[q][p].x *= f;
+                acc[q][p].y *= f;
+            }
+    }
     float2* __restrict__ Y = corner ? a.y[1] : a.y[0];
 #pragma unroll
     for (int q = 0; q < BT; ++q)
@@ -266,13 +290,14 @@ EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// 3-D fp32 tensor [d2][d1][d0] (d0 innermost), box (b0, b1, b2).
+// 3-D fp32 tensor with dims (d0 innermost, d1, d2) and byte strides s1, s2 of dims 1 and 2 (in
+// either order: a transposed view of a stored tensor), box (b0, b1, b2).
 bool encode3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0, uint32_t b1,
-              uint32_t b2) {
+              uint32_t b2, uint64_t s1 = 0, uint64_t s2 = 0) {
     EncodeTiledFn fn = encode_tiled();
     if (fn == nullptr) return false;
     const cuuint64_t dims[3] = {d0, d1, d2};
-    const cuuint64_t strides[2] = {d0 * 4, d0 * d1 * 4};
+    const cuuint64_t strides[2] = {s1 ? s1 : d0 * 4, s2 ? s2 : d0 * d1 * 4};
     const cuuint32_t box[3] = {b0, b1, b2};
     const cuuint32_t es[3] = {1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, es,
@@ -289,17 +314,22 @@ const RingCfg kRingCands[] = {{5, 2, 4, 4, 2}, {5, 2, 4, 2, 4}, {4, 4, 4, 4, 2},
                               {4, 2, 4, 4, 2}, {2, 2, 4, 4, 2}, {1, 2, 2, 4, 2}, {1, 2, 1, 8, 2}};
 constexpr int kNumRingCands = static_cast<int>(sizeof(kRingCands) / sizeof(kRingCands[0]));
 
-const void* ring_kernel(int ci) {
+template <int CJ>
+const void* ring_kernel_cj(int ci) {
     switch (ci) {
-        case 0: return reinterpret_cast<const void*>(mix_ring_kernel<5, 2, 4, 4, 2>);
-        case 1: return reinterpret_cast<const void*>(mix_ring_kernel<5, 2, 4, 2, 4>);
-        case 2: return reinterpret_cast<const void*>(mix_ring_kernel<4, 4, 4, 4, 2>);
-        case 3: return reinterpret_cast<const void*>(mix_ring_kernel<4, 4, 4, 2, 4>);
-        case 4: return reinterpret_cast<const void*>(mix_ring_kernel<4, 2, 4, 4, 2>);
-        case 5: return reinterpret_cast<const void*>(mix_ring_kernel<2, 2, 4, 4, 2>);
-        case 6: return reinterpret_cast<const void*>(mix_ring_kernel<1, 2, 2, 4, 2>);
-        default: return reinterpret_cast<const void*>(mix_ring_kernel<1, 2, 1, 8, 2>);
+        case 0: return reinterpret_cast<const void*>(mix_ring_kernel<5, 2, 4, 4, 2, CJ>);
+        case 1: return reinterpret_cast<const void*>(mix_ring_kernel<5, 2, 4, 2, 4, CJ>);
+        case 2: return reinterpret_cast<const void*>(mix_ring_kernel<4, 4, 4, 4, 2, CJ>);
+        case 3: return reinterpret_cast<const void*>(mix_ring_kernel<4, 4, 4, 2, 4, CJ>);
+        case 4: return reinterpret_cast<const void*>(mix_ring_kernel<4, 2, 4, 4, 2, CJ>);
+        case 5: return reinterpret_cast<const void*>(mix_ring_kernel<2, 2, 4, 4, 2, CJ>);
+        case 6: return reinterpret_cast<const void*>(mix_ring_kernel<1, 2, 2, 4, 2, CJ>);
+        default: return reinterpret_cast<const void*>(mix_ring_kernel<1, 2, 1, 8, 2, CJ>);
     }
+}
+
+const void* ring_kernel(int ci, int cj = 0) {
+    return cj == 1 ? ring_kernel_cj<1>(ci) : cj == 2 ? ring_kernel_cj<2>(ci) : ring_kernel_cj<0>(ci);
 }
 
 struct RingChoice {
@@ -361,11 +391,12 @@ bool smem_kernel_fits(int B, int Cin, int Cout) {
 // The TMA ring launch; returns cudaErrorNotSupported when the shape or alignment does not fit
 // its boxes (the caller then uses mix_smem_kernel).
 cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1, const float2* w2, float2* y1,
-                            float2* y2, int ncorner, int B, int Cin, int Cout, int NM, cudaStream_t stream) {
+                            float2* y2, int ncorner, int B, int Cin, int Cout, int NM, cudaStream_t stream,
+                            int cj = 0, int m2 = 1, int Wd = 1, float inv_hw = 1.f) {
     const uintptr_t al = reinterpret_cast<uintptr_t>(x1) | reinterpret_cast<uintptr_t>(w1) |
                          (ncorner == 2 ? (reinterpret_cast<uintptr_t>(x2) | reinterpret_cast<uintptr_t>(w2)) : 0);
     if (NM % 2 != 0 || (al & 15) != 0 || Cin < kRingIC) return cudaErrorNotSupported;
-    const int forced = mix_variant(ncorner, B, Cin, Cout, NM);
+    const int forced = cj == 0 ? mix_variant(ncorner, B, Cin, Cout, NM) : kMixAuto;
     // measured: the per-thread kernel wins (when one mode's operands fit its shared memory)
     if (forced == kMixSmem && smem_kernel_fits(B, Cin, Cout)) return cudaErrorNotSupported;
     // Tile shapes: the measured one when the variant table names one that fits, else the one
@@ -411,6 +442,9 @@ cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1
     a.NS = best_ns;
     a.n_os = (Cout + OC - 1) / OC;
     a.stage_bytes = static_cast<uint32_t>(BB + OC) * kRingIC * kRingTM * 8u;
+    a.m2 = m2;
+    a.W = Wd;
+    a.inv_hw = inv_hw;
     const int n_bs = (B + BB - 1) / BB;
     const int threads = 16 * cfg.NBQ * cfg.NOQ * cfg.KS;
     e = device_watchdog(&a.watchdog);
@@ -418,18 +452,35 @@ cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1
     CUtensorMap tx[2], tw[2];
     const float2* xs[2] = {x1, x2};
     const float2* ws[2] = {w1, w2};
+    const uint64_t row = 2ull * NM * 4ull;  // bytes between consecutive channels of one mode row
     for (int c = 0; c < 2; ++c) {
         const int src = c < ncorner ? c : 0;  // an unused second corner repeats the first map
-        if (!encode3d(&tx[c], xs[src], 2ull * NM, Cin, B, 2u * kRingTM, kRingIC, BB) ||
-            !encode3d(&tw[c], ws[src], 2ull * NM, Cout, Cin, 2u * kRingTM, OC, kRingIC))
+        // cj = 2: x is stored [Cin][B] per mode (read transposed); cj = 1: w is stored [Cout][Cin]
+        const bool xt = cj == 2, wt = cj == 1;
+        if (!encode3d(&tx[c], xs[src], 2ull * NM, Cin, B, 2u * kRingTM, kRingIC, BB, xt ? row * B : 0, xt ? row : 0) ||
+            !encode3d(&tw[c], ws[src], 2ull * NM, Cout, Cin, 2u * kRingTM, OC, kRingIC, wt ? row * Cin : 0,
+                      wt ? row : 0))
             return cudaErrorNotSupported;
     }
     const dim3 grid(static_cast<unsigned>((NM + kRingTM - 1) / kRingTM), ncorner, a.n_os * n_bs);
     void* args[] = {&tx[0], &tx[1], &tw[0], &tw[1], &a};
-    return launch_chained_raw(ring_kernel(best), grid, dim3(threads), best_smem, stream, args);
+    const void* kernel = ring_kernel(best, cj);
+    if (cj != 0) {
+        int per_sm = 1;
+        e = prepare_kernel(kernel, best_smem, threads, &per_sm);
+        if (e != cudaSuccess) return e;
+    }
+    return launch_chained_raw(kernel, grid, dim3(threads), best_smem, stream, args);
 }
 
 }  // namespace
+
+cudaError_t launch_mix_ring_ct(const float2* x1, const float2* x2, const float2* w1, const float2* w2, float2* y1,
+                               float2* y2, int ncorner, int B, int Cin, int Cout, int NM, int mode, int m2, int W,
+                               float inv_hw, cudaStream_t stream) {
+    if (mode < 1 || mode > 2) return cudaErrorInvalidValue;
+    return launch_mix_ring(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream, mode, m2, W, inv_hw);
+}
 
 cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, const float2* w2,
                        float2* y1, float2* y2, int ncorner, int B, int Cin, int Cout, int NM,

@@ -244,9 +244,10 @@ int scx_spectral_conv2d_fwd(const float* x, const float* weights1, const float* 
     e = scx::dft_fwd(x, X1, X2, NM, modes2, batch_size * channels_in, height, width, modes1, modes2, *tw, s,
                      scratch_bytes ? scratch : nullptr, scratch_bytes);
     if (e != cudaSuccess) return e;
+    // the weights are not written by the forward DFT it follows
     e = scx::launch_mix(X1, X2, reinterpret_cast<const float2*>(weights1),
                         reinterpret_cast<const float2*>(weights2), Y1, Y2, 2, batch_size, channels_in,
-                        channels_out, static_cast<int>(NM), s);
+                        channels_out, static_cast<int>(NM), s, true);
     if (e != cudaSuccess) return e;
     return scx::dft_inv(Y1, Y2, NM, modes2, y, batch_size * channels_out, height, width, modes1, modes2, *tw, s,
                         scratch_bytes ? scratch : nullptr, scratch_bytes);

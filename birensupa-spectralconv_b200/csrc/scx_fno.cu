@@ -728,7 +728,7 @@ extern "C" int scx_fno2d_fwd(const scx_fno2d_config* cfg, const scx_fno2d_params
         if (e != cudaSuccess) return e;
         e = scx::launch_mix(X1, X2, reinterpret_cast<const float2*>(prm->spectral_w1[l]),
                             reinterpret_cast<const float2*>(prm->spectral_w2[l]), Y1, Y2, 2, B, C, C,
-                            static_cast<int>(NM), s);
+                            static_cast<int>(NM), s, true);  // weights are not written in the forward
         if (e != cudaSuccess) return e;
         e = scx::dft_inv(Y1, Y2, NM, m2, act[spec], B * C, H, W, m1, m2, *tw, s);
         if (e != cudaSuccess) return e;

@@ -168,10 +168,13 @@ cudaError_t launch_fno_project_tc(const float* h, float* y, const float* w1, con
 cudaError_t read_watchdog(int* value, bool reset);
 
 // Per-mode complex channel mixing y_c[b,o,k] = sum_i x_c[b,i,k] * w_c[i,o,k] for
-// ncorner (1 or 2) corners, k over NM = m1*m2 modes.
+// ncorner (1 or 2) corners, k over NM = m1*m2 modes.  The kernel is a programmatic dependent of
+// the previous kernel in the stream; `w_early` tells it that w is not written by the kernels it
+// is chained after (the layer's weights in a forward), so the TMA-ring kernel may request the
+// first w boxes before waiting for them.
 cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, const float2* w2,
                        float2* y1, float2* y2, int ncorner, int B, int Cin, int Cout, int NM,
-                       cudaStream_t stream);
+                       cudaStream_t stream, bool w_early = false);
 
 // The mixing with one operand read as the conjugate transpose of a stored tensor, on the
 // TMA-ring kernel only (the backward's W^H and X^H without a transpose pass).  B, Cin, Cout are

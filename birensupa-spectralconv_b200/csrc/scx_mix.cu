@@ -130,6 +130,8 @@ struct MixRingArgs {
     int* watchdog;
     int m2, W;          // CJ = 2: the per-mode output scale c_ky * inv_hw (ky = mode % m2)
     float inv_hw;
+    int w_early;        // w is not written by the kernels this one is chained after: the first
+                        // stages' w boxes are requested before griddepcontrol.wait
 };
 
 // x_c viewed as [B][Cin][2*NM] floats, w_c as [Cin][Cout][2*NM].  Chunk c of the ring holds
@@ -163,19 +165,32 @@ __global__ void __launch_bounds__(16 * NBQ * NOQ * KS) mix_ring_kernel(const __g
     const CUtensorMap* mx = corner ? &tx1 : &tx0;
     const CUtensorMap* mw = corner ? &tw1 : &tw0;
     const int NS = a.NS, NCH = a.NCH;
-    auto issue = [&](int c) {
-        uint8_t* st = base + static_cast<uint32_t>(c % NS) * a.stage_bytes;
+    auto issue_x = [&](int c) {
+        tc::tma_load_3d(base + static_cast<uint32_t>(c % NS) * a.stage_bytes, mx, 2 * k0, c * IC, b_base, &full[c % NS]);
+    };
+    auto issue_w = [&](int c) {
         uint64_t* bar = &full[c % NS];
         tc::mbar_arrive_expect_tx(bar, a.stage_bytes);
-        tc::tma_load_3d(st, mx, 2 * k0, c * IC, b_base, bar);
-        tc::tma_load_3d(st + XB, mw, 2 * k0, o_base, c * IC, bar);
+        tc::tma_load_3d(base + static_cast<uint32_t>(c % NS) * a.stage_bytes + XB, mw, 2 * k0, o_base, c * IC, bar);
+    };
+    auto issue = [&](int c) {
+        issue_w(c);
+        issue_x(c);
     };
     if (threadIdx.x == 0) {
         tc::grid_dep_launch();  // the next kernel's CTAs may start their prologue
         for (int i = 0; i < kRingMaxStages; ++i) tc::mbar_init(&full[i], 1);
         tc::fence_async_smem();
-        tc::grid_dep_wait();  // x comes from the previous kernel in the stream
-        for (int c = 0; c < min(NS, NCH); ++c) issue(c);
+        const int first = min(NS, NCH);
+        if (a.w_early) {
+            // the weights do not depend on the previous kernel: their boxes overlap its tail
+            for (int c = 0; c < first; ++c) issue_w(c);
+            tc::grid_dep_wait();  // x comes from the previous kernel in the stream
+            for (int c = 0; c < first; ++c) issue_x(c);
+        } else {
+            tc::grid_dep_wait();  // x (and w) may come from the previous kernel in the stream
+            for (int c = 0; c < first; ++c) issue(c);
+        }
         failed = 0;
     }
     __syncthreads();
@@ -392,7 +407,7 @@ bool smem_kernel_fits(int B, int Cin, int Cout) {
 // its boxes (the caller then uses mix_smem_kernel).
 cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1, const float2* w2, float2* y1,
                             float2* y2, int ncorner, int B, int Cin, int Cout, int NM, cudaStream_t stream,
-                            int cj = 0, int m2 = 1, int Wd = 1, float inv_hw = 1.f) {
+                            int cj = 0, int m2 = 1, int Wd = 1, float inv_hw = 1.f, bool w_early = false) {
     const uintptr_t al = reinterpret_cast<uintptr_t>(x1) | reinterpret_cast<uintptr_t>(w1) |
                          (ncorner == 2 ? (reinterpret_cast<uintptr_t>(x2) | reinterpret_cast<uintptr_t>(w2)) : 0);
     if (NM % 2 != 0 || (al & 15) != 0 || Cin < kRingIC) return cudaErrorNotSupported;
@@ -445,6 +460,7 @@ cudaError_t launch_mix_ring(const float2* x1, const float2* x2, const float2* w1
     a.m2 = m2;
     a.W = Wd;
     a.inv_hw = inv_hw;
+    a.w_early = w_early ? 1 : 0;
     const int n_bs = (B + BB - 1) / BB;
     const int threads = 16 * cfg.NBQ * cfg.NOQ * cfg.KS;
     e = device_watchdog(&a.watchdog);
@@ -479,12 +495,13 @@ cudaError_t launch_mix_ring_ct(const float2* x1, const float2* x2, const float2*
                                float2* y2, int ncorner, int B, int Cin, int Cout, int NM, int mode, int m2, int W,
                                float inv_hw, cudaStream_t stream) {
     if (mode < 1 || mode > 2) return cudaErrorInvalidValue;
-    return launch_mix_ring(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream, mode, m2, W, inv_hw);
+    // mode 1 reads the weights (never written in the chain); mode 2 reads G, which the chain writes
+    return launch_mix_ring(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream, mode, m2, W, inv_hw, mode == 1);
 }
 
 cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, const float2* w2,
                        float2* y1, float2* y2, int ncorner, int B, int Cin, int Cout, int NM,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, bool w_early) {
     // The tensor-core kernel only where the variant table names it: with B <= 16 each weight
     // element feeds 2B real products, and its conversion into tf32 operands costs more than the
     // FFMA work it replaces (B16 C64 m32: 61 us against 45 us for the TMA-ring kernel).
@@ -493,7 +510,8 @@ cudaError_t launch_mix(const float2* x1, const float2* x2, const float2* w1, con
         const cudaError_t ce = launch_mix_tc(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream);
         if (ce != cudaErrorNotSupported) return ce;
     }
-    const cudaError_t te = launch_mix_ring(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream);
+    const cudaError_t te = launch_mix_ring(x1, x2, w1, w2, y1, y2, ncorner, B, Cin, Cout, NM, stream, 0, 1, 1, 1.f,
+                                           w_early);
     if (te != cudaErrorNotSupported) return te;
     MixArgs a;
     a.x[0] = x1;

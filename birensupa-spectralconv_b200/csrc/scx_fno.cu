@@ -22,6 +22,11 @@
 
 #include <algorithm>
 #include <cmath>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include <cuda.h>
 
 #include "scx.h"
 #include "scx_internal.h"
@@ -488,6 +493,170 @@ __global__ void __launch_bounds__(kThreads, 3) fno_skip_norm_kernel(const float*
 // Largest cluster the fused skip+norm kernel is launched with (portable cluster size).
 constexpr int kMaxNormCluster = 8;
 
+// Fourier-layer epilogue with instance norm, tiled by pixels with every output channel in one
+// CTA (hidden == kTileC, HW a multiple of kTilePx, at most kMaxTileCluster tiles per plane):
+//   z[o][p] = s[o][p] + (bias[o] + sum_i Wskip[o][i] h[i][p])        (i in order, fmaf)
+//   h_next[o][p] = GELU((z - mean_o) / sqrt(var_o + eps))              (fno_ns/model.py:96-99,133-134)
+// One CTA takes kTilePx pixels of one batch item b, two adjacent pixels per thread, so each h
+// element is read once and each weight read from shared memory feeds two pixels.  One thread
+// issues all loads: the weights and bias (bulk copies), the tile's h rows as four boxes of
+// kTileGroupRows channels and its s rows as four more (2-D tensor copies), each h group on an
+// mbarrier of its own so that the skip GEMM starts on the first group while the rest land.
+// Statistics: z replaces s in shared memory; four threads per channel sum 64 pixels each (a
+// rotated order keeps the float4 reads free of bank conflicts), then two shuffles, first the
+// CTA's channel sum, then its sum of squared deviations about the CTA's own mean.  Each CTA
+// writes the pair into every CTA of the cluster (distributed shared memory), and after one
+// cluster barrier every CTA combines the partials in rank order (the pairwise variance formula of
+// Chan, Golub and LeVeque), so all CTAs of a plane group hold the same mean and biased variance.
+// grid = (HW / kTilePx, B), cluster = (HW / kTilePx, 1, 1), kTileThreads threads, dynamic smem
+// kTileSmem; th, ts: 2-D fp32 maps (HW, B * kTileC) of h and s with box (kTilePx, kTileGroupRows)
+constexpr int kTileC = 32;
+constexpr int kTilePx = 256;
+constexpr int kTileThreads = kTilePx / 2;
+constexpr int kTileGroups = 4;  // h channel groups, one mbarrier each
+constexpr int kTileGroupRows = kTileC / kTileGroups;
+constexpr int kMaxTileCluster = 16;  // non-portable cluster size, opted into at set-up
+constexpr size_t kTileSmem = 2ull * kTileC * kTilePx * sizeof(float) + 128;  // + alignment slack
+
+__global__ void __launch_bounds__(kTileThreads, 3) fno_skip_norm_tile_kernel(const __grid_constant__ CUtensorMap th,
+                                                                          const __grid_constant__ CUtensorMap ts,
+                                                                          float* __restrict__ h_next,
+                                                                          const float* __restrict__ w,
+                                                                          const float* __restrict__ bias, int HW,
+                                                                          int* watchdog) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    scx::tc::grid_dep_launch();
+    extern __shared__ uint8_t tile_raw[];
+    // tensor-copy destinations start on 128-byte boundaries
+    float* hs = reinterpret_cast<float*>(tile_raw + ((128u - (scx::tc::smem_u32(tile_raw) & 127u)) & 127u));  // [kTileC][kTilePx]
+    float* ss = hs + kTileC * kTilePx;  // [kTileC][kTilePx]: s, then z
+    __shared__ __align__(16) float2 xpart[kMaxTileCluster][kTileC];  // W [o][i] first, then the partials
+    __shared__ __align__(16) float bs[kTileC];
+    __shared__ float stat[2][kTileC];  // the plane's mean and 1 / sqrt(var + eps)
+    __shared__ __align__(8) uint64_t bar[kTileGroups + 1];  // h groups (the first also W and bias), s
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int b = blockIdx.y, px0 = blockIdx.x * kTilePx;
+    constexpr uint32_t kBox = kTilePx * kTileGroupRows * 4u;
+    float* wraw = reinterpret_cast<float*>(&xpart[0][0]);
+    if (tid == 0) {
+        for (int g = 0; g <= kTileGroups; ++g) scx::tc::mbar_init(&bar[g], 1);
+        scx::tc::fence_async_smem();
+        scx::tc::mbar_arrive_expect_tx(&bar[0], kBox + kTileC * kTileC * 4u + kTileC * 4u);
+        for (int g = 1; g < kTileGroups; ++g) scx::tc::mbar_arrive_expect_tx(&bar[g], kBox);
+        scx::tc::mbar_arrive_expect_tx(&bar[kTileGroups], kTileGroups * kBox);
+        // the weights are not written by the kernels chained before this one
+        scx::tc::bulk_g2s(wraw, w, kTileC * kTileC * 4u, &bar[0]);
+        scx::tc::bulk_g2s(bs, bias, kTileC * 4u, &bar[0]);
+        scx::tc::grid_dep_wait();  // s and h come from earlier kernels in the stream
+        for (int g = 0; g < kTileGroups; ++g)
+            scx::tc::tma_load_2d(hs + g * kTileGroupRows * kTilePx, &th, px0, b * kTileC + g * kTileGroupRows, &bar[g]);
+        for (int g = 0; g < kTileGroups; ++g)
+            scx::tc::tma_load_2d(ss + g * kTileGroupRows * kTilePx, &ts, px0, b * kTileC + g * kTileGroupRows,
+                                 &bar[kTileGroups]);
+    }
+    __syncthreads();  // the barriers are initialised
+    // z = s + (bias + W h) in two halves of 16 output channels, written over s.  Four input
+    // channels at a time: one float4 W[o][i..i+3] of each row feeds eight FMAs (two pixels).
+    bool ok = true;
+    constexpr int kHalf = kTileC / 2;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        float2 acc[kHalf];
+#pragma unroll
+        for (int g = 0; g < kTileGroups; ++g) {
+            if (half == 0) ok = scx::tc::mbar_wait_bounded(&bar[g], 0) && ok;
+            if (g == 0) {
+#pragma unroll
+                for (int o = 0; o < kHalf; ++o) acc[o] = make_float2(bs[kHalf * half + o], bs[kHalf * half + o]);
+            }
+#pragma unroll
+            for (int i4 = 0; i4 < kTileGroupRows / 4; ++i4) {
+                const int i = g * kTileGroupRows + 4 * i4;
+                float2 hv[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) hv[k] = reinterpret_cast<const float2*>(hs + (i + k) * kTilePx)[tid];
+#pragma unroll
+                for (int o = 0; o < kHalf; ++o) {
+                    const float4 wv = *reinterpret_cast<const float4*>(wraw + (kHalf * half + o) * kTileC + i);
+                    const float wk[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        acc[o].x = fmaf(wk[k], hv[k].x, acc[o].x);
+                        acc[o].y = fmaf(wk[k], hv[k].y, acc[o].y);
+                    }
+                }
+            }
+        }
+        if (half == 0) {
+            ok = scx::tc::mbar_wait_bounded(&bar[kTileGroups], 0) && ok;
+            if (!ok && lane == 0) atomicExch(watchdog, 30);
+        }
+#pragma unroll
+        for (int o = 0; o < kHalf; ++o) {
+            float2* zp = reinterpret_cast<float2*>(ss + (kHalf * half + o) * kTilePx) + tid;
+            const float2 sv = *zp;
+            *zp = make_float2(sv.x + acc[o].x, sv.y + acc[o].y);
+        }
+    }
+    // once this barrier phase completes, every CTA of the cluster has started and has read its
+    // weights for the last time, so its xpart may be written; it is waited for before the
+    // first remote store
+    asm volatile("barrier.cluster.arrive.aligned;" ::: "memory");
+    __syncthreads();  // z complete in shared memory
+
+    // channel co = tid / 4, pixels [64 ck, 64 ck + 64) with ck = tid % 4, as sixteen float4 in
+    // the rotated order (j + 2 ck + co % 2) % 16: the eight threads of a quarter warp read eight
+    // different bank groups
+    const int co = tid >> 2, ck = tid & 3, rot = 2 * ck + (co & 1);
+    const float4* zr = reinterpret_cast<const float4*>(ss + co * kTilePx) + ck * 16;
+    float csum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const float4 q = zr[(j + rot) & 15];
+        csum += (q.x + q.y) + (q.z + q.w);
+    }
+    csum += __shfl_xor_sync(0xffffffffu, csum, 1);
+    csum += __shfl_xor_sync(0xffffffffu, csum, 2);
+    const float cmean = csum * (1.0f / kTilePx);
+    float cm2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        const float4 q = zr[(j + rot) & 15];
+        const float dx = q.x - cmean, dy = q.y - cmean, dz = q.z - cmean, dw = q.w - cmean;
+        cm2 += fmaf(dx, dx, dy * dy) + fmaf(dz, dz, dw * dw);
+    }
+    cm2 += __shfl_xor_sync(0xffffffffu, cm2, 1);
+    cm2 += __shfl_xor_sync(0xffffffffu, cm2, 2);
+    // push (sum, m2) of channel co into slot `rank` of every CTA of the cluster: the four
+    // threads of the channel take the ranks ck, ck + 4, ...
+    const unsigned ranks = cluster.num_blocks(), rank = cluster.block_rank();
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // all CTAs have started
+    const float2 mine = make_float2(csum, cm2);
+    for (unsigned r = ck; r < ranks; r += 4) cluster.map_shared_rank(&xpart[0][0], r)[rank * kTileC + co] = mine;
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (tid < kTileC) {
+        float tot = 0.f;
+        for (unsigned r = 0; r < ranks; ++r) tot += xpart[r][tid].x;
+        const float mean = tot / static_cast<float>(HW);
+        float m2 = 0.f;
+        for (unsigned r = 0; r < ranks; ++r) {
+            const float2 p = xpart[r][tid];
+            const float d = p.x * (1.0f / kTilePx) - mean;
+            m2 += fmaf(static_cast<float>(kTilePx) * d, d, p.y);
+        }
+        stat[0][tid] = mean;
+        stat[1][tid] = 1.0f / sqrtf(m2 / static_cast<float>(HW) + 1e-5f);
+    }
+    __syncthreads();
+    float2* out = reinterpret_cast<float2*>(h_next + static_cast<size_t>(b) * kTileC * HW + px0) + tid;
+#pragma unroll
+    for (int o = 0; o < kTileC; ++o) {
+        const float2 zv = reinterpret_cast<const float2*>(ss + o * kTilePx)[tid];
+        const float mean = stat[0][o], rstd = stat[1][o];
+        out[static_cast<size_t>(o) * (HW / 2)] = scx::tc::gelu_pair((zv.x - mean) * rstd, (zv.y - mean) * rstd);
+    }
+}
 
 // y[b][oc][p] = b2[oc] + sum_j W2[oc][j] GELU(b1[j] + sum_c W1[j][c] h[b][c][p])
 // Each thread takes PX pixels (kThreads apart, so loads and stores stay coalesced): one
@@ -615,10 +784,99 @@ cudaError_t run_pixel_kernels_lift(const scx_fno2d_config* cfg, const scx_fno2d_
                                cfg->height, cfg->width, cfg->in_frames, cfg->hidden, cfg->input_layout);
 }
 
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// A [rows][HW] fp32 activation as a 2-D tensor map with box (kTilePx, kTileGroupRows), through the
+// runtime's driver entry point (no libcuda link).
+bool encode_act_map(CUtensorMap* m, const float* ptr, int HW, int rows) {
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(HW), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(HW) * 4};
+    const cuuint32_t box[2] = {kTilePx, kTileGroupRows};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Whether the pixel-tiled skip+norm kernel can run with clusters of `ctas` CTAs on the current
+// device.  Set-up (non-portable cluster size, dynamic shared memory, an occupancy check) runs
+// once per device and cluster size.
+bool tile_norm_ready(int ctas) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    static std::mutex m;
+    static std::map<std::pair<int, int>, bool> seen;
+    std::lock_guard<std::mutex> lock(m);
+    const auto key = std::make_pair(dev, ctas);
+    auto it = seen.find(key);
+    if (it != seen.end()) return it->second;
+    bool ok = cudaFuncSetAttribute(fno_skip_norm_tile_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                  cudaSuccess &&
+              cudaFuncSetAttribute(fno_skip_norm_tile_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(kTileSmem)) == cudaSuccess;
+    if (ok) {
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(ctas, 1, 1);
+        lc.blockDim = dim3(kTileThreads);
+        lc.dynamicSmemBytes = kTileSmem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = ctas;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        int clusters = 0;
+        ok = cudaOccupancyMaxActiveClusters(&clusters, fno_skip_norm_tile_kernel, &lc) == cudaSuccess && clusters > 0;
+    }
+    cudaGetLastError();  // a refused attribute or query leaves no sticky error behind
+    seen[key] = ok;
+    return ok;
+}
+
 template <int HMAX>
 cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const float* h, float* h_next, const float* w, const float* bias, cudaStream_t s) {
     const int HW = cfg->height * cfg->width;
     cudaError_t e;
+    const int tiles = HW / kTilePx;
+    if (cfg->instance_norm && cfg->hidden == kTileC && HW % kTilePx == 0 && tiles >= 1 && tiles <= kMaxTileCluster &&
+        ((reinterpret_cast<uintptr_t>(spec) | reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(h_next) |
+          reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(bias)) & 15) == 0 &&
+        tile_norm_ready(tiles)) {
+        int* wd = nullptr;
+        e = scx::device_watchdog(&wd);
+        if (e != cudaSuccess) return e;
+        CUtensorMap th, ts;
+        const int rows = cfg->batch_size * cfg->hidden;
+        if (!encode_act_map(&th, h, HW, rows) || !encode_act_map(&ts, spec, HW, rows)) return cudaErrorInvalidValue;
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(tiles, cfg->batch_size, 1);
+        lc.blockDim = dim3(kTileThreads);
+        lc.dynamicSmemBytes = kTileSmem;
+        lc.stream = s;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = tiles;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 2;
+        return cudaLaunchKernelEx(&lc, fno_skip_norm_tile_kernel, th, ts, h_next, w, bias, HW, wd);
+    }
     const bool quads = HW % 4 == 0 && cfg->hidden % 16 == 0 &&
                        ((reinterpret_cast<uintptr_t>(spec) | reinterpret_cast<uintptr_t>(h) |
                          reinterpret_cast<uintptr_t>(h_next)) & 15) == 0;

@@ -52,6 +52,9 @@ def test_fno_matches_reference_golden(cuda_device):
     dict(B=2, T=4, H=88, W=88, width=32, m1=10, m2=12, layers=4, norm=True),    # 8-CTA cluster, partial CTA
     dict(B=2, T=4, H=96, W=96, width=16, m1=8, m2=8, layers=4, norm=True),      # plane too large for a cluster
     dict(B=2, T=5, H=32, W=32, width=32, m1=8, m2=8, layers=4, norm=False),     # four-pixel skip with GELU
+    dict(B=3, T=4, H=32, W=32, width=32, m1=8, m2=8, layers=4, norm=True),      # pixel tiles, 4-CTA cluster
+    dict(B=2, T=4, H=16, W=16, width=32, m1=4, m2=5, layers=4, norm=True),      # pixel tiles, one CTA per plane
+    dict(B=1, T=10, H=64, W=64, width=32, m1=12, m2=12, layers=4, norm=True),   # pixel tiles, 16-CTA cluster
 ])
 def test_fno_shapes_vs_oracle(cfg, cuda_device):
     import fno_model

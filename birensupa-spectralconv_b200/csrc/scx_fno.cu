@@ -495,31 +495,36 @@ constexpr int kMaxNormCluster = 8;
 
 // Fourier-layer epilogue with instance norm, tiled by pixels with every output channel in one
 // CTA (hidden == kTileC, HW a multiple of kTilePx, at most kMaxTileCluster tiles per plane):
-//   z[o][p] = s[o][p] + (bias[o] + sum_i Wskip[o][i] h[i][p])        (i in order, fmaf)
+//   z[o][p] = s[o][p] + (bias[o] + sum_i Wskip[o][i] h[i][p])
 //   h_next[o][p] = GELU((z - mean_o) / sqrt(var_o + eps))              (fno_ns/model.py:96-99,133-134)
-// One CTA takes kTilePx pixels of one batch item b, two adjacent pixels per thread, so each h
-// element is read once and each weight read from shared memory feeds two pixels.  One thread
-// issues all loads: the weights and bias (bulk copies), the tile's h rows as four boxes of
-// kTileGroupRows channels and its s rows as four more (2-D tensor copies), each h group on an
-// mbarrier of its own so that the skip GEMM starts on the first group while the rest land.
-// Statistics: z replaces s in shared memory; four threads per channel sum 64 pixels each (a
-// rotated order keeps the float4 reads free of bank conflicts), then two shuffles, first the
-// CTA's channel sum, then its sum of squared deviations about the CTA's own mean.  Each CTA
-// writes the pair into every CTA of the cluster (distributed shared memory), and after one
-// cluster barrier every CTA combines the partials in rank order (the pairwise variance formula of
-// Chan, Golub and LeVeque), so all CTAs of a plane group hold the same mean and biased variance.
+// One CTA takes kTilePx pixels of one batch item b, one pixel per thread.  The skip GEMM runs on
+// the tensor core: D[pixel][o] = sum_i h[i][pixel] W[o][i] for two M = 128 pixel tiles (N = 32,
+// K = 32) in 3xTF32 (hi*hi + hi*lo + lo*hi, hi = the top 19 bits, lo = the exact remainder; fp32
+// TMEM accumulators), the same scheme as the FNO projection.  One thread brings the weights, the
+// bias (bulk copies) and the tile's h rows (four 2-D tensor copies) into shared memory; each
+// thread splits its pixel's 32 channels into the K-major operands, and two threads issue the
+// MMAs of one pixel tile each.  Each thread then reads its pixel's 32 accumulators from TMEM
+// and adds bias and s (read from global memory while the MMAs run).
+// Statistics: z goes to shared memory; eight threads per channel sum 32 pixels each (a rotated
+// order keeps the float4 reads free of bank conflicts), then three shuffles, first the CTA's
+// channel sum, then its sum of squared deviations about the CTA's own mean.  Each CTA writes the
+// pair into every CTA of the cluster (distributed shared memory), and after one cluster barrier
+// every CTA combines the partials in rank order (the pairwise variance formula of Chan, Golub and
+// LeVeque), so all CTAs of a plane group hold the same mean and biased variance.
 // grid = (HW / kTilePx, B), cluster = (HW / kTilePx, 1, 1), kTileThreads threads, dynamic smem
-// kTileSmem; th, ts: 2-D fp32 maps (HW, B * kTileC) of h and s with box (kTilePx, kTileGroupRows)
+// kTileSmem; th: 2-D fp32 map (HW, B * kTileC) of h with box (kTilePx, kTileGroupRows)
 constexpr int kTileC = 32;
 constexpr int kTilePx = 256;
-constexpr int kTileThreads = kTilePx / 2;
-constexpr int kTileGroups = 4;  // h channel groups, one mbarrier each
+constexpr int kTileThreads = kTilePx;
+constexpr int kTileGroups = 4;  // tensor copies of the h tile
 constexpr int kTileGroupRows = kTileC / kTileGroups;
 constexpr int kMaxTileCluster = 16;  // non-portable cluster size, opted into at set-up
-constexpr size_t kTileSmem = 2ull * kTileC * kTilePx * sizeof(float) + 128;  // + alignment slack
+constexpr uint32_t kTileA = kTilePx * kTileC * 4u;          // one operand part of both pixel tiles
+constexpr size_t kTileSmem = 2ull * kTileA + 1024;          // A hi | A lo, + alignment slack
+constexpr uint32_t kTileCols = 2 * kTileC;                  // TMEM: D of pixel tiles 0 and 1
 
 __global__ void __launch_bounds__(kTileThreads, 3) fno_skip_norm_tile_kernel(const __grid_constant__ CUtensorMap th,
-                                                                          const __grid_constant__ CUtensorMap ts,
+                                                                          const float* __restrict__ s,
                                                                           float* __restrict__ h_next,
                                                                           const float* __restrict__ w,
                                                                           const float* __restrict__ bias, int HW,
@@ -528,120 +533,161 @@ __global__ void __launch_bounds__(kTileThreads, 3) fno_skip_norm_tile_kernel(con
     cg::cluster_group cluster = cg::this_cluster();
     scx::tc::grid_dep_launch();
     extern __shared__ uint8_t tile_raw[];
-    // tensor-copy destinations start on 128-byte boundaries
-    float* hs = reinterpret_cast<float*>(tile_raw + ((128u - (scx::tc::smem_u32(tile_raw) & 127u)) & 127u));  // [kTileC][kTilePx]
-    float* ss = hs + kTileC * kTilePx;  // [kTileC][kTilePx]: s, then z
-    __shared__ __align__(16) float2 xpart[kMaxTileCluster][kTileC];  // W [o][i] first, then the partials
+    // A hi | A lo, K-major SW128 (pixel rows of 32 channels; tile t at t * kTileA / 2).  Before
+    // the split, the raw weights land in the A hi area and the raw h tile [i][pixel] in the A lo
+    // area; after the MMAs, z [o][pixel] reuses A hi and the cluster partials A lo.
+    uint8_t* a_hi = scx::tc::align1024(tile_raw);
+    uint8_t* a_lo = a_hi + kTileA;
+    float* wraw = reinterpret_cast<float*>(a_hi);
+    float* hraw = reinterpret_cast<float*>(a_lo);
+    float* zs = reinterpret_cast<float*>(a_hi);
+    float2* xpart = reinterpret_cast<float2*>(a_lo);  // [kMaxTileCluster][kTileC]
+    __shared__ __align__(1024) uint8_t wsw[2][kTileC * kTileC * 4];  // W hi | W lo, K-major SW128
     __shared__ __align__(16) float bs[kTileC];
     __shared__ float stat[2][kTileC];  // the plane's mean and 1 / sqrt(var + eps)
-    __shared__ __align__(8) uint64_t bar[kTileGroups + 1];  // h groups (the first also W and bias), s
-    const int tid = threadIdx.x, lane = tid & 31;
+    __shared__ __align__(8) uint64_t bar[2];  // 0: W, bias and h landed; 1: the MMAs are done
+    __shared__ uint32_t tmem_base;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int b = blockIdx.y, px0 = blockIdx.x * kTilePx;
-    constexpr uint32_t kBox = kTilePx * kTileGroupRows * 4u;
-    float* wraw = reinterpret_cast<float*>(&xpart[0][0]);
-    if (tid == 0) {
-        for (int g = 0; g <= kTileGroups; ++g) scx::tc::mbar_init(&bar[g], 1);
+    if (warp == 0) {
+        scx::tc::tmem_alloc(&tmem_base, kTileCols);
+        scx::tc::tmem_relinquish();
+    }
+    if (tid == 32) {
+        scx::tc::mbar_init(&bar[0], 1);
+        scx::tc::mbar_init(&bar[1], 2);
         scx::tc::fence_async_smem();
-        scx::tc::mbar_arrive_expect_tx(&bar[0], kBox + kTileC * kTileC * 4u + kTileC * 4u);
-        for (int g = 1; g < kTileGroups; ++g) scx::tc::mbar_arrive_expect_tx(&bar[g], kBox);
-        scx::tc::mbar_arrive_expect_tx(&bar[kTileGroups], kTileGroups * kBox);
+        scx::tc::mbar_arrive_expect_tx(&bar[0], kTileC * kTileC * 4u + kTileC * 4u + kTileA);
         // the weights are not written by the kernels chained before this one
         scx::tc::bulk_g2s(wraw, w, kTileC * kTileC * 4u, &bar[0]);
         scx::tc::bulk_g2s(bs, bias, kTileC * 4u, &bar[0]);
-        scx::tc::grid_dep_wait();  // s and h come from earlier kernels in the stream
+        scx::tc::grid_dep_wait();  // h comes from earlier kernels in the stream
         for (int g = 0; g < kTileGroups; ++g)
-            scx::tc::tma_load_2d(hs + g * kTileGroupRows * kTilePx, &th, px0, b * kTileC + g * kTileGroupRows, &bar[g]);
-        for (int g = 0; g < kTileGroups; ++g)
-            scx::tc::tma_load_2d(ss + g * kTileGroupRows * kTilePx, &ts, px0, b * kTileC + g * kTileGroupRows,
-                                 &bar[kTileGroups]);
+            scx::tc::tma_load_2d(hraw + g * kTileGroupRows * kTilePx, &th, px0, b * kTileC + g * kTileGroupRows,
+                                 &bar[0]);
     }
-    __syncthreads();  // the barriers are initialised
-    // z = s + (bias + W h) in two halves of 16 output channels, written over s.  Four input
-    // channels at a time: one float4 W[o][i..i+3] of each row feeds eight FMAs (two pixels).
-    bool ok = true;
-    constexpr int kHalf = kTileC / 2;
+    scx::tc::fence_before_sync();
+    __syncthreads();  // barriers initialised, TMEM allocated
+    scx::tc::fence_after_sync();
+    const uint32_t tmem = tmem_base;
+    bool ok = scx::tc::mbar_wait_bounded(&bar[0], 0);
+    {
+        // W [o][i] -> hi / lo, K-major SW128 with N = kTileC rows: four channels per thread
+        const int e = tid * 4, o = e / kTileC, i0 = e % kTileC;
+        const float4 v = *reinterpret_cast<const float4*>(wraw + e);
+        float4 hi, lo;
+        scx::tc::split_tf32(v.x, hi.x, lo.x);
+        scx::tc::split_tf32(v.y, hi.y, lo.y);
+        scx::tc::split_tf32(v.z, hi.z, lo.z);
+        scx::tc::split_tf32(v.w, hi.w, lo.w);
+        const uint32_t off = scx::tc::kmajor_offset32(kTileC, o, i0);
+        *reinterpret_cast<float4*>(&wsw[0][off]) = hi;
+        *reinterpret_cast<float4*>(&wsw[1][off]) = lo;
+    }
+    float hv[kTileC];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        float2 acc[kHalf];
+    for (int i = 0; i < kTileC; ++i) hv[i] = hraw[i * kTilePx + tid];
+    __syncthreads();  // the raw tiles have been read: A hi and A lo overwrite them
+    {
+        const int t = tid >> 7, m = tid & 127;
+        uint8_t* ah = a_hi + t * (kTileA / 2);
+        uint8_t* al = a_lo + t * (kTileA / 2);
 #pragma unroll
-        for (int g = 0; g < kTileGroups; ++g) {
-            if (half == 0) ok = scx::tc::mbar_wait_bounded(&bar[g], 0) && ok;
-            if (g == 0) {
-#pragma unroll
-                for (int o = 0; o < kHalf; ++o) acc[o] = make_float2(bs[kHalf * half + o], bs[kHalf * half + o]);
-            }
-#pragma unroll
-            for (int i4 = 0; i4 < kTileGroupRows / 4; ++i4) {
-                const int i = g * kTileGroupRows + 4 * i4;
-                float2 hv[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) hv[k] = reinterpret_cast<const float2*>(hs + (i + k) * kTilePx)[tid];
-#pragma unroll
-                for (int o = 0; o < kHalf; ++o) {
-                    const float4 wv = *reinterpret_cast<const float4*>(wraw + (kHalf * half + o) * kTileC + i);
-                    const float wk[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        acc[o].x = fmaf(wk[k], hv[k].x, acc[o].x);
-                        acc[o].y = fmaf(wk[k], hv[k].y, acc[o].y);
-                    }
-                }
-            }
-        }
-        if (half == 0) {
-            ok = scx::tc::mbar_wait_bounded(&bar[kTileGroups], 0) && ok;
-            if (!ok && lane == 0) atomicExch(watchdog, 30);
-        }
-#pragma unroll
-        for (int o = 0; o < kHalf; ++o) {
-            float2* zp = reinterpret_cast<float2*>(ss + (kHalf * half + o) * kTilePx) + tid;
-            const float2 sv = *zp;
-            *zp = make_float2(sv.x + acc[o].x, sv.y + acc[o].y);
+        for (int c4 = 0; c4 < kTileC / 4; ++c4) {
+            float4 hi, lo;
+            scx::tc::split_tf32(hv[4 * c4 + 0], hi.x, lo.x);
+            scx::tc::split_tf32(hv[4 * c4 + 1], hi.y, lo.y);
+            scx::tc::split_tf32(hv[4 * c4 + 2], hi.z, lo.z);
+            scx::tc::split_tf32(hv[4 * c4 + 3], hi.w, lo.w);
+            const uint32_t off = scx::tc::kmajor_offset32(128, m, 4 * c4);
+            *reinterpret_cast<float4*>(ah + off) = hi;
+            *reinterpret_cast<float4*>(al + off) = lo;
         }
     }
-    // once this barrier phase completes, every CTA of the cluster has started and has read its
-    // weights for the last time, so its xpart may be written; it is waited for before the
+    scx::tc::fence_async_smem();  // the operands are visible to the tensor core
+    scx::tc::fence_before_sync();
+    __syncthreads();
+    scx::tc::fence_after_sync();
+    if ((tid & 31) == 0 && warp < 2) {
+        // pixel tile t = warp: (A hi, W hi), (A hi, W lo), (A lo, W hi), 8 channels per MMA
+        const int t = warp;
+        const uint64_t dA[2] = {scx::tc::desc_sw128(scx::tc::smem_u32(a_hi + t * (kTileA / 2))),
+                                scx::tc::desc_sw128(scx::tc::smem_u32(a_lo + t * (kTileA / 2)))};
+        const uint64_t dW[2] = {scx::tc::desc_sw128(scx::tc::smem_u32(&wsw[0][0])),
+                                scx::tc::desc_sw128(scx::tc::smem_u32(&wsw[1][0]))};
+        constexpr uint32_t id = scx::tc::idesc_tf32(128, kTileC);
+        const uint32_t d = tmem + static_cast<uint32_t>(t * kTileC);
+#pragma unroll
+        for (int part = 0; part < 3; ++part) {
+            const int ap = part == 2 ? 1 : 0, bp = part == 1 ? 1 : 0;
+#pragma unroll
+            for (int ks = 0; ks < kTileC / 8; ++ks)
+                scx::tc::mma_tf32(d, dA[ap] + 2u * ks, dW[bp] + 2u * ks, id, (part | ks) ? 1u : 0u);
+        }
+        scx::tc::mma_commit(&bar[1]);
+    }
+    // s of this pixel while the MMAs run (written by the kernels chained before this one)
+    scx::tc::grid_dep_wait();
+    float sv[kTileC];
+    const float* sp = s + static_cast<size_t>(b) * kTileC * HW + px0 + tid;
+#pragma unroll
+    for (int o = 0; o < kTileC; ++o) sv[o] = sp[static_cast<size_t>(o) * HW];
+    ok = scx::tc::mbar_wait_bounded(&bar[1], 0) && ok;
+    if (!ok && lane == 0) atomicExch(watchdog, 30);
+    scx::tc::fence_after_sync();
+    {
+        // D row of pixel tid: tile warp / 4, TMEM lanes 32 (warp % 4) ..
+        float d[kTileC];
+        scx::tc::tmem_ld32(tmem + (static_cast<uint32_t>(32 * (warp & 3)) << 16) + static_cast<uint32_t>((warp >> 2) * kTileC), d);
+#pragma unroll
+        for (int o = 0; o < kTileC; ++o) zs[o * kTilePx + tid] = sv[o] + (bs[o] + d[o]);
+    }
+    // once this barrier phase completes, every CTA of the cluster has started and its MMAs have
+    // finished reading A lo, so its partials area may be written; it is waited for before the
     // first remote store
     asm volatile("barrier.cluster.arrive.aligned;" ::: "memory");
+    scx::tc::fence_before_sync();
     __syncthreads();  // z complete in shared memory
+    scx::tc::fence_after_sync();
 
-    // channel co = tid / 4, pixels [64 ck, 64 ck + 64) with ck = tid % 4, as sixteen float4 in
-    // the rotated order (j + 2 ck + co % 2) % 16: the eight threads of a quarter warp read eight
-    // different bank groups
-    const int co = tid >> 2, ck = tid & 3, rot = 2 * ck + (co & 1);
-    const float4* zr = reinterpret_cast<const float4*>(ss + co * kTilePx) + ck * 16;
+    // channel co = tid / 8, pixels [32 ck, 32 ck + 32) with ck = tid % 8, as eight float4 in the
+    // rotated order (j + ck) % 8
+    const int co = tid >> 3, ck = tid & 7;
+    const float4* zr = reinterpret_cast<const float4*>(zs + co * kTilePx) + ck * 8;
     float csum = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const float4 q = zr[(j + rot) & 15];
+    for (int j = 0; j < 8; ++j) {
+        const float4 q = zr[(j + ck) & 7];
         csum += (q.x + q.y) + (q.z + q.w);
     }
     csum += __shfl_xor_sync(0xffffffffu, csum, 1);
     csum += __shfl_xor_sync(0xffffffffu, csum, 2);
+    csum += __shfl_xor_sync(0xffffffffu, csum, 4);
     const float cmean = csum * (1.0f / kTilePx);
     float cm2 = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        const float4 q = zr[(j + rot) & 15];
+    for (int j = 0; j < 8; ++j) {
+        const float4 q = zr[(j + ck) & 7];
         const float dx = q.x - cmean, dy = q.y - cmean, dz = q.z - cmean, dw = q.w - cmean;
         cm2 += fmaf(dx, dx, dy * dy) + fmaf(dz, dz, dw * dw);
     }
     cm2 += __shfl_xor_sync(0xffffffffu, cm2, 1);
     cm2 += __shfl_xor_sync(0xffffffffu, cm2, 2);
-    // push (sum, m2) of channel co into slot `rank` of every CTA of the cluster: the four
-    // threads of the channel take the ranks ck, ck + 4, ...
+    cm2 += __shfl_xor_sync(0xffffffffu, cm2, 4);
+    // push (sum, m2) of channel co into slot `rank` of every CTA of the cluster: the eight
+    // threads of the channel take the ranks ck and ck + 8
     const unsigned ranks = cluster.num_blocks(), rank = cluster.block_rank();
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // all CTAs have started
     const float2 mine = make_float2(csum, cm2);
-    for (unsigned r = ck; r < ranks; r += 4) cluster.map_shared_rank(&xpart[0][0], r)[rank * kTileC + co] = mine;
+    for (unsigned r = ck; r < ranks; r += 8) cluster.map_shared_rank(xpart, r)[rank * kTileC + co] = mine;
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
     if (tid < kTileC) {
         float tot = 0.f;
-        for (unsigned r = 0; r < ranks; ++r) tot += xpart[r][tid].x;
+        for (unsigned r = 0; r < ranks; ++r) tot += xpart[r * kTileC + tid].x;
         const float mean = tot / static_cast<float>(HW);
         float m2 = 0.f;
         for (unsigned r = 0; r < ranks; ++r) {
-            const float2 p = xpart[r][tid];
+            const float2 p = xpart[r * kTileC + tid];
             const float d = p.x * (1.0f / kTilePx) - mean;
             m2 += fmaf(static_cast<float>(kTilePx) * d, d, p.y);
         }
@@ -649,13 +695,15 @@ __global__ void __launch_bounds__(kTileThreads, 3) fno_skip_norm_tile_kernel(con
         stat[1][tid] = 1.0f / sqrtf(m2 / static_cast<float>(HW) + 1e-5f);
     }
     __syncthreads();
-    float2* out = reinterpret_cast<float2*>(h_next + static_cast<size_t>(b) * kTileC * HW + px0) + tid;
+    float* out = h_next + static_cast<size_t>(b) * kTileC * HW + px0 + tid;
 #pragma unroll
-    for (int o = 0; o < kTileC; ++o) {
-        const float2 zv = reinterpret_cast<const float2*>(ss + o * kTilePx)[tid];
-        const float mean = stat[0][o], rstd = stat[1][o];
-        out[static_cast<size_t>(o) * (HW / 2)] = scx::tc::gelu_pair((zv.x - mean) * rstd, (zv.y - mean) * rstd);
+    for (int o = 0; o < kTileC; o += 2) {
+        const float z0 = zs[o * kTilePx + tid], z1 = zs[(o + 1) * kTilePx + tid];
+        const float2 g = scx::tc::gelu_pair((z0 - stat[0][o]) * stat[1][o], (z1 - stat[0][o + 1]) * stat[1][o + 1]);
+        out[static_cast<size_t>(o) * HW] = g.x;
+        out[static_cast<size_t>(o + 1) * HW] = g.y;
     }
+    if (warp == 0) scx::tc::tmem_dealloc(tmem, kTileCols);
 }
 
 // y[b][oc][p] = b2[oc] + sum_j W2[oc][j] GELU(b1[j] + sum_c W1[j][c] h[b][c][p])
@@ -858,9 +906,8 @@ cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const f
         int* wd = nullptr;
         e = scx::device_watchdog(&wd);
         if (e != cudaSuccess) return e;
-        CUtensorMap th, ts;
-        const int rows = cfg->batch_size * cfg->hidden;
-        if (!encode_act_map(&th, h, HW, rows) || !encode_act_map(&ts, spec, HW, rows)) return cudaErrorInvalidValue;
+        CUtensorMap th;
+        if (!encode_act_map(&th, h, HW, cfg->batch_size * cfg->hidden)) return cudaErrorInvalidValue;
         cudaLaunchConfig_t lc = {};
         lc.gridDim = dim3(tiles, cfg->batch_size, 1);
         lc.blockDim = dim3(kTileThreads);
@@ -875,7 +922,8 @@ cudaError_t run_layer_epilogue(const scx_fno2d_config* cfg, float* spec, const f
         attr[1].val.clusterDim.z = 1;
         lc.attrs = attr;
         lc.numAttrs = 2;
-        return cudaLaunchKernelEx(&lc, fno_skip_norm_tile_kernel, th, ts, h_next, w, bias, HW, wd);
+        return cudaLaunchKernelEx(&lc, fno_skip_norm_tile_kernel, th, static_cast<const float*>(spec), h_next, w, bias,
+                                  HW, wd);
     }
     const bool quads = HW % 4 == 0 && cfg->hidden % 16 == 0 &&
                        ((reinterpret_cast<uintptr_t>(spec) | reinterpret_cast<uintptr_t>(h) |

@@ -107,13 +107,13 @@ def launches_per_forward(c: dict) -> int:
     return 7 if split and not direct(H, W, m1, m2) and not quad else 3
 
 
-def fixture_error(name: str, y: torch.Tensor) -> dict | None:
+def fixture_error(name: str, y: torch.Tensor, prefix: str = "spectral", ref: str = "reference_pytorch.py") -> dict | None:
     """Error of a device result against the reference's output for the same workload, as
     committed in tests/golden (4096 sampled outputs, per-plane norms): the margin left under
     the 1e-4 bound."""
     import numpy as np
 
-    path = REPO / "tests" / "golden" / f"spectral_{name}.npz"
+    path = REPO / "tests" / "golden" / f"{prefix}_{name}.npz"
     if not path.exists():
         return None
     with np.load(path, allow_pickle=False) as z:
@@ -124,7 +124,7 @@ def fixture_error(name: str, y: torch.Tensor) -> dict | None:
     norms = np.sqrt((yh ** 2).sum(axis=(-2, -1)))
     norm_rel = float(np.abs(norms - g["y_plane_norm"]).max() / max(float(g["y_plane_norm"].max()), 1e-30))
     return {"max_abs_rel_sampled": sampled, "plane_norm_rel": norm_rel, "tol": 1e-4,
-            "vs": f"tests/golden/spectral_{name}.npz (the reference's reference_pytorch.py output)"}
+            "vs": f"tests/golden/{prefix}_{name}.npz (the reference's {ref} output)"}
 
 
 class ClockSampler:
@@ -572,7 +572,10 @@ def run_fno(steps: int, warmup: int, device, world: int, rank: int) -> dict:
         peer.sync()
         peer.close()
     del graph
-    return {"ms_per_step": ms, "samples_per_s": world * B / (ms / 1e3), "batch_per_gpu": B,
+    # rank 0's own shard has the seeds of the reference's fixture
+    accuracy = fixture_error("fno_ns_b20_w32_64x64_m12_l4", out[:B], prefix="fno", ref="fno_ns/model.py") \
+        if rank == 0 else None
+    return {"ms_per_step": ms, "samples_per_s": world * B / (ms / 1e3), "batch_per_gpu": B, "accuracy": accuracy,
             # lift, then per layer forward DFT, mixing, inverse DFT and the fused skip +
             # instance norm + GELU (one cluster launch at 64x64), then the projection
             "launches_per_step": 2 + 4 * fw["layers"], "cuda_graph": True,

@@ -14,6 +14,8 @@
 // TMEM, 16 columns at a time, and finishes bias, GELU and the second layer for its half of the
 // hidden units in order; the two halves' sums are added through shared memory.  The wait for the MMAs is bounded (about a
 // second); a CTA that gives up stores a code in the device watchdog word and writes nothing.
+#include <algorithm>
+
 #include "scx_internal.h"
 #include "scx_tc.cuh"
 
@@ -23,6 +25,7 @@ namespace {
 constexpr int kProjThreads = 256;  // 8 warps: two per TMEM sub-partition
 constexpr int kTile = 128;         // pixels per CTA (MMA M)
 constexpr int kMaxOut = 4;
+constexpr int kProjCtasPerSm = 3;  // register budget of the launch bounds; the persistent grid
 
 // W [N][K] (row-major, K = channels) -> tf32 hi/lo (fp32 containers), K-major SW128: 4
 // consecutive k of row n per 16-byte unit.
@@ -45,7 +48,37 @@ __device__ __forceinline__ void stage_weights(const float* __restrict__ w, int N
 // The [C][kTile] pixel tile at hb (channel stride HW) -> tf32 hi/lo, K-major SW128 (row =
 // pixel, K = channel): each unit reads 4 channels of one pixel (consecutive lanes take
 // consecutive pixels, so every load instruction reads 128 contiguous bytes) and writes one
-// 16-byte unit.
+// 16-byte unit.  load_tile / store_tile do the same in two steps for C == kPrefC, so that the
+// next tile's loads are in flight while the current tile is finished.
+constexpr int kPrefC = 32;
+constexpr int kPrefUnits = kTile * (kPrefC / 4) / kProjThreads;  // units per thread
+
+__device__ __forceinline__ void load_tile(const float* __restrict__ hb, int HW, float4 (&v)[kPrefUnits]) {
+#pragma unroll
+    for (int j = 0; j < kPrefUnits; ++j) {
+        const int u = threadIdx.x + j * kProjThreads;
+        const int m = u % kTile, c0 = (u / kTile) * 4;
+        const float* src = hb + static_cast<size_t>(c0) * HW + m;
+        v[j] = make_float4(__ldg(src), __ldg(src + HW), __ldg(src + 2 * static_cast<size_t>(HW)),
+                           __ldg(src + 3 * static_cast<size_t>(HW)));
+    }
+}
+
+__device__ __forceinline__ void store_tile(const float4 (&v)[kPrefUnits], uint8_t* a_hi, uint8_t* a_lo) {
+#pragma unroll
+    for (int j = 0; j < kPrefUnits; ++j) {
+        const int u = threadIdx.x + j * kProjThreads;
+        const int m = u % kTile, c0 = (u / kTile) * 4;
+        float4 hi, lo;
+        tc::split_tf32(v[j].x, hi.x, lo.x);
+        tc::split_tf32(v[j].y, hi.y, lo.y);
+        tc::split_tf32(v[j].z, hi.z, lo.z);
+        tc::split_tf32(v[j].w, hi.w, lo.w);
+        const uint32_t off = tc::kmajor_offset32(kTile, m, c0);
+        *reinterpret_cast<float4*>(a_hi + off) = hi;
+        *reinterpret_cast<float4*>(a_lo + off) = lo;
+    }
+}
 __device__ __forceinline__ void stage_tile(const float* __restrict__ hb, int C, int HW, uint8_t* a_hi,
                                            uint8_t* a_lo) {
     for (int u = threadIdx.x; u < kTile * (C / 4); u += blockDim.x) {
@@ -119,12 +152,16 @@ struct ProjArgs {
     const float* w2;  // [oc][ph]
     const float* b2;  // [oc]
     int HW, C, ph, oc;
+    int ntiles;  // B * HW / kTile
     uint32_t tmem_cols;
     int* watchdog;
 };
 
 // Shared memory: W1 hi | W1 lo | h tile hi | h tile lo (all K-major SW128, fp32) | b1 | w2.
-__global__ void __launch_bounds__(kProjThreads) fno_project_tc_kernel(const ProjArgs a) {
+// Persistent: CTA i takes the pixel tiles i, i + gridDim.x, ...; the weights are staged once,
+// and for hidden == kPrefC the next tile's h loads are in flight during the current tile's MMAs
+// and epilogue.
+__global__ void __launch_bounds__(kProjThreads, kProjCtasPerSm) fno_project_tc_kernel(const ProjArgs a) {
     extern __shared__ uint8_t proj_raw[];
     __shared__ uint64_t done;
     __shared__ uint32_t tmem_base;
@@ -154,52 +191,69 @@ __global__ void __launch_bounds__(kProjThreads) fno_project_tc_kernel(const Proj
     for (int i = tid; i < a.oc * ph; i += kProjThreads) w2s[i] = __ldg(a.w2 + i);
     tc::grid_dep_wait();  // h comes from the last layer's kernels
     const int tiles_per_plane = a.HW / kTile;
-    const int b = blockIdx.x / tiles_per_plane;
-    const int p0 = (blockIdx.x % tiles_per_plane) * kTile;
-    stage_tile(a.h + static_cast<size_t>(b) * C * a.HW + p0, C, a.HW, a_hi, a_lo);
-    tc::fence_async_smem();
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    const uint32_t tmem = tmem_base;
-    if (tid == 0) issue_gemm(tmem, w_hi, w_lo, a_hi, a_lo, ph, C, &done);
-    const bool ok = tc::mbar_wait_bounded(&done, 0);
-    tc::fence_after_sync();
-    // warps w and w + 4 read the same TMEM lanes (pixels 32 (w % 4) ..): the first takes the
-    // hidden units [0, ph/2), the second [ph/2, ph); the outputs are the first half's sums plus
-    // the second's
+    auto tile_src = [&](int t) {
+        return a.h + static_cast<size_t>(t / tiles_per_plane) * C * a.HW + (t % tiles_per_plane) * kTile;
+    };
+    const bool pref = C == kPrefC;
+    float4 nxt[kPrefUnits];
+    if (pref && static_cast<int>(blockIdx.x) < a.ntiles) load_tile(tile_src(blockIdx.x), a.HW, nxt);
     const int sub = warp & 3, half = warp >> 2, m = sub * 32 + lane;
-    float out[kMaxOut];
+    bool ok = true;
+    int it = 0;
+    for (int t = blockIdx.x; t < a.ntiles; t += gridDim.x, ++it) {
+        if (pref)
+            store_tile(nxt, a_hi, a_lo);
+        else
+            stage_tile(tile_src(t), C, a.HW, a_hi, a_lo);
+        tc::fence_async_smem();
+        tc::fence_before_sync();
+        __syncthreads();
+        tc::fence_after_sync();
+        const uint32_t tmem = tmem_base;
+        if (tid == 0) issue_gemm(tmem, w_hi, w_lo, a_hi, a_lo, ph, C, &done);
+        const int tn = t + static_cast<int>(gridDim.x);
+        if (pref && tn < a.ntiles) load_tile(tile_src(tn), a.HW, nxt);
+        ok = tc::mbar_wait_bounded(&done, it & 1);
+        tc::fence_after_sync();
+        // warps w and w + 4 read the same TMEM lanes (pixels 32 (w % 4) ..): the first takes the
+        // hidden units [0, ph/2), the second [ph/2, ph); the outputs are the first half's sums
+        // plus the second's
+        float out[kMaxOut];
 #pragma unroll
-    for (int o = 0; o < kMaxOut; ++o) out[o] = 0.f;
-    if (ok) {
-        const uint32_t row = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-        const int jh = ph / 2;
-        switch (a.oc) {
-            case 1: finish_units<1>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
-            case 2: finish_units<2>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
-            case 3: finish_units<3>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
-            default: finish_units<4>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
+        for (int o = 0; o < kMaxOut; ++o) out[o] = 0.f;
+        if (ok) {
+            const uint32_t row = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+            const int jh = ph / 2;
+            switch (a.oc) {
+                case 1: finish_units<1>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
+                case 2: finish_units<2>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
+                case 3: finish_units<3>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
+                default: finish_units<4>(row, half * jh, (half + 1) * jh, b1s, w2s, ph, out); break;
+            }
+            if (half == 1) {
+#pragma unroll
+                for (int o = 0; o < kMaxOut; ++o) part[o * kTile + m] = out[o];
+            }
         }
-        if (half == 1) {
+        __syncthreads();
+        if (ok && half == 0) {
+            const int b = t / tiles_per_plane, p = (t % tiles_per_plane) * kTile + m;
 #pragma unroll
-            for (int o = 0; o < kMaxOut; ++o) part[o * kTile + m] = out[o];
+            for (int o = 0; o < kMaxOut; ++o)
+                if (o < a.oc)
+                    a.y[(static_cast<size_t>(b) * a.oc + o) * a.HW + p] = (out[o] + part[o * kTile + m]) + __ldg(a.b2 + o);
         }
-    }
-    __syncthreads();
-    if (ok && half == 0) {
-        const int p = p0 + m;
-#pragma unroll
-        for (int o = 0; o < kMaxOut; ++o)
-            if (o < a.oc)
-                a.y[(static_cast<size_t>(b) * a.oc + o) * a.HW + p] = (out[o] + part[o * kTile + m]) + __ldg(a.b2 + o);
+        // this tile's TMEM rows, A operand and partials are no longer read; every thread agrees
+        // on whether to go on
+        tc::fence_before_sync();
+        ok = __syncthreads_and(ok) != 0;
+        tc::fence_after_sync();
+        if (!ok) break;
     }
     if (!ok && tid == 0) atomicExch(a.watchdog, 50);
-    tc::fence_before_sync();
-    __syncthreads();
     if (warp == 0) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, a.tmem_cols);
+        tc::tmem_dealloc(tmem_base, a.tmem_cols);
     }
 }
 
@@ -233,13 +287,16 @@ cudaError_t launch_fno_project_tc(const float* h, float* y, const float* w1, con
     a.ph = ph;
     a.oc = oc;
     a.tmem_cols = tmem_cols_for(ph);
+    a.ntiles = static_cast<int>(static_cast<long long>(B) * (HW / kTile));
     cudaError_t e = device_watchdog(&a.watchdog);
     if (e != cudaSuccess) return e;
     const size_t smem = proj_smem(hidden, ph, oc);
     int per_sm = 1;
     e = prepare_kernel(reinterpret_cast<const void*>(fno_project_tc_kernel), smem, kProjThreads, &per_sm);
     if (e != cudaSuccess) return e;
-    const unsigned grid = static_cast<unsigned>(static_cast<long long>(B) * (HW / kTile));
+    // persistent: kProjCtasPerSm CTAs per SM (the launch bounds' register budget; the shared
+    // memory of three fits), at most one per tile; CTAs that do not fit at once simply start later
+    const unsigned grid = static_cast<unsigned>(std::min<long long>(a.ntiles, static_cast<long long>(kProjCtasPerSm) * num_sms()));
     return launch_chained(fno_project_tc_kernel, dim3(grid), dim3(kProjThreads), smem, stream, a);
 }
 

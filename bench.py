@@ -396,10 +396,14 @@ def run_spectral(name: str, steps: int, warmup: int, device, world: int, rank: i
 def run_strong(name: str, steps: int, warmup: int, device, world: int, rank: int) -> dict:
     """Strong scaling: the workload's whole batch (B=16 at 256x256, C64, m32) is split into
     contiguous shards over the ranks (16/8/4/2 items per GPU at N = 1/2/4/8); a step is the
-    forward of this rank's shard (one CUDA graph) followed by the gather of every shard into
-    a preallocated [B, Cout, H, W] tensor on rank 0 (one group of NCCL point-to-point
-    transfers).  L2 is flushed (256 MiB write, not timed) before every step; each step has its
-    own CUDA events on the launching stream, and the step time is the max over ranks.
+    forward of this rank's shard and the gather of every shard into a preallocated
+    [B, Cout, H, W] tensor on rank 0, as one CUDA graph: scx_dist.PipelinedGather, which runs
+    the shard in sub-batches of two items and pushes each sub-batch's output to rank 0 by a peer
+    copy while the next one is computed.  For comparison the line also times the forward of the whole
+    shard followed by one push (``ms_per_step_push_after_forward``) and followed by the NCCL
+    gather (``ms_per_step_nccl_gather``).  L2 is flushed (256 MiB write, not timed) before every
+    step; each step has its own CUDA events on the launching stream, and the step time is the
+    max over ranks.
 
     Rank 0 then runs the whole batch alone with the same protocol: its time is the one-GPU
     time the scaling efficiency is taken against, and its output is compared with the
@@ -475,14 +479,38 @@ def run_strong(name: str, steps: int, warmup: int, device, world: int, rank: int
             step_nccl()
         t_nccl = scx_dist.max_over_ranks(timed(step_nccl, steps), device)
         torch.distributed.barrier()
-    t_step = scx_dist.max_over_ranks(timed(step_gather, steps), device)
+    t_push_after = scx_dist.max_over_ranks(timed(step_gather, steps), device) if world > 1 else None
+    t_step = t_push_after
+    pipe = graph_pipe = None
     if world > 1:
-        peer.sync()  # every push has landed before rank 0 reads the gathered output
+        peer.sync()
+        peer.close()  # the pipelined gather maps rank 0's output once more
+        out_all_check = out_all.clone() if rank == 0 else None
+        if rank == 0:
+            out_all.fill_(float("nan"))  # the pipelined gather must fill every slot again
+        torch.distributed.barrier()
+        pipe = scx_dist.PipelinedGather(x_loc, y_loc, w1, w2, m1, m2, out_all, B)
+        pipe.run(stream)  # outside any capture first
+        torch.cuda.synchronize(device)
+        graph_pipe = capture_graphs(device, [lambda h: pipe.run(torch.cuda.current_stream(device))])[0]
+        for _ in range(warmup):
+            graph_pipe.replay()
+        torch.cuda.synchronize(device)
+        torch.distributed.barrier()
+        t_step = scx_dist.max_over_ranks(timed(graph_pipe.replay, steps), device)
+        pipe.peer.sync()  # every push has landed before rank 0 reads the gathered output
+        if rank == 0:
+            # the sub-batch forwards may split the mixing's channel sum differently
+            scale = max(out_all_check.abs().max().item(), 1e-30)
+            pipelined_rel = (out_all - out_all_check).abs().max().item() / scale
+    else:
+        t_step = scx_dist.max_over_ranks(timed(step_gather, steps), device)
     res = {"workload": name, "batch_total": B, "batch_per_gpu": scx_dist.shard_sizes(B, world),
            "ms_per_step": t_step, "samples_per_s": B / (t_step / 1e3), "ms_forward_only": t_fwd,
            "gather_share": max(0.0, (t_step - t_fwd) / t_step) if world > 1 else 0.0,
-           "gather": "one peer copy per rank into a preallocated tensor on rank 0 (CUDA IPC, copy engines over "
-                     "NVLink)" if world > 1 else None,
+           "gather": "peer copies into a preallocated tensor on rank 0 (CUDA IPC, copy engines over NVLink), "
+                     "one per two-item sub-batch, each overlapping the next sub-batch's forward" if world > 1 else None,
+           "ms_per_step_push_after_forward": t_push_after,
            "ms_per_step_nccl_gather": t_nccl,
            "launches_per_step": launches_per_forward(c), "cuda_graph": True, "scaling": "strong",
            "l2": "256 MiB flush between steps (not timed)"}
@@ -507,10 +535,12 @@ def run_strong(name: str, steps: int, warmup: int, device, world: int, rank: int
                    sharded_equals_single=bool(diff <= 1e-5 * max(scale, 1e-30)),
                    sharded_bitwise_equal=bool(torch.equal(out_all, y_all)),
                    sharded_max_abs_rel_diff=diff / max(scale, 1e-30),
+                   pipelined_vs_push_after_forward_rel=pipelined_rel if world > 1 else 0.0,
                    accuracy=fixture_error(name, out_all))
     if world > 1:
         torch.distributed.barrier()
-        peer.close()
+        del graph_pipe
+        pipe.close()
     del graph
     return res
 

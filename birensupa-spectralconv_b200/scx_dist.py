@@ -135,6 +135,17 @@ class PeerGather:
             _scx.check(self.lib.scx_copy_async(self.dst_ptr, self.local.data_ptr(), self.nbytes, stream),
                        "scx_copy_async")
 
+    def push_items(self, stream: int, lo: int, hi: int) -> None:
+        """Copies items [lo, hi) of this rank's shard into their slots of the output (one copy on
+        ``stream``, ordered after what ``stream`` has already been given)."""
+        if hi <= lo or self.nbytes == 0 or self.dst_ptr == self.local.data_ptr():
+            return
+        import _scx
+
+        item = self.nbytes // self.local.shape[0]
+        _scx.check(self.lib.scx_copy_async(self.dst_ptr + lo * item, self.local.data_ptr() + lo * item,
+                                           (hi - lo) * item, stream), "scx_copy_async")
+
     def sync(self) -> None:
         torch.cuda.synchronize(self.local.device)
         dist.barrier()
@@ -143,6 +154,85 @@ class PeerGather:
         if self.base is not None:
             self.lib.scx_ipc_close(self.base)
             self.base = None
+
+
+def chunk_ranges(n: int, chunks: int) -> list[tuple[int, int]]:
+    """[lo, hi) ranges of ``n`` items in ``min(chunks, n)`` contiguous pieces whose sizes differ
+    by at most one."""
+    k = max(1, min(int(chunks), int(n)))
+    return [(n * i // k, n * (i + 1) // k) for i in range(k)] if n > 0 else []
+
+
+# Items per sub-batch of PipelinedGather: at 256 x 256, C64, a one-item forward is latency-bound
+# (eight of them took longer than the eight-item forward and its push together), two items
+# keep the forward efficient while the pushes overlap.
+DEFAULT_CHUNK_ITEMS = 2
+
+
+class PipelinedGather:
+    """SpectralConv2d forward of this rank's batch shard, then the gather of all shards to rank
+    ``dst``, with the transfer overlapped with the forward.  On a rank other than ``dst`` the
+    shard runs as ``chunks`` sub-batches (of ``DEFAULT_CHUNK_ITEMS`` items by default) on the
+    caller's stream, and
+    each sub-batch's output is pushed into its slots of ``dst``'s output by a copy on a second
+    stream as soon as its forward has finished: the NVLink transfer of sub-batch k runs while
+    sub-batch k + 1 is computed.  Rank ``dst`` runs its shard in one forward straight into its
+    slice of ``out`` (``y`` must be that slice).  ``run(stream)`` enqueues one step and makes
+    ``stream`` wait for the last push, so a step is complete when ``stream`` reaches its end; it
+    can be captured in a CUDA graph once the shape has run outside a capture (the first use
+    builds the twiddle tables).
+
+    x [nb, Cin, H, W] and y [nb, Cout, H, W]: this rank's contiguous shard on its GPU; w1, w2:
+    [Cin, Cout, m1, m2, 2] interleaved float32 on the same GPU; out: the preallocated
+    [batch, Cout, H, W] output on rank ``dst`` (None elsewhere).  Built collectively (it builds a
+    ``PeerGather``); ``close()`` releases the peer mapping."""
+
+    def __init__(self, x: torch.Tensor, y: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, m1: int, m2: int,
+                 out: torch.Tensor | None, batch: int, chunks: int | None = None, dst: int = 0):
+        import _scx
+
+        if not (x.is_cuda and y.is_cuda and x.is_contiguous() and y.is_contiguous() and x.dim() == 4 and y.dim() == 4):
+            raise ValueError("x and y must be contiguous 4-D CUDA tensors")
+        self.lib = _scx.lib
+        self.x, self.y, self.w1, self.w2 = x, y, w1, w2
+        self.nb, self.cin, self.h, self.w = (int(v) for v in x.shape)
+        self.cout = int(y.shape[1])
+        self.m1, self.m2 = int(m1), int(m2)
+        self.peer = PeerGather(y, out, batch, dst)
+        remote = self.peer.dst_ptr != y.data_ptr()
+        default = max(1, -(-self.nb // DEFAULT_CHUNK_ITEMS))
+        self.ranges = chunk_ranges(self.nb, (chunks or default) if remote else 1)
+        self.remote = remote
+        biggest = max((hi - lo for lo, hi in self.ranges), default=0)
+        self.ws_bytes = self.lib.scx_spectral_conv2d_workspace_size(max(1, biggest), self.cin, self.cout, self.h,
+                                                                    self.w, self.m1, self.m2)
+        if self.ws_bytes == 0:
+            raise ValueError("invalid SpectralConv2d sizes")
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=x.device)
+        self.copy_stream = torch.cuda.Stream(x.device)
+        self.x_item = x[0].numel() * x.element_size() if self.nb else 0
+        self.y_item = y[0].numel() * y.element_size() if self.nb else 0
+
+    def run(self, stream: torch.cuda.Stream) -> None:
+        import _scx
+
+        h = stream.cuda_stream
+        for lo, hi in self.ranges:
+            _scx.check(self.lib.scx_spectral_conv2d_fwd(self.x.data_ptr() + lo * self.x_item, self.w1.data_ptr(),
+                                                        self.w2.data_ptr(), self.y.data_ptr() + lo * self.y_item,
+                                                        hi - lo, self.cin, self.cout, self.h, self.w, self.m1,
+                                                        self.m2, self.ws.data_ptr(), self.ws_bytes, h),
+                       "scx_spectral_conv2d_fwd")
+            if self.remote:
+                done = torch.cuda.Event()
+                done.record(stream)
+                self.copy_stream.wait_event(done)
+                self.peer.push_items(self.copy_stream.cuda_stream, lo, hi)
+        if self.remote:
+            stream.wait_stream(self.copy_stream)
+
+    def close(self) -> None:
+        self.peer.close()
 
 
 def gather_batch(local: torch.Tensor, batch: int, dst: int = 0) -> torch.Tensor | None:

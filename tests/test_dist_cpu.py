@@ -107,3 +107,16 @@ def test_rank_that_never_joins_fails_the_gather_in_time():
     assert hung == 0, "a rank kept waiting for its missing peer"
     assert res[1] == "left"
     assert isinstance(res[0], str) and res[0].startswith("error"), res[0]
+
+
+def test_chunk_ranges_cover_the_shard_in_order():
+    import scx_dist
+
+    for n in range(0, 12):
+        for k in range(1, 10):
+            r = scx_dist.chunk_ranges(n, k)
+            assert len(r) == (min(k, n) if n else 0)
+            assert [i for lo, hi in r for i in range(lo, hi)] == list(range(n))
+            if r:
+                sizes = [hi - lo for lo, hi in r]
+                assert max(sizes) - min(sizes) <= 1 and min(sizes) >= 1

@@ -5,7 +5,9 @@
 * Two or more GPUs (skipped otherwise): one process per GPU under torchrun, NCCL; each rank
   runs its shard on its own GPU, the shards are gathered into a preallocated tensor on rank 0
   (scx_dist.gather_batch_into), and rank 0 compares them with the whole batch run alone on its
-  GPU; the peer-copy gather (scx_dist.PeerGather) must give the NCCL gather's bits.
+  GPU; the peer-copy gather (scx_dist.PeerGather) must give the NCCL gather's bits, and the
+  overlapped form (scx_dist.PipelinedGather: sub-batch forwards, each pushed while the next is
+  computed) the single-GPU result to the same tolerance.
 
 Per plane the transforms are computed the same way whatever the batch; the mixing kernel's
 tile shape is chosen per batch size and may split the channel sum into a different number of
@@ -86,10 +88,20 @@ peer = scx_dist.PeerGather(y.contiguous(), out2, B)
 for _ in range(2):
     peer.push(torch.cuda.current_stream(dev).cuda_stream)
 peer.sync()
+peer.close()
+# the overlapped form: sub-batch forwards, each pushed while the next is computed, twice
+out3 = torch.full((B,) + tuple(y.shape[1:]), float("nan"), device=dev) if rank == 0 else None
+y3 = out3[lo:hi] if rank == 0 else torch.empty_like(y)
+pipe = scx_dist.PipelinedGather(x[lo:hi].contiguous().to(dev), y3, torch.view_as_real(w1.to(dev)).contiguous(),
+                                torch.view_as_real(w2.to(dev)).contiguous(), c["m1"], c["m2"], out3, B)
+for _ in range(2):
+    pipe.run(torch.cuda.current_stream(dev))
+pipe.peer.sync()
+pipe.close()
 if rank == 0:
     print(json.dumps({"rel": (out - whole).abs().max().item() / scale, "bitwise": bool(torch.equal(out, whole)),
-                      "peer_equal": bool(torch.equal(out2, out))}))
-peer.close()
+                      "peer_equal": bool(torch.equal(out2, out)),
+                      "pipe_rel": (out3 - whole).abs().max().item() / scale}))
 torch.distributed.barrier()
 torch.distributed.destroy_process_group()
 """
@@ -121,3 +133,4 @@ def test_nccl_sharded_equals_single_gpu(name, tmp_path):
     r = json.loads(lines[-1])
     assert r["rel"] <= TOL, r
     assert r["peer_equal"], r
+    assert r["pipe_rel"] <= TOL, r  # NaN (a slot never written) fails too
